@@ -1,0 +1,359 @@
+"""Benchmark: HGRN-Bit 1.3B lockstep decode tok/s (configuration 3) on N B200s.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  (N > 1: launched by torch.distributed.run, one rank per GPU)
+
+Workload: the seeded random-init 1.3B blob (seed 0), 64
+independent streams with 256-id seeded prompts (seed 1000 + b), FixedQ510 greedy decode.
+The 64 streams are sharded over the N ranks (64/N each, no inter-GPU communication; total
+work fixed, so scaling is "strong"). One step = one lockstep decode step of every stream
+(64 new tokens in total); value = 64 * K / (max over ranks of the device time of K steps).
+The prefill of the prompts happens before the timed region (untimed), so the timed steps
+start from resident state. Weights (325 MB packed) exceed the 126 MB L2, so consecutive
+steps stream them from HBM without an explicit flush.
+
+Also reported: e2e (the same metric through the public serving API, one
+mmfree_cuda_serve_step call per step: pinned host ids in, next ids out), b=1 decode tok/s
+(configuration 2 shape, rank 0), the per-kernel roofline of the dominant kernel class and
+the reference CPU engine timed on this host on a bounded sample (rank 0, N=1).
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+N_STREAMS = 64
+PROMPT_LEN = 256
+GEN_TOKENS = 512          # configuration 3: 512 generated tokens per stream
+B1_PROMPT, B1_GEN = 128, 256
+METRIC = "HGRN-Bit 1.3B decode tok/s (b=64 lockstep, 64 streams / N GPUs)"
+DTYPE = "q5.10-int16 x ternary(2-bit) -> int32"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+def prompts_all():
+    from matmulfreellmcpu_b200.blob import seeded_ids
+    return [seeded_ids(PROMPT_LEN, 1000 + b) for b in range(N_STREAMS)]
+
+
+class Clocks:
+    """nvidia-smi sampler for the timed region (clocks and throttle reasons)."""
+    Q = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, dev: int):
+        self.dev, self.p = dev, None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "-i", str(self.dev),
+                                       "--format=csv,noheader,nounits", "-lms", "100"],
+                                      stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.p = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.p:
+            time.sleep(0.2)
+            self.p.terminate()
+            try:
+                self.out, _ = self.p.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.p.kill()
+                self.out, _ = self.p.communicate()
+
+    def summary(self):
+        rows = []
+        for line in (self.out or "").strip().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) == 6:
+                rows.append(parts)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[2 + i] == "Active"})
+        load = [s for s in sm if mx and s >= 0.5 * max(mx)] or sm
+        return {"sm_mhz": statistics.median(load) if load else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def allmax(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def blob_path(rank, world):
+    from matmulfreellmcpu_b200 import blob as B
+    cache = os.environ.get("MMFREE_BLOB_CACHE", "/tmp/mmfree_blobs")
+    if rank == 0:
+        p = B.cached_blob("1.3B", 0, cache)
+    barrier(world)
+    if rank != 0:
+        p = B.cached_blob("1.3B", 0, cache)  # written by rank 0 already
+    return p
+
+
+# ------------------------------------------------------------------ reference (CPU) arm
+def cpu_reference(steps: int, warmup: int, threads: int | None = None):
+    """The reference engine (oracle/_ref, compiled from the reference sources) on this host:
+    Model::generate_serve with 64 streams; the decode window of one call is timed by the
+    reference's own token callbacks. Prompts are 4 ids (state cost per step does not depend
+    on prompt length), so the sample is `steps` lockstep decode steps of 64 streams."""
+    import oracle
+    from matmulfreellmcpu_b200.blob import seeded_ids
+    R = oracle.Reference()
+    if threads:
+        R.set_threads(threads)
+    path = blob_path(0, 1)
+    m = R.model(path, 1)
+    prompts = [seeded_ids(4, 1000 + b) for b in range(N_STREAMS)]
+    if warmup > 0:
+        m.bench_serve(prompts[:8], 2)
+    pre_s, dec_s, dec_tok = m.bench_serve(prompts, steps + 1)
+    m.close()
+    value = dec_tok / dec_s if dec_s > 0 else 0.0
+    return {"value": value, "unit": "tok/s", "cores": R.threads(), "kind": "reference",
+            "sample": f"64 streams x {steps} lockstep decode steps (4-id seeded prompts, "
+                      f"prefill excluded; {dec_tok} tokens in {dec_s:.2f} s)",
+            "ms_per_step": 1e3 * dec_s / max(steps, 1)}
+
+
+def run_reference_arm(a, rank, world):
+    if rank != 0:
+        return
+    steps = max(1, min(a.steps, 4))
+    cb = cpu_reference(steps, min(a.warmup, 1))
+    line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "tok/s",
+            "n_gpus": world, "steps": steps, "warmup": min(a.warmup, 1),
+            "ms_per_step": cb["ms_per_step"], "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": DTYPE, "data": "synthetic (seeded random-init blob)",
+            "config": {"workload": "config3: 1.3B lockstep decode, 64 streams",
+                       "model": "HGRN-Bit 1.3B random-init seed 0", "streams": N_STREAMS,
+                       "mode": "fixed", "engine": "reference CPU (AVX2 + OpenMP)"},
+            "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ our arm
+def run_ours(a, rank, world, local):
+    import torch
+
+    from matmulfreellmcpu_b200 import api
+    from matmulfreellmcpu_b200.dp import shard_bounds
+
+    torch.cuda.set_device(local)
+    path = blob_path(rank, world)
+    model = api.Model(path, a.mode, 10, device=local)
+    stream = torch.cuda.ExternalStream(model.stream_ptr, device=torch.device("cuda", local))
+    b0, b1 = shard_bounds(N_STREAMS, rank, world)
+    shard = prompts_all()[b0:b1]
+    S = len(shard)
+    budget = GEN_TOKENS - 1  # decode steps available after the prefill token
+    K = min(a.steps, budget)
+    W = a.warmup
+
+    # warm-up session (graph capture, clocks up), then a fresh session for the timed steps
+    model.serve_begin(shard)
+    model.serve_run(max(W, 1))
+    model.serve_end()
+    model.serve_begin(shard)
+    barrier(world)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        ev0.record(stream)
+        model.serve_run(K)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = allmax(ev0.elapsed_time(ev1), world)
+    value = N_STREAMS * K / (ms / 1e3)
+
+    # per-kernel-class breakdown of the same decode steps (event pairs, not graph-captured)
+    prof_steps = min(16, max(1, budget - K)) if budget - K > 0 else 8
+    if budget - K <= 0:
+        model.serve_end()
+        model.serve_begin(shard)
+    prof = model.serve_profile(prof_steps)
+    model.serve_end()
+    launches_per_step = sum(v["launches"] for v in prof.values()) / prof_steps
+
+    # e2e through the public per-step API: pinned host ids in, next ids out, every step
+    first = model.serve_begin(shard)
+    K_e2e = min(K, 128)
+    hin = torch.empty(S, dtype=torch.int64).pin_memory()
+    hout = torch.empty(S, dtype=torch.int64).pin_memory()
+    hin.copy_(torch.from_numpy(first))
+    model.serve_step_ptr(hin.data_ptr(), hout.data_ptr())  # first step outside timing
+    hin.copy_(hout)
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(K_e2e):
+        model.serve_step_ptr(hin.data_ptr(), hout.data_ptr())
+        hin.copy_(hout)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms_e2e = allmax(e0.elapsed_time(e1), world)
+    model.serve_end()
+    e2e = N_STREAMS * K_e2e / (ms_e2e / 1e3)
+
+    # b = 1 decode (configuration 2 shape: 128-id prompt, 255 decode steps), rank 0
+    b1 = None
+    if rank == 0:
+        from matmulfreellmcpu_b200.blob import seeded_ids
+        model.serve_begin([seeded_ids(B1_PROMPT, 0)])
+        model.serve_run(3)
+        model.serve_end()
+        model.serve_begin([seeded_ids(B1_PROMPT, 0)])
+        torch.cuda.synchronize()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        model.serve_run(B1_GEN - 1)
+        f1.record(stream)
+        torch.cuda.synchronize()
+        b1_ms = f0.elapsed_time(f1)
+        prof1 = model.serve_profile(8)
+        model.serve_end()
+        b1 = {"decode_tok_s": (B1_GEN - 1) / (b1_ms / 1e3), "steps": B1_GEN - 1,
+              "ms_per_token": b1_ms / (B1_GEN - 1),
+              "kernel_ms_per_token": {k: v["ms"] / 8 for k, v in prof1.items()}}
+        mm = prof1["bitlinear_matmul"]
+        b1["bitlinear_hbm_gbs"] = mm["bytes"] / (mm["ms"] / 1e3) / 1e9 if mm["ms"] else None
+    barrier(world)
+
+    if rank != 0:
+        model.close()
+        return
+    peaks, src = load_peaks()
+    mm = prof["bitlinear_matmul"]
+    t = mm["ms"] / 1e3
+    gbs = mm["bytes"] / t / 1e9
+    tops = mm["ops"] / t / 1e12
+    int8_peak = 2.0 * float(peaks["bf16_tflops"])
+    t_hbm = mm["bytes"] / (float(peaks["hbm_gbs"]) * 1e9)
+    t_tc = mm["ops"] / (int8_peak * 1e12)
+    if t_tc > t_hbm:
+        roof = {"bound": "tensor", "achieved": tops, "peak": int8_peak, "unit": "TOP/s",
+                "frac": tops / int8_peak, "traffic": None,
+                "peak_source": f"int8 dense = 2 x bf16_tflops of {src} peaks (no int8 entry)",
+                "alt_hbm": {"achieved": gbs, "peak": float(peaks["hbm_gbs"]), "unit": "GB/s",
+                            "frac": gbs / float(peaks["hbm_gbs"])}}
+    else:
+        roof = {"bound": "hbm", "achieved": gbs, "peak": float(peaks["hbm_gbs"]), "unit": "GB/s",
+                "frac": gbs / float(peaks["hbm_gbs"]), "traffic": None,
+                "peak_source": f"hbm_gbs of {src} peaks"}
+    roof.update({"kernel": "bitlinear_matmul (all per-layer BitLinear projections)",
+                 "launches_per_step": mm["launches"] / prof_steps,
+                 "avg_launch_us": 1e3 * mm["ms"] / mm["launches"],
+                 "algorithmic_bytes_per_launch": mm["bytes"] / mm["launches"],
+                 "share_of_step": mm["ms"] / sum(v["ms"] for v in prof.values())})
+
+    cpu = None
+    if world == 1 and not a.no_cpu:
+        try:
+            cb = cpu_reference(2, 0)
+            cpu = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        except Exception as ex:  # the baseline is reported, never required
+            cpu = {"value": None, "unit": "tok/s", "cores": None, "kind": "reference",
+                   "sample": f"unavailable: {ex}"}
+
+    line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K,
+            "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": DTYPE,
+            "data": "synthetic (seeded random-init 1.3B blob, seeded prompt ids)",
+            "config": {"workload": "config3: 1.3B lockstep decode, 64 streams, 256-id prompts",
+                       "model": "HGRN-Bit 1.3B random-init seed 0 (L24 H2048 I5632 V32000)",
+                       "streams": N_STREAMS, "streams_per_gpu": S, "prompt_len": PROMPT_LEN,
+                       "mode": a.mode, "parallelism": f"dp{world} (independent streams)",
+                       "l2": "no flush: 325 MB packed weights > 126 MB L2 per step"},
+            "e2e": {"value": e2e, "unit": "tok/s", "steps": K_e2e,
+                    "h2d_bytes_per_step": 8 * S + 16, "d2h_bytes_per_step": 8 * S},
+            "gpu_launches": int(round(launches_per_step * K)),
+            "roofline": roof, "cpu_baseline": cpu, "b1": b1,
+            "kernel_ms_per_step": {k: v["ms"] / prof_steps for k, v in prof.items()},
+            "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+    model.close()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=500)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--mode", choices=["fixed", "float"], default="fixed")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    a = ap.parse_args()
+    if a.impl == "reference":
+        # rank 0 alone times the CPU reference; the other ranks exit without work
+        rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
+        run_reference_arm(a, rank, world)
+        return
+    rank, world, local = dist_setup()
+    try:
+        run_ours(a, rank, world, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

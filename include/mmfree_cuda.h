@@ -1,0 +1,176 @@
+/* mmfree_cuda.h -- C ABI of the B200 (sm_100a) HGRN-Bit engine, libmmfree_cuda.so.
+ *
+ * Drop-in for the hot path of the matmulfreellmCPU C++ engine. Every entry point names the
+ * reference interface it replaces (paths inside the reference project). Conventions:
+ *   - every function returns MMFREE_OK (0) or a negative MMFREE_E_* code; the message of the
+ *     last failure on the calling thread is mmfree_cuda_last_error();
+ *   - kernel entry points take DEVICE pointers and a cudaStream_t passed as void* (NULL =
+ *     the legacy default stream); they are asynchronous like any CUDA launch;
+ *   - model entry points take HOST buffers and return when their results are in them;
+ *   - act_quant is MMFREE_ACT_FLOAT (the reference's ActQuant::Float) or
+ *     MMFREE_ACT_FIXED_Q510 (ActQuant::FixedQ510, static Q(15-f).f int16 activations with an
+ *     int32 accumulator); frac_bits is the reference's --frac (10 = Q5.10).
+ * FixedQ510 results are bit-identical to the reference's x86 AVX2 build; Float results agree
+ * to fp32 reduction-order noise. There is no CPU fallback: without a CUDA device every call
+ * fails with MMFREE_E_CUDA.
+ * Like the reference kernels (bitlinear.cpp:49-53), the kernel entry points share one
+ * library-owned scratch arena per device and are not re-entrant across host threads; the
+ * arena grows with cudaMalloc on first use of a larger shape, so call once outside any
+ * stream capture before capturing. A model handle must be used by one host thread at a time.
+ */
+#ifndef MMFREE_CUDA_H
+#define MMFREE_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MMFREE_CUDA_ABI_VERSION 1
+
+enum {
+  MMFREE_OK = 0,
+  MMFREE_E_INVALID = -1, /* bad argument (null pointer, zero or oversize dimension, ...) */
+  MMFREE_E_CUDA = -2,    /* CUDA runtime error (no device, launch failure, out of memory) */
+  MMFREE_E_IO = -3,      /* blob file missing, unreadable or malformed */
+  MMFREE_E_RANGE = -4,   /* token id outside [0, vocab_size) or code outside int16 */
+  MMFREE_E_STATE = -5,   /* call out of order (e.g. serve_step without serve_begin) */
+  MMFREE_E_INTERNAL = -6
+};
+
+enum { MMFREE_ACT_FLOAT = 0, MMFREE_ACT_FIXED_Q510 = 1 };
+
+/* Largest in_dim accepted by the kernel entry points (one row is staged in shared memory). */
+#define MMFREE_CUDA_MAX_IN_DIM 57344
+
+const char* mmfree_cuda_last_error(void);
+int mmfree_cuda_abi_version(void);
+
+/* ---- packed ternary weights ---------------------------------------------------------
+ * The reference keeps int8 {-1,0,+1} weights [out_dim, in_dim] (kernels.hpp:32-33,
+ * weights.hpp:34). The CUDA engine streams them as 2 bits per weight in a tiled layout
+ * (32-row groups x 64-column chunks, 512 bytes each); these calls produce it. */
+size_t mmfree_cuda_packed_bytes(size_t out_dim, size_t in_dim);
+/* device int8 [out_dim, in_dim] -> device packed (mmfree_cuda_packed_bytes bytes). */
+int mmfree_cuda_repack_ternary(void* dst, const int8_t* wq, size_t out_dim, size_t in_dim,
+                               void* stream);
+/* Same format computed on the host (for offline caches and tests). */
+int mmfree_cuda_pack_ternary_host(void* dst, const int8_t* wq, size_t out_dim, size_t in_dim);
+
+/* ---- kernel entry points (device pointers) ------------------------------------------- */
+
+/* Replaces mmfree::bitlinear (kernels.hpp:41-44, bitlinear.cpp:21-117): per row
+ * RMSNorm(eps) * norm_weight, then Float or FixedQ510 activation handling, ternary
+ * accumulate and dequant. out [rows, out_dim]; x [rows, in_dim]; norm_out (nullable)
+ * [rows, in_dim]; acc_out (nullable, FixedQ510 only) [rows, out_dim] int32 accumulators,
+ * the values a TernaryBackend would produce (ternary_backend.hpp:26-31). */
+int mmfree_cuda_bitlinear(float* out, const float* x, const float* norm_weight,
+                          const void* wpacked, float scale_w, size_t rows, size_t in_dim,
+                          size_t out_dim, float eps, float* norm_out, int act_quant,
+                          int frac_bits, int32_t* acc_out, void* stream);
+
+/* Replaces mmfree::bitlinear_cluster (kernels.hpp:50-53, bitlinear.cpp:119-159): k <= 3
+ * FixedQ510 projections sharing x, each with its own norm weight, packed weight, scale and
+ * output. outs / norm_weights / wpacked are HOST arrays of k device pointers, scale_w a
+ * host array of k floats; acc_out (nullable) is [k, rows, out_dim]. */
+int mmfree_cuda_bitlinear_cluster(float* const* outs, const float* x,
+                                  const float* const* norm_weights,
+                                  const void* const* wpacked, const float* scale_w, int k,
+                                  size_t rows, size_t in_dim, size_t out_dim, float eps,
+                                  int frac_bits, int32_t* acc_out, void* stream);
+
+/* Replaces TernaryBackend::matmul_batch (ternary_backend.hpp:43-48): acc[i*M + m] =
+ * sum_n x[i*N + n] * wq[m, n] for b rows of int32 activations in int16 range. */
+int mmfree_cuda_ternary_matmul(int32_t* acc, const int32_t* x, const void* wpacked, size_t N,
+                               size_t M, size_t b, void* stream);
+
+/* Replaces mmfree::rmsnorm (kernels.hpp:29-30, rmsnorm.cpp:11-22). */
+int mmfree_cuda_rmsnorm(float* y, const float* x, const float* weight, size_t rows,
+                        size_t cols, float eps, void* stream);
+/* Replaces mmfree::swiglu (kernels.hpp:56, activations.cpp:9-15): out = silu(a) * b. */
+int mmfree_cuda_swiglu(float* out, const float* a, const float* b, size_t n, void* stream);
+/* Replaces mmfree::hgrn_scan (kernels.hpp:61-62, hgrn_scan.cpp:11-19); state_io nullable. */
+int mmfree_cuda_hgrn_scan(float* out, const float* i, const float* f, size_t T, size_t D,
+                          float* state_io, void* stream);
+/* Replaces mmfree::rmsnorm_swishgate (kernels.hpp:65-66, rmsnorm_swishgate.cpp:13-30). */
+int mmfree_cuda_rmsnorm_swishgate(float* out, const float* g, const float* o,
+                                  const float* weight, size_t rows, size_t cols, float eps,
+                                  void* stream);
+
+/* ---- model (host buffers) ------------------------------------------------------------ */
+typedef struct mmfree_cuda_model mmfree_cuda_model;
+
+typedef struct {
+  size_t vocab_size, hidden_size, num_hidden_layers, num_heads, expand_ratio,
+      intermediate_size;
+  int use_lower_bound, use_short_conv;
+  float rms_norm_eps;
+} mmfree_cuda_config; /* mirrors mmfree::Config (config.hpp:8-21) */
+
+/* Parses only the header of a model.mmfree blob (mmfree::Weights(path).config(),
+ * weights.cpp:191-235 + weights.hpp:44); needs no GPU. MMFREE_E_IO on a bad file. */
+int mmfree_cuda_blob_config(const char* blob_path, mmfree_cuda_config* out);
+
+/* Replaces mmfree::Weights(path) + mmfree::Model(w, aq, frac_bits) (weights.cpp:191-254,
+ * model.hpp:33-34): parses model.mmfree, uploads it to `device` and repacks the ternary
+ * weights. Errors: MMFREE_E_IO (file/format), MMFREE_E_CUDA, MMFREE_E_INVALID. */
+int mmfree_cuda_model_open(const char* blob_path, int device, int act_quant, int frac_bits,
+                           mmfree_cuda_model** out);
+void mmfree_cuda_model_close(mmfree_cuda_model* m);
+int mmfree_cuda_model_config(const mmfree_cuda_model* m, mmfree_cuda_config* out);
+size_t mmfree_cuda_model_weight_bytes(const mmfree_cuda_model* m); /* packed ternary bytes */
+
+/* Replaces Model::generate (model.hpp:36-50): out_ids receives prompt + generated ids
+ * (*out_len of them; out_cap >= n + new_tokens). temperature <= 0 is greedy. */
+int mmfree_cuda_generate(mmfree_cuda_model* m, const int64_t* ids, size_t n,
+                         size_t new_tokens, int64_t eos_id, float temperature, int top_k,
+                         uint64_t seed, int64_t* out_ids, size_t out_cap, size_t* out_len);
+
+/* Replaces Model::forward (model.hpp:34): logits [T, vocab_size]. */
+int mmfree_cuda_forward(mmfree_cuda_model* m, const int64_t* ids, size_t T, float* logits);
+/* The last row of Model::forward only (what mmfree-cli --logits-out writes, main.cpp:217-224). */
+int mmfree_cuda_forward_last(mmfree_cuda_model* m, const int64_t* ids, size_t T,
+                             float* logits);
+
+/* Replaces Model::generate_serve (model.hpp:52-70): B prompts (host pointers + lengths);
+ * out is [B, out_stride], stream b's full ids in out[b*out_stride ...], length out_lens[b]. */
+int mmfree_cuda_generate_serve(mmfree_cuda_model* m, size_t B, const int64_t* const* prompts,
+                               const size_t* lens, size_t new_tokens, int64_t eos_id,
+                               float temperature, int top_k, uint64_t seed, int64_t* out,
+                               size_t out_stride, size_t* out_lens);
+
+/* Step-wise lockstep serving (the decode loop of hgrn_model.cpp:432-452 exposed one step per
+ * call, greedy). begin prefills the B prompts and writes each stream's first token;
+ * step feeds one token per stream and returns the next; run performs `steps` steps on the
+ * device from the last tokens and writes [B, steps] ids; end releases the session. */
+int mmfree_cuda_serve_begin(mmfree_cuda_model* m, size_t B, const int64_t* const* prompts,
+                            const size_t* lens, int64_t* first_ids);
+int mmfree_cuda_serve_step(mmfree_cuda_model* m, const int64_t* in_ids, int64_t* out_ids);
+int mmfree_cuda_serve_run(mmfree_cuda_model* m, size_t steps, int64_t* out);
+int mmfree_cuda_serve_end(mmfree_cuda_model* m);
+
+/* ---- measurement (no reference counterpart: the reference times host code with its
+ * Profiler, profile.hpp:20-73; device work is timed with CUDA events instead) ---------- */
+/* The cudaStream_t (as void*) every kernel of the model is launched on, for event timing. */
+void* mmfree_cuda_model_stream(mmfree_cuda_model* m);
+
+typedef struct {
+  const char* name;  /* kernel class: prep, bitlinear_matmul, lm_head_matmul, mixer, ... */
+  double ms;         /* summed device time of its launches */
+  int64_t launches;
+  double bytes;      /* algorithmic bytes moved */
+  double ops;        /* algorithmic ops (2*M*K*N per BitLinear matmul) */
+} mmfree_cuda_kernel_stats;
+
+/* Runs `steps` greedy decode steps of the active serving session (like serve_run, but not
+ * graph-captured) with a CUDA event pair around every launch; fills up to max_classes
+ * entries of out and sets *n_classes. */
+int mmfree_cuda_serve_profile(mmfree_cuda_model* m, size_t steps, mmfree_cuda_kernel_stats* out,
+                              int max_classes, int* n_classes);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MMFREE_CUDA_H */

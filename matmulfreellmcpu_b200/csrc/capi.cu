@@ -1,0 +1,484 @@
+// capi.cu -- the extern "C" boundary of libmmfree_cuda.so (declared in include/mmfree_cuda.h).
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../include/mmfree_cuda.h"
+#include "common.cuh"
+#include "kernels.h"
+#include "blob.h"
+#include "model.h"
+
+using namespace mmfree_cuda;
+
+struct mmfree_cuda_model {
+  Model* impl;
+};
+
+namespace {
+
+thread_local std::string g_last_error;
+
+struct CudaError : std::runtime_error {
+  using std::runtime_error::runtime_error;
+};
+
+void ck(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) throw CudaError(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+// Map exceptions to status codes; the message is kept for mmfree_cuda_last_error().
+template <class F>
+int guard(F&& f) {
+  try {
+    f();
+    return MMFREE_OK;
+  } catch (const std::invalid_argument& e) {
+    g_last_error = e.what();
+    return MMFREE_E_INVALID;
+  } catch (const std::out_of_range& e) {
+    g_last_error = e.what();
+    return MMFREE_E_RANGE;
+  } catch (const std::logic_error& e) {
+    g_last_error = e.what();
+    return MMFREE_E_STATE;
+  } catch (const CudaError& e) {
+    g_last_error = e.what();
+    return MMFREE_E_CUDA;
+  } catch (const std::bad_alloc&) {
+    g_last_error = "host out of memory";
+    return MMFREE_E_INTERNAL;
+  } catch (const std::runtime_error& e) {
+    g_last_error = e.what();
+    const bool cuda = std::strncmp(e.what(), "cuda:", 5) == 0;
+    return cuda ? MMFREE_E_CUDA : MMFREE_E_IO;
+  } catch (...) {
+    g_last_error = "unknown error";
+    return MMFREE_E_INTERNAL;
+  }
+}
+
+void need(bool ok, const char* what) {
+  if (!ok) throw std::invalid_argument(what);
+}
+
+cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+// Library-owned scratch of the kernel entry points: one grow-only arena per device, plus a
+// device word of error flags at its start.
+struct Scratch {
+  void* base = nullptr;
+  size_t bytes = 0;
+};
+std::mutex g_scratch_mu;
+Scratch g_scratch[64];
+
+char* scratch(size_t bytes) {
+  int dev = 0;
+  ck(cudaGetDevice(&dev), "cudaGetDevice");
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  Scratch& s = g_scratch[dev & 63];
+  bytes += 256;
+  if (bytes > s.bytes) {
+    if (s.base) ck(cudaFree(s.base), "cudaFree");  // synchronizes with work still using it
+    s.base = nullptr;
+    s.bytes = 0;
+    const size_t grow = bytes < (size_t(1) << 20) ? (size_t(1) << 20) : bytes;
+    ck(cudaMalloc(&s.base, grow), "cudaMalloc(scratch)");
+    ck(cudaMemset(s.base, 0, 256), "cudaMemset(scratch)");
+    s.bytes = grow;
+  }
+  return static_cast<char*>(s.base);
+}
+
+size_t a256(size_t n) { return (n + 255) / 256 * 256; }
+
+void check_flags(uint32_t* flags, cudaStream_t st) {
+  uint32_t f = 0;
+  ck(cudaMemcpyAsync(&f, flags, 4, cudaMemcpyDeviceToHost, st), "cudaMemcpyAsync(flags)");
+  ck(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+  if (f) {
+    ck(cudaMemsetAsync(flags, 0, 4, st), "cudaMemsetAsync(flags)");
+    ck(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+    if (f & kErrRange) throw std::out_of_range("activation code outside int16");
+    if (f & kErrNotTernary) throw std::out_of_range("weight outside {-1,0,+1}");
+    throw std::runtime_error("device error flag set");
+  }
+}
+
+void check_dims(size_t rows, size_t in_dim, size_t out_dim) {
+  need(in_dim > 0 && out_dim > 0, "in_dim and out_dim must be positive");
+  need(in_dim <= MMFREE_CUDA_MAX_IN_DIM, "in_dim above MMFREE_CUDA_MAX_IN_DIM");
+  need(out_dim <= (size_t(1) << 30) && rows <= (size_t(1) << 30), "dimension too large");
+}
+
+// One or more BitLinear projections sharing x (bitlinear / bitlinear_cluster).
+void run_bitlinear(int k, float* const* outs, const float* x, const float* const* nws,
+                   const void* const* ws, const float* scales, size_t rows, size_t in_dim,
+                   size_t out_dim, float eps, float* norm_out, bool fixed, int frac_bits,
+                   int32_t* acc_out, cudaStream_t st) {
+  check_dims(rows, in_dim, out_dim);
+  need(frac_bits >= 0 && frac_bits <= 30, "frac_bits must be in [0, 30]");
+  need(x != nullptr, "null x");
+  for (int j = 0; j < k; ++j) need(outs[j] && nws[j] && ws[j], "null output, norm weight or weights");
+  if (rows == 0) return;
+  const size_t kp = static_cast<size_t>(padded_k(static_cast<int64_t>(in_dim)));
+  const size_t per = fixed ? a256(2 * rows * kp) + a256(rows * 4) : a256(rows * kp * 4);
+  char* base = scratch(static_cast<size_t>(k) * per);
+  PrepArgs p;
+  p.x = x;
+  p.nproj = k;
+  p.norm_out = norm_out;
+  p.M = static_cast<int>(rows);
+  p.K = static_cast<int>(in_dim);
+  p.eps = eps;
+  p.qs = static_cast<float>(1u << frac_bits);
+  p.fixed = fixed;
+  for (int j = 0; j < k; ++j) {
+    char* b = base + 256 + j * per;
+    p.normw[j] = nws[j];
+    if (fixed) {
+      p.planes[j] = reinterpret_cast<int8_t*>(b);
+      p.rowsum[j] = reinterpret_cast<int32_t*>(b + a256(2 * rows * kp));
+    } else {
+      p.yf[j] = reinterpret_cast<float*>(b);
+    }
+  }
+  ck(launch_prep(p, st), "prep kernel");
+  for (int j = 0; j < k; ++j) {
+    MatmulArgs a;
+    a.w = ws[j];
+    a.planes = p.planes[j];
+    a.rowsum = p.rowsum[j];
+    a.yf = p.yf[j];
+    a.M = static_cast<int>(rows);
+    a.N = static_cast<int>(out_dim);
+    a.K = static_cast<int>(in_dim);
+    a.scale = fixed ? 1.0f / (p.qs * scales[j]) : 1.0f / scales[j];
+    a.out = outs[j];
+    a.ldo = static_cast<int>(out_dim);
+    a.acc_out = (acc_out && fixed) ? acc_out + static_cast<size_t>(j) * rows * out_dim : nullptr;
+    a.fixed = fixed;
+    ck(launch_matmul(a, st), "matmul kernel");
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* mmfree_cuda_last_error(void) { return g_last_error.c_str(); }
+int mmfree_cuda_abi_version(void) { return MMFREE_CUDA_ABI_VERSION; }
+
+size_t mmfree_cuda_packed_bytes(size_t out_dim, size_t in_dim) {
+  return static_cast<size_t>(packed_bytes(static_cast<int64_t>(out_dim), static_cast<int64_t>(in_dim)));
+}
+
+int mmfree_cuda_repack_ternary(void* dst, const int8_t* wq, size_t out_dim, size_t in_dim,
+                               void* stream) {
+  return guard([&] {
+    need(dst && wq && out_dim > 0 && in_dim > 0, "repack: null pointer or zero dimension");
+    uint32_t* flags = reinterpret_cast<uint32_t*>(scratch(0));
+    ck(launch_repack(dst, wq, static_cast<int64_t>(out_dim), static_cast<int64_t>(in_dim), flags,
+                     as_stream(stream)),
+       "repack kernel");
+    check_flags(flags, as_stream(stream));
+  });
+}
+
+int mmfree_cuda_pack_ternary_host(void* dst, const int8_t* wq, size_t out_dim, size_t in_dim) {
+  return guard([&] {
+    need(dst && wq && out_dim > 0 && in_dim > 0, "pack: null pointer or zero dimension");
+    const int64_t kc = packed_chunks(static_cast<int64_t>(in_dim));
+    const int64_t ng = packed_groups(static_cast<int64_t>(out_dim));
+    auto* out = static_cast<uint32_t*>(dst);
+    for (int64_t g = 0; g < ng; ++g)
+      for (int64_t c = 0; c < kc; ++c)
+        for (int r = 0; r < kRowsPerGroup; ++r)
+          for (int w = 0; w < 4; ++w) {
+            const int64_t row = g * kRowsPerGroup + r;
+            uint32_t word = 0;
+            for (int i = 0; i < 16; ++i) {
+              const int64_t k = c * kChunkK + w * 16 + i;
+              uint32_t u = 1;
+              if (row < static_cast<int64_t>(out_dim) && k < static_cast<int64_t>(in_dim)) {
+                const int v = wq[row * static_cast<int64_t>(in_dim) + k];
+                if (v < -1 || v > 1) throw std::out_of_range("weight outside {-1,0,+1}");
+                u = static_cast<uint32_t>(v + 1);
+              }
+              word |= u << (8 * (i & 3) + 2 * (i >> 2));
+            }
+            out[((g * kc + c) * kRowsPerGroup + r) * 4 + w] = word;
+          }
+  });
+}
+
+int mmfree_cuda_bitlinear(float* out, const float* x, const float* norm_weight,
+                          const void* wpacked, float scale_w, size_t rows, size_t in_dim,
+                          size_t out_dim, float eps, float* norm_out, int act_quant,
+                          int frac_bits, int32_t* acc_out, void* stream) {
+  return guard([&] {
+    need(act_quant == MMFREE_ACT_FLOAT || act_quant == MMFREE_ACT_FIXED_Q510, "bad act_quant");
+    float* outs[1] = {out};
+    const float* nws[1] = {norm_weight};
+    const void* ws[1] = {wpacked};
+    run_bitlinear(1, outs, x, nws, ws, &scale_w, rows, in_dim, out_dim, eps, norm_out,
+                  act_quant == MMFREE_ACT_FIXED_Q510, frac_bits, acc_out, as_stream(stream));
+  });
+}
+
+int mmfree_cuda_bitlinear_cluster(float* const* outs, const float* x,
+                                  const float* const* norm_weights,
+                                  const void* const* wpacked, const float* scale_w, int k,
+                                  size_t rows, size_t in_dim, size_t out_dim, float eps,
+                                  int frac_bits, int32_t* acc_out, void* stream) {
+  return guard([&] {
+    need(k >= 1 && k <= 3, "cluster size k must be 1..3");
+    need(outs && norm_weights && wpacked && scale_w, "null array");
+    run_bitlinear(k, outs, x, norm_weights, wpacked, scale_w, rows, in_dim, out_dim, eps,
+                  nullptr, true, frac_bits, acc_out, as_stream(stream));
+  });
+}
+
+int mmfree_cuda_ternary_matmul(int32_t* acc, const int32_t* x, const void* wpacked, size_t N,
+                               size_t M, size_t b, void* stream) {
+  return guard([&] {
+    check_dims(b, N, M);
+    need(acc && x && wpacked, "null pointer");
+    if (b == 0) return;
+    const size_t kp = static_cast<size_t>(padded_k(static_cast<int64_t>(N)));
+    char* base = scratch(a256(2 * b * kp) + a256(b * 4));
+    auto* flags = reinterpret_cast<uint32_t*>(base);
+    auto* planes = reinterpret_cast<int8_t*>(base + 256);
+    auto* rowsum = reinterpret_cast<int32_t*>(base + 256 + a256(2 * b * kp));
+    cudaStream_t st = as_stream(stream);
+    ck(launch_codes_to_planes(planes, rowsum, x, static_cast<int>(b), static_cast<int>(N), flags,
+                              st),
+       "codes kernel");
+    MatmulArgs a;
+    a.w = wpacked;
+    a.planes = planes;
+    a.rowsum = rowsum;
+    a.M = static_cast<int>(b);
+    a.N = static_cast<int>(M);
+    a.K = static_cast<int>(N);
+    a.acc_out = acc;
+    a.fixed = true;
+    ck(launch_matmul(a, st), "matmul kernel");
+    check_flags(flags, st);
+  });
+}
+
+int mmfree_cuda_rmsnorm(float* y, const float* x, const float* weight, size_t rows,
+                        size_t cols, float eps, void* stream) {
+  return guard([&] {
+    need(y && x && weight, "null pointer");
+    check_dims(rows, cols, 1);
+    ck(launch_rmsnorm(y, x, weight, static_cast<int>(rows), static_cast<int>(cols), eps,
+                      as_stream(stream)),
+       "rmsnorm kernel");
+  });
+}
+
+int mmfree_cuda_swiglu(float* out, const float* a, const float* b, size_t n, void* stream) {
+  return guard([&] {
+    need(out && a && b, "null pointer");
+    ck(launch_swiglu(out, a, b, static_cast<int64_t>(n), as_stream(stream)), "swiglu kernel");
+  });
+}
+
+int mmfree_cuda_hgrn_scan(float* out, const float* i, const float* f, size_t T, size_t D,
+                          float* state_io, void* stream) {
+  return guard([&] {
+    need(out && i && f, "null pointer");
+    need(T < (size_t(1) << 31) && D < (size_t(1) << 31), "dimension too large");
+    ck(launch_scan(out, i, f, static_cast<int>(T), static_cast<int>(D), state_io,
+                   as_stream(stream)),
+       "scan kernel");
+  });
+}
+
+int mmfree_cuda_rmsnorm_swishgate(float* out, const float* g, const float* o,
+                                  const float* weight, size_t rows, size_t cols, float eps,
+                                  void* stream) {
+  return guard([&] {
+    need(out && g && o && weight, "null pointer");
+    check_dims(rows, cols, 1);
+    ck(launch_swishgate(out, g, o, weight, static_cast<int>(rows), static_cast<int>(cols), eps,
+                        as_stream(stream)),
+       "swishgate kernel");
+  });
+}
+
+// ---- model -------------------------------------------------------------------------------
+int mmfree_cuda_model_open(const char* blob_path, int device, int act_quant, int frac_bits,
+                           mmfree_cuda_model** out) {
+  return guard([&] {
+    need(blob_path && out, "null pointer");
+    need(act_quant == MMFREE_ACT_FLOAT || act_quant == MMFREE_ACT_FIXED_Q510, "bad act_quant");
+    need(frac_bits >= 0 && frac_bits <= 30, "frac_bits must be in [0, 30]");
+    *out = nullptr;
+    int n = 0;
+    ck(cudaGetDeviceCount(&n), "cudaGetDeviceCount");
+    need(device >= 0 && device < n, "no such CUDA device");
+    auto* h = new mmfree_cuda_model{nullptr};
+    try {
+      h->impl = new Model(blob_path, device, act_quant == MMFREE_ACT_FIXED_Q510, frac_bits);
+    } catch (...) {
+      delete h;
+      throw;
+    }
+    *out = h;
+  });
+}
+
+void mmfree_cuda_model_close(mmfree_cuda_model* m) {
+  if (!m) return;
+  delete m->impl;
+  delete m;
+}
+
+static void fill_config(const BlobConfig& c, mmfree_cuda_config* out) {
+    out->vocab_size = c.vocab_size;
+    out->hidden_size = c.hidden_size;
+    out->num_hidden_layers = c.num_hidden_layers;
+    out->num_heads = c.num_heads;
+    out->expand_ratio = c.expand_ratio;
+    out->intermediate_size = c.intermediate_size;
+    out->use_lower_bound = c.use_lower_bound;
+    out->use_short_conv = c.use_short_conv;
+    out->rms_norm_eps = c.rms_norm_eps;
+}
+
+int mmfree_cuda_model_config(const mmfree_cuda_model* m, mmfree_cuda_config* out) {
+  return guard([&] {
+    need(m && out, "null pointer");
+    fill_config(m->impl->config(), out);
+  });
+}
+
+int mmfree_cuda_blob_config(const char* blob_path, mmfree_cuda_config* out) {
+  return guard([&] {
+    need(blob_path && out, "null pointer");
+    Blob b(blob_path);
+    fill_config(b.config(), out);
+  });
+}
+
+size_t mmfree_cuda_model_weight_bytes(const mmfree_cuda_model* m) {
+  return m ? m->impl->weight_bytes() : 0;
+}
+
+int mmfree_cuda_generate(mmfree_cuda_model* m, const int64_t* ids, size_t n,
+                         size_t new_tokens, int64_t eos_id, float temperature, int top_k,
+                         uint64_t seed, int64_t* out_ids, size_t out_cap, size_t* out_len) {
+  return guard([&] {
+    need(m && ids && out_ids && out_len, "null pointer");
+    need(out_cap >= n + new_tokens, "out_cap < n + new_tokens");
+    Sampling s{temperature, top_k, seed};
+    auto st = m->impl->generate(ids, n, new_tokens, eos_id, s);
+    std::memcpy(out_ids, st.data(), st.size() * 8);
+    *out_len = st.size();
+  });
+}
+
+int mmfree_cuda_forward(mmfree_cuda_model* m, const int64_t* ids, size_t T, float* logits) {
+  return guard([&] {
+    need(m && ids && logits, "null pointer");
+    m->impl->forward(ids, T, logits, false);
+  });
+}
+
+int mmfree_cuda_forward_last(mmfree_cuda_model* m, const int64_t* ids, size_t T,
+                             float* logits) {
+  return guard([&] {
+    need(m && ids && logits, "null pointer");
+    m->impl->forward(ids, T, logits, true);
+  });
+}
+
+static std::vector<std::vector<int64_t>> gather_prompts(size_t B, const int64_t* const* prompts,
+                                                        const size_t* lens) {
+  need(B > 0 && prompts && lens, "null prompts");
+  std::vector<std::vector<int64_t>> ps(B);
+  for (size_t b = 0; b < B; ++b) {
+    need(prompts[b] != nullptr || lens[b] == 0, "null prompt pointer");
+    ps[b].assign(prompts[b], prompts[b] + lens[b]);
+  }
+  return ps;
+}
+
+int mmfree_cuda_generate_serve(mmfree_cuda_model* m, size_t B, const int64_t* const* prompts,
+                               const size_t* lens, size_t new_tokens, int64_t eos_id,
+                               float temperature, int top_k, uint64_t seed, int64_t* out,
+                               size_t out_stride, size_t* out_lens) {
+  return guard([&] {
+    need(m && out && out_lens, "null pointer");
+    auto ps = gather_prompts(B, prompts, lens);
+    for (size_t b = 0; b < B; ++b)
+      need(out_stride >= lens[b] + (new_tokens > 0 ? new_tokens : 1), "out_stride too small");
+    Sampling s{temperature, top_k, seed};
+    auto st = m->impl->generate_serve(ps, new_tokens, eos_id, s);
+    for (size_t b = 0; b < B; ++b) {
+      std::memcpy(out + b * out_stride, st[b].data(), st[b].size() * 8);
+      out_lens[b] = st[b].size();
+    }
+  });
+}
+
+int mmfree_cuda_serve_begin(mmfree_cuda_model* m, size_t B, const int64_t* const* prompts,
+                            const size_t* lens, int64_t* first_ids) {
+  return guard([&] {
+    need(m && first_ids, "null pointer");
+    m->impl->serve_begin(gather_prompts(B, prompts, lens), first_ids);
+  });
+}
+
+int mmfree_cuda_serve_step(mmfree_cuda_model* m, const int64_t* in_ids, int64_t* out_ids) {
+  return guard([&] {
+    need(m && in_ids && out_ids, "null pointer");
+    m->impl->serve_step(in_ids, out_ids);
+  });
+}
+
+int mmfree_cuda_serve_run(mmfree_cuda_model* m, size_t steps, int64_t* out) {
+  return guard([&] {
+    need(m && out, "null pointer");
+    m->impl->serve_run(steps, out);
+  });
+}
+
+void* mmfree_cuda_model_stream(mmfree_cuda_model* m) {
+  return m ? static_cast<void*>(m->impl->stream()) : nullptr;
+}
+
+int mmfree_cuda_serve_profile(mmfree_cuda_model* m, size_t steps, mmfree_cuda_kernel_stats* out,
+                              int max_classes, int* n_classes) {
+  return guard([&] {
+    need(m && out && n_classes, "null pointer");
+    auto st = m->impl->serve_profile(steps);
+    int n = 0;
+    for (int c = 0; c < static_cast<int>(st.size()) && n < max_classes; ++c, ++n) {
+      out[n].name = Model::class_name(c);
+      out[n].ms = st[c].ms;
+      out[n].launches = st[c].launches;
+      out[n].bytes = st[c].bytes;
+      out[n].ops = st[c].ops;
+    }
+    *n_classes = n;
+  });
+}
+
+int mmfree_cuda_serve_end(mmfree_cuda_model* m) {
+  return guard([&] {
+    need(m != nullptr, "null pointer");
+    m->impl->serve_end();
+  });
+}
+
+}  // extern "C"

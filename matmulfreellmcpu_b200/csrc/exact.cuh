@@ -1,0 +1,143 @@
+// exact.cuh -- device arithmetic that reproduces the reference CPU engine bit for bit.
+//
+// The reference (matmulfreellmCPU) defines its numerics by its x86 build: AVX2 primitives in
+// cpp/include/mmfree/simd.hpp compiled by g++ -O2 -mavx2 -mfma with GCC's default FP
+// contraction. Every operation below is an explicitly rounded intrinsic (__fmul_rn,
+// __fadd_rn, __fdiv_rn, __fsqrt_rn, __fmaf_rn), so nvcc cannot contract or reorder it, and
+// each mul+add pair that the reference build fuses is written as one __fmaf_rn:
+//   * hgrn_step:          state = fma(f, state, in)              (simd.hpp:340, :354)
+//   * lower bound:        f = fma(1 - lb, f, lb)                 (hgrn_model.cpp:121)
+//   * expf_poly tail:     the GCC-fused form of simd.hpp:215-224
+// The sumsq tail (simd.hpp:87) stays unfused, as in the reference build.
+#pragma once
+
+#include <cstdint>
+
+namespace mmfree_cuda {
+
+// Cephes single-precision exp (S. L. Moshier, Cephes Math Library expf.c): log2(e), ln(2)
+// split hi/lo and the degree-6 minimax polynomial, in the form the reference writes it
+// (simd.hpp:208-249).
+constexpr float kExpHi = 88.3762626647949f;
+constexpr float kLog2e = 1.44269504088896341f;
+constexpr float kLn2Hi = 0.693359375f;
+constexpr float kLn2Lo = -2.12194440e-4f;
+constexpr float kP0 = 1.9875691500E-4f;
+constexpr float kP1 = 1.3981999507E-3f;
+constexpr float kP2 = 8.3334519073E-3f;
+constexpr float kP3 = 4.1665795894E-2f;
+constexpr float kP4 = 1.6666665459E-1f;
+constexpr float kP5 = 5.0000001201E-1f;
+
+__device__ __forceinline__ float pow2_of(float fx) {
+  // fx is integral in [-127, 128]; build the exponent field directly (simd.hpp:246-248).
+  uint32_t e = static_cast<uint32_t>(__float2int_rz(fx) + 127) << 23;
+  return __uint_as_float(e);
+}
+
+// One lane of the vector exp (simd.hpp:232-249).
+__device__ __forceinline__ float exp_vec(float x) {
+  x = (x > -kExpHi) ? x : -kExpHi;  // vmaxps: a NaN input selects the bound
+  x = (x < kExpHi) ? x : kExpHi;    // vminps
+  float fx = floorf(__fmaf_rn(x, kLog2e, 0.5f));
+  float r = __fmaf_rn(-fx, kLn2Hi, x);
+  r = __fmaf_rn(-fx, kLn2Lo, r);
+  float p = kP0;
+  p = __fmaf_rn(p, r, kP1);
+  p = __fmaf_rn(p, r, kP2);
+  p = __fmaf_rn(p, r, kP3);
+  p = __fmaf_rn(p, r, kP4);
+  p = __fmaf_rn(p, r, kP5);
+  p = __fmaf_rn(p, __fmul_rn(r, r), __fadd_rn(r, 1.0f));
+  return __fmul_rn(p, pow2_of(fx));
+}
+
+// The scalar-tail exp of the compiled reference (simd.hpp:212-229).
+__device__ __forceinline__ float exp_tail(float x) {
+  if (x > kExpHi) x = kExpHi;
+  else if (x < -kExpHi) x = -kExpHi;
+  float fx = floorf(__fmaf_rn(x, kLog2e, 0.5f));
+  float r = __fmaf_rn(-fx, kLn2Hi, x);
+  r = __fmaf_rn(-fx, kLn2Lo, r);
+  float p = kP0;
+  p = __fmaf_rn(p, r, kP1);
+  p = __fmaf_rn(p, r, kP2);
+  p = __fmaf_rn(p, r, kP3);
+  p = __fmaf_rn(p, r, kP4);
+  p = __fmaf_rn(p, r, kP5);
+  p = __fadd_rn(__fmaf_rn(p, __fmul_rn(r, r), r), 1.0f);
+  return __fmul_rn(p, pow2_of(fx));
+}
+
+// Element e of an n-element vector op is in the 8-wide SIMD body iff e < 8*floor(n/8);
+// the rest is the scalar tail, which uses exp_tail.
+__device__ __forceinline__ bool in_body(uint64_t e, uint64_t n) { return e < (n & ~uint64_t(7)); }
+
+__device__ __forceinline__ float exp_neg(float x, bool body) {
+  return body ? exp_vec(-x) : exp_tail(-x);
+}
+
+// simd::sigmoid / silu / swiglu (simd.hpp:270-330), one element.
+__device__ __forceinline__ float sigmoid_x(float x, bool body) {
+  return __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_neg(x, body)));
+}
+__device__ __forceinline__ float silu_x(float x, bool body) {
+  return __fdiv_rn(x, __fadd_rn(1.0f, exp_neg(x, body)));
+}
+__device__ __forceinline__ float swiglu_x(float a, float b, bool body) {
+  return __fmul_rn(__fdiv_rn(a, __fadd_rn(1.0f, exp_neg(a, body))), b);
+}
+
+// rstd = 1 / sqrt(sumsq / n + eps)  (rmsnorm.cpp:18, bitlinear.cpp:86).
+__device__ __forceinline__ float rstd_of(float sumsq, float n, float eps) {
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sumsq, n), eps)));
+}
+
+// y = x * rstd * w, left to right (rmsnorm.cpp:19).
+__device__ __forceinline__ float norm_x(float x, float rstd, float w) {
+  return __fmul_rn(__fmul_rn(x, rstd), w);
+}
+
+// simd::quant_q510 (simd.hpp:162-187), one element. In the SIMD body the float->int
+// conversion is cvtps2dq (round half to even, NaN / out-of-range -> INT32_MIN) followed by
+// an integer clamp; in the scalar tail the clamp is in float and the cast truncates.
+__device__ __forceinline__ int32_t quant_x(float y, float qs, bool body) {
+  float q = __fmul_rn(y, qs);
+  if (body) {
+    int32_t v;
+    if (isnan(q) || q >= 2147483648.0f || q < -2147483648.0f) v = INT32_MIN;
+    else v = __float2int_rn(q);
+    return v < -32768 ? -32768 : (v > 32767 ? 32767 : v);
+  }
+  float r = rintf(q);
+  if (r > 32767.0f) r = 32767.0f;
+  else if (r < -32768.0f) r = -32768.0f;
+  return isnan(r) ? INT32_MIN : static_cast<int32_t>(r);
+}
+
+// Lower-bounded forget gate of layers > 0 (hgrn_model.cpp:116-124), as fused by the build.
+__device__ __forceinline__ float lower_bound_x(float f, float lb) {
+  return __fmaf_rn(__fadd_rn(1.0f, -lb), f, lb);
+}
+
+// One recurrence step (simd.hpp:335-357), as fused by the build.
+__device__ __forceinline__ float hgrn_step_x(float f, float state, float in) {
+  return __fmaf_rn(f, state, in);
+}
+
+// The AVX2 horizontal sum of 8 lane partials (simd.hpp:48-57), for lanes held by 8
+// consecutive threads of a warp (lane j of the group holds partial j). Every thread of the
+// 8-lane group receives the sum.
+__device__ __forceinline__ float hsum8_lanes(float v, unsigned mask = 0xffffffffu) {
+  const int j = threadIdx.x & 7;
+  float hi = __shfl_down_sync(mask, v, 4, 8);    // lanes 0..3 get v[j+4]
+  float b = __fadd_rn(v, hi);                    // b_j = v_j + v_{j+4}
+  float b1 = __shfl_down_sync(mask, b, 1, 8);    // lane 0 gets b1, lane 2 gets b3
+  float c = __fadd_rn(b, b1);                    // c0 = b0+b1, c2 = b2+b3
+  float c2 = __shfl_down_sync(mask, c, 2, 8);    // lane 0 gets c2
+  float s = __fadd_rn(c, c2);
+  (void)j;
+  return __shfl_sync(mask, s, 0, 8);
+}
+
+}  // namespace mmfree_cuda

@@ -1,0 +1,568 @@
+// kernels.cu -- the unfused mmfree CUDA kernels (any row count M).
+//
+// prep      one CTA per row: the exact AVX2-order RMSNorm chain(s), the row transform
+//           (plain / rmsnorm / gated rmsnorm), the BitLinear norm and the Q5.10 quantisation
+//           into high/low byte planes (fixed) or fp32 activations (float).
+//           Restates bitlinear.cpp:79-95 (+ rmsnorm.cpp:11-22, rmsnorm_swishgate.cpp:13-30).
+// matmul    ternary x activations over the tiled 2-bit weight format with dp4a (fixed) or
+//           fp32 FMA (float), dequant and optional residual add in the epilogue.
+//           Restates ternary_backend.hpp:96-103 + simd.hpp:191-206 (+ hgrn_model.cpp:161-166,
+//           :189-194 for the residual).
+// gate/scan the HGRN token mixer (hgrn_model.cpp:109-150).
+// others    swiglu split (hgrn_model.cpp:171-185), embedding gather, greedy argmax.
+#include "common.cuh"
+#include "exact.cuh"
+#include "kernels.h"
+
+#include <cfloat>
+#include <mutex>
+
+namespace mmfree_cuda {
+
+namespace {
+constexpr int kPrepThreads = 256;
+constexpr int kMatmulThreads = 128;
+constexpr int kMaxDynSmem = 227 * 1024;
+}  // namespace
+
+// ------------------------------------------------------------------------------ repack
+__global__ void repack_kernel(uint32_t* __restrict__ dst, const int8_t* __restrict__ wq, int64_t n,
+                              int64_t k, int64_t kc, int64_t nwords, uint32_t* bad) {
+  int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (idx >= nwords) return;
+  const int w = static_cast<int>(idx & 3);
+  int64_t t = idx >> 2;
+  const int r = static_cast<int>(t & 31);
+  t >>= 5;
+  const int64_t c = t % kc, g = t / kc;
+  const int64_t row = g * kRowsPerGroup + r, k0 = c * kChunkK + w * 16;
+  uint32_t word = 0;
+  bool nonternary = false;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int64_t kk = k0 + i;
+    uint32_t u = 1;
+    if (row < n && kk < k) {
+      const int v = wq[row * k + kk];
+      nonternary |= (v < -1 || v > 1);
+      u = v > 0 ? 2u : (v < 0 ? 0u : 1u);
+    }
+    word |= u << (8 * (i & 3) + 2 * (i >> 2));
+  }
+  dst[idx] = word;
+  if (nonternary && bad) atomicOr(bad, kErrNotTernary);
+}
+
+cudaError_t launch_repack(void* dst, const int8_t* wq, int64_t n, int64_t k, uint32_t* err,
+                          cudaStream_t s) {
+  const int64_t kc = packed_chunks(k);
+  const int64_t nwords = packed_groups(n) * kc * kRowsPerGroup * 4;
+  const int threads = 256;
+  repack_kernel<<<static_cast<unsigned>(ceil_div(nwords, threads)), threads, 0, s>>>(
+      static_cast<uint32_t*>(dst), wq, n, k, kc, nwords, err);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------ prep
+// sum of squares of s[0..K) in the reference order (simd.hpp:69-89): lanes 0..7 of warp 0
+// each run one serial FMA chain, then the AVX2 horizontal tree, then the unfused tail.
+__device__ __forceinline__ float chain_sumsq(const float* s, int K) {
+  const int j = threadIdx.x & 7;
+  const int n8 = K >> 3;
+  float acc = 0.0f;
+#pragma unroll 8
+  for (int i = 0; i < n8; ++i) {
+    const float v = s[8 * i + j];
+    acc = __fmaf_rn(v, v, acc);
+  }
+  float sum = hsum8_lanes(acc, 0xffu);
+  for (int c = n8 * 8; c < K; ++c) sum = __fadd_rn(sum, __fmul_rn(s[c], s[c]));
+  return sum;
+}
+
+__device__ __forceinline__ int block_sum_int(int v, int* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  int t = 0;
+  if (threadIdx.x == 0)
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t += red[w];
+  __syncthreads();
+  return t;
+}
+
+__global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepArgs a, int mode) {
+  extern __shared__ float srow[];  // the row being normalized, K floats
+  __shared__ float s_rstd;
+  __shared__ int s_red[kPrepThreads / 32];
+  const int m = blockIdx.x, K = a.K, tid = threadIdx.x;
+  const int64_t Kp = padded_k(K);
+  const float* x = a.x + static_cast<int64_t>(m) * K;
+  for (int c = tid; c < K; c += blockDim.x) srow[c] = x[c];
+  __syncthreads();
+
+  if (mode != kPrepPlain) {
+    if (tid < 8) {
+      const float r = rstd_of(chain_sumsq(srow, K), static_cast<float>(K), a.eps);
+      if (tid == 0) s_rstd = r;
+    }
+    __syncthreads();
+    const float r1 = s_rstd;
+    const float* o = a.o + static_cast<int64_t>(m) * K;
+    for (int c = tid; c < K; c += blockDim.x) {
+      float t = norm_x(srow[c], r1, a.prew[c]);
+      if (mode == kPrepSwishgate) t = __fmul_rn(t, silu_x(o[c], in_body(c, K)));
+      srow[c] = t;
+      if (a.pre_out) a.pre_out[static_cast<int64_t>(m) * K + c] = t;
+    }
+    __syncthreads();
+  }
+  if (a.nproj == 0) return;
+
+  if (tid < 8) {
+    const float r = rstd_of(chain_sumsq(srow, K), static_cast<float>(K), a.eps);
+    if (tid == 0) s_rstd = r;
+  }
+  __syncthreads();
+  const float r2 = s_rstd;
+
+  for (int j = 0; j < a.nproj; ++j) {
+    const float* nw = a.normw[j];
+    int local = 0;
+    for (int c = tid; c < Kp; c += blockDim.x) {
+      float y = 0.0f;
+      if (c < K) {
+        y = norm_x(srow[c], r2, nw[c]);
+        if (j == 0 && a.norm_out) a.norm_out[static_cast<int64_t>(m) * K + c] = y;
+      }
+      if (a.fixed) {
+        const int32_t q = c < K ? quant_x(y, a.qs, in_body(c, K)) : 0;
+        local += q;
+        a.planes[j][static_cast<int64_t>(m) * Kp + c] = static_cast<int8_t>(q >> 8);
+        a.planes[j][(static_cast<int64_t>(a.M) + m) * Kp + c] = static_cast<int8_t>(q & 0xff);
+      } else {
+        a.yf[j][static_cast<int64_t>(m) * Kp + c] = y;
+      }
+    }
+    if (a.fixed) {
+      const int total = block_sum_int(local, s_red);
+      if (tid == 0) a.rowsum[j][m] = total;
+    }
+  }
+}
+
+static void raise_smem_limit(const void* fn) {
+  static std::once_flag flags[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::call_once(flags[dev & 63], [&] {
+    cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+  });
+}
+
+cudaError_t launch_prep(const PrepArgs& a, cudaStream_t s) {
+  if (a.M <= 0) return cudaSuccess;
+  const size_t smem = static_cast<size_t>(a.K) * sizeof(float);
+  if (smem > kMaxDynSmem) return cudaErrorInvalidValue;
+  if (smem > 48 * 1024) raise_smem_limit(reinterpret_cast<const void*>(prep_kernel));
+  int mode = kPrepPlain;
+  if (a.prew) mode = a.o ? kPrepSwishgate : kPrepNorm;
+  prep_kernel<<<a.M, kPrepThreads, smem, s>>>(a, mode);
+  return cudaGetLastError();
+}
+
+__global__ void __launch_bounds__(kPrepThreads) codes_kernel(int8_t* __restrict__ planes,
+                                                            int32_t* __restrict__ rowsum,
+                                                            const int32_t* __restrict__ x, int M,
+                                                            int K, uint32_t* err) {
+  __shared__ int s_red[kPrepThreads / 32];
+  const int m = blockIdx.x;
+  const int64_t Kp = padded_k(K);
+  int local = 0;
+  bool bad = false;
+  for (int c = threadIdx.x; c < Kp; c += blockDim.x) {
+    int32_t q = c < K ? x[static_cast<int64_t>(m) * K + c] : 0;
+    if (q < -32768 || q > 32767) {
+      bad = true;
+      q = 0;
+    }
+    local += q;
+    planes[static_cast<int64_t>(m) * Kp + c] = static_cast<int8_t>(q >> 8);
+    planes[(static_cast<int64_t>(M) + m) * Kp + c] = static_cast<int8_t>(q & 0xff);
+  }
+  if (bad && err) atomicOr(err, kErrRange);
+  const int total = block_sum_int(local, s_red);
+  if (threadIdx.x == 0) rowsum[m] = total;
+}
+
+cudaError_t launch_codes_to_planes(int8_t* planes, int32_t* rowsum, const int32_t* x, int M,
+                                   int K, uint32_t* err, cudaStream_t s) {
+  if (M <= 0) return cudaSuccess;
+  codes_kernel<<<M, kPrepThreads, 0, s>>>(planes, rowsum, x, M, K, err);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------ matmul
+// CTA = one 32-row group of the packed weights x MT activation rows; its 4 warps split the
+// k-chunks round robin and reduce through shared memory. Lane r owns output row 32g + r.
+template <int MT>
+__global__ void __launch_bounds__(kMatmulThreads) matmul_fixed_kernel(MatmulArgs a) {
+  const int g = blockIdx.x, m0 = blockIdx.y * MT;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t kc = packed_chunks(a.K), kp = kc * kChunkK;
+  const uint4* wp = static_cast<const uint4*>(a.w) + static_cast<int64_t>(g) * kc * 32 + lane;
+  int acc_hi[MT][4], acc_lo[MT][4];
+#pragma unroll
+  for (int mi = 0; mi < MT; ++mi)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) acc_hi[mi][q] = acc_lo[mi][q] = 0;
+
+  for (int64_t c = warp; c < kc; c += kMatmulThreads / 32) {
+    const uint4 wv = __ldg(wp + c * 32);
+    const uint32_t wd[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+    for (int mi = 0; mi < MT; ++mi) {
+      const int m = min(m0 + mi, a.M - 1);  // rows past M repeat row M-1; never stored
+      const uint4* hp = reinterpret_cast<const uint4*>(a.planes + static_cast<int64_t>(m) * kp + c * kChunkK);
+      const uint4* lp = reinterpret_cast<const uint4*>(a.planes + (static_cast<int64_t>(a.M) + m) * kp + c * kChunkK);
+#pragma unroll
+      for (int w4 = 0; w4 < 4; ++w4) {
+        const uint4 h = __ldg(hp + w4), l = __ldg(lp + w4);
+        const uint32_t hw[4] = {h.x, h.y, h.z, h.w}, lw[4] = {l.x, l.y, l.z, l.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint32_t mw = wd[w4] & (0x03030303u << (2 * q));
+          acc_hi[mi][q] = dp4a_us(mw, hw[q], acc_hi[mi][q]);
+          acc_lo[mi][q] = dp4a_uu(mw, lw[q], acc_lo[mi][q]);
+        }
+      }
+    }
+  }
+
+  __shared__ uint32_t red[kMatmulThreads / 32][MT][32];
+#pragma unroll
+  for (int mi = 0; mi < MT; ++mi) {
+    uint32_t t = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      t += static_cast<uint32_t>(acc_hi[mi][q] >> (2 * q)) << 8;
+      t += static_cast<uint32_t>(acc_lo[mi][q] >> (2 * q));
+    }
+    red[warp][mi][lane] = t;
+  }
+  __syncthreads();
+  const int n = g * kRowsPerGroup + lane;
+  for (int mi = warp; mi < MT; mi += kMatmulThreads / 32) {
+    const int m = m0 + mi;
+    if (m >= a.M || n >= a.N) continue;
+    uint32_t t = 0;
+#pragma unroll
+    for (int w = 0; w < kMatmulThreads / 32; ++w) t += red[w][mi][lane];
+    const int32_t acc = static_cast<int32_t>(t - static_cast<uint32_t>(a.rowsum[m]));
+    if (a.acc_out) a.acc_out[static_cast<int64_t>(m) * a.N + n] = acc;
+    if (!a.out) continue;
+    float v = __fmul_rn(__int2float_rn(acc), a.scale);
+    if (a.resid) v = __fadd_rn(a.resid[static_cast<int64_t>(m) * a.ldr + n], v);
+    a.out[static_cast<int64_t>(m) * a.ldo + n] = v;
+  }
+}
+
+template <int MT>
+__global__ void __launch_bounds__(kMatmulThreads) matmul_float_kernel(MatmulArgs a) {
+  const int g = blockIdx.x, m0 = blockIdx.y * MT;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t kc = packed_chunks(a.K), kp = kc * kChunkK;
+  const uint4* wp = static_cast<const uint4*>(a.w) + static_cast<int64_t>(g) * kc * 32 + lane;
+  float acc[MT];
+#pragma unroll
+  for (int mi = 0; mi < MT; ++mi) acc[mi] = 0.0f;
+  for (int64_t c = warp; c < kc; c += kMatmulThreads / 32) {
+    const uint4 wv = __ldg(wp + c * 32);
+    const uint32_t wd[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+    for (int mi = 0; mi < MT; ++mi) {
+      const int m = min(m0 + mi, a.M - 1);
+      const float4* yp = reinterpret_cast<const float4*>(a.yf + static_cast<int64_t>(m) * kp + c * kChunkK);
+#pragma unroll
+      for (int w4 = 0; w4 < 4; ++w4) {
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const float4 y = __ldg(yp + 4 * w4 + q4);
+          const float yv[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int i = 4 * q4 + e;  // weight i of the 16 in word w4
+            const int code = static_cast<int>((wd[w4] >> (8 * (i & 3) + 2 * (i >> 2))) & 3u);
+            acc[mi] = __fmaf_rn(__int2float_rn(code - 1), yv[e], acc[mi]);
+          }
+        }
+      }
+    }
+  }
+  __shared__ float red[kMatmulThreads / 32][MT][32];
+#pragma unroll
+  for (int mi = 0; mi < MT; ++mi) red[warp][mi][lane] = acc[mi];
+  __syncthreads();
+  const int n = g * kRowsPerGroup + lane;
+  for (int mi = warp; mi < MT; mi += kMatmulThreads / 32) {
+    const int m = m0 + mi;
+    if (m >= a.M || n >= a.N) continue;
+    float t = red[0][mi][lane];
+#pragma unroll
+    for (int w = 1; w < kMatmulThreads / 32; ++w) t = __fadd_rn(t, red[w][mi][lane]);
+    float v = __fmul_rn(t, a.scale);
+    if (a.resid) v = __fadd_rn(a.resid[static_cast<int64_t>(m) * a.ldr + n], v);
+    a.out[static_cast<int64_t>(m) * a.ldo + n] = v;
+  }
+}
+
+template <int MT>
+static cudaError_t launch_matmul_mt(const MatmulArgs& a, cudaStream_t s) {
+  dim3 grid(static_cast<unsigned>(packed_groups(a.N)), static_cast<unsigned>(ceil_div(a.M, MT)));
+  if (a.fixed) matmul_fixed_kernel<MT><<<grid, kMatmulThreads, 0, s>>>(a);
+  else matmul_float_kernel<MT><<<grid, kMatmulThreads, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_matmul(const MatmulArgs& a, cudaStream_t s) {
+  if (a.M <= 0 || a.N <= 0) return cudaSuccess;
+  if (a.M == 1) return launch_matmul_mt<1>(a, s);
+  if (a.M == 2) return launch_matmul_mt<2>(a, s);
+  if (a.M <= 4) return launch_matmul_mt<4>(a, s);
+  return launch_matmul_mt<8>(a, s);
+}
+
+// ------------------------------------------------------------------------------ mixer
+// In place: f <- lower-bounded sigmoid(f); i <- silu(i) * (1 - f). The SIMD body/tail split
+// of element e is taken within its segment of seg elements (one reference block() call).
+__global__ void gate_kernel(float* __restrict__ i, float* __restrict__ f,
+                            const float* __restrict__ lb, int64_t n, int64_t seg, int H) {
+  const int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (e >= n) return;
+  const bool body = in_body(e % seg, seg);
+  float fv = sigmoid_x(f[e], body);
+  if (lb) fv = lower_bound_x(fv, lb[e % H]);
+  const float onemf = __fadd_rn(1.0f, -fv);
+  i[e] = swiglu_x(i[e], onemf, body);
+  f[e] = fv;
+}
+
+// state = fma(f, state, s) along t for each of nseq x H lanes; x layout [nseq][T][H],
+// state [nseq][H] (nullable: zero start, not written back).
+__global__ void scan_kernel(float* __restrict__ out, const float* __restrict__ s,
+                            const float* __restrict__ f, float* __restrict__ state, int nseq,
+                            int T, int H) {
+  const int64_t lane = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (lane >= static_cast<int64_t>(nseq) * H) return;
+  const int64_t q = lane / H, c = lane % H;
+  const int64_t base = q * T * H + c;
+  float st = state ? state[lane] : 0.0f;
+#pragma unroll 4
+  for (int t = 0; t < T; ++t) {
+    const int64_t e = base + static_cast<int64_t>(t) * H;
+    st = hgrn_step_x(f[e], st, s[e]);
+    out[e] = st;
+  }
+  if (state) state[lane] = st;
+}
+
+cudaError_t launch_mixer(float* i, float* f, float* recur, float* state, const float* lb,
+                         int nseq, int len, int H, int seg_rows, cudaStream_t s) {
+  const int64_t n = static_cast<int64_t>(nseq) * len * H;
+  if (n == 0) return cudaSuccess;
+  gate_kernel<<<static_cast<unsigned>(ceil_div(n, 256)), 256, 0, s>>>(
+      i, f, lb, n, static_cast<int64_t>(seg_rows) * H, H);
+  const int64_t lanes = static_cast<int64_t>(nseq) * H;
+  scan_kernel<<<static_cast<unsigned>(ceil_div(lanes, 128)), 128, 0, s>>>(recur, i, f, state, nseq,
+                                                                         len, H);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_scan(float* out, const float* i, const float* f, int T, int D, float* state,
+                        cudaStream_t s) {
+  if (T == 0 || D == 0) return cudaSuccess;
+  scan_kernel<<<static_cast<unsigned>(ceil_div(D, 128)), 128, 0, s>>>(out, i, f, state, 1, T, D);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------ swiglu
+__global__ void swiglu_split_kernel(float* __restrict__ z, const float* __restrict__ y,
+                                    int64_t n, int64_t seg, int I) {
+  const int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (e >= n) return;
+  const int64_t t = e / I, c = e % I;
+  const float* yr = y + t * 2 * I;
+  z[e] = swiglu_x(yr[c], yr[I + c], in_body(e % seg, seg));
+}
+
+cudaError_t launch_swiglu_split(float* z, const float* y, int rows, int I, int seg_rows,
+                                cudaStream_t s) {
+  const int64_t n = static_cast<int64_t>(rows) * I;
+  if (n == 0) return cudaSuccess;
+  swiglu_split_kernel<<<static_cast<unsigned>(ceil_div(n, 256)), 256, 0, s>>>(
+      z, y, n, static_cast<int64_t>(seg_rows) * I, I);
+  return cudaGetLastError();
+}
+
+__global__ void swiglu_kernel(float* __restrict__ out, const float* __restrict__ a,
+                              const float* __restrict__ b, int64_t n) {
+  const int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (e < n) out[e] = swiglu_x(a[e], b[e], in_body(e, n));
+}
+
+cudaError_t launch_swiglu(float* out, const float* a, const float* b, int64_t n, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  swiglu_kernel<<<static_cast<unsigned>(ceil_div(n, 256)), 256, 0, s>>>(out, a, b, n);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rmsnorm(float* y, const float* x, const float* w, int rows, int cols,
+                           float eps, cudaStream_t s) {
+  PrepArgs a;
+  a.x = x;
+  a.prew = w;
+  a.pre_out = y;
+  a.nproj = 0;
+  a.M = rows;
+  a.K = cols;
+  a.eps = eps;
+  return launch_prep(a, s);
+}
+
+cudaError_t launch_swishgate(float* out, const float* g, const float* o, const float* w, int rows,
+                             int cols, float eps, cudaStream_t s) {
+  PrepArgs a;
+  a.x = g;
+  a.o = o;
+  a.prew = w;
+  a.pre_out = out;
+  a.nproj = 0;
+  a.M = rows;
+  a.K = cols;
+  a.eps = eps;
+  return launch_prep(a, s);
+}
+
+// ------------------------------------------------------------------------------ embed
+__global__ void embed_kernel(float* __restrict__ h, const float* __restrict__ emb,
+                             const int64_t* __restrict__ ids, int H, int V, uint32_t* err) {
+  const int t = blockIdx.x;
+  const int64_t id = ids[t];
+  const bool ok = id >= 0 && id < V;
+  if (!ok && threadIdx.x == 0 && err) atomicOr(err, kErrBadToken);
+  const float4* src = reinterpret_cast<const float4*>(emb + (ok ? id : 0) * static_cast<int64_t>(H));
+  float* dst = h + static_cast<int64_t>(t) * H;
+  if ((H & 3) == 0) {
+    for (int c = threadIdx.x; c < H / 4; c += blockDim.x)
+      reinterpret_cast<float4*>(dst)[c] = ok ? __ldg(src + c) : make_float4(0, 0, 0, 0);
+  } else {
+    const float* s1 = emb + (ok ? id : 0) * static_cast<int64_t>(H);
+    for (int c = threadIdx.x; c < H; c += blockDim.x) dst[c] = ok ? s1[c] : 0.0f;
+  }
+}
+
+cudaError_t launch_embed(float* h, const float* emb, const int64_t* ids, int T, int H, int V,
+                         uint32_t* err, cudaStream_t s) {
+  if (T == 0) return cudaSuccess;
+  embed_kernel<<<T, 256, 0, s>>>(h, emb, ids, H, V, err);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------ argmax
+// First index of the maximum; NaN never wins, and a NaN at index 0 wins outright, exactly
+// like the reference's sequential `if (l[v] > l[chosen]) chosen = v` scan. Whole block.
+__device__ int block_argmax(const float* __restrict__ l, int V) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  __shared__ int result;
+  const float first = l[0];
+  if (isnan(first)) return 0;
+  float bv = first;
+  int bi = 0;
+  for (int v = threadIdx.x; v < V; v += blockDim.x) {
+    const float x = l[v];
+    if (x > bv) { bv = x; bi = v; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) { sv[warp] = bv; si[warp] = bi; }
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    bv = lane < nw ? sv[lane] : first;
+    bi = lane < nw ? si[lane] : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    if (lane == 0) result = bi;
+  }
+  __syncthreads();
+  return result;
+}
+
+__global__ void argmax_kernel(int64_t* __restrict__ ids, const float* __restrict__ logits, int V,
+                              int ld) {
+  const int best = block_argmax(logits + static_cast<int64_t>(blockIdx.x) * ld, V);
+  if (threadIdx.x == 0) ids[blockIdx.x] = best;
+}
+
+cudaError_t launch_argmax(int64_t* ids, const float* logits, int M, int V, int ld,
+                          cudaStream_t s) {
+  if (M == 0) return cudaSuccess;
+  argmax_kernel<<<M, 1024, 0, s>>>(ids, logits, V, ld);
+  return cudaGetLastError();
+}
+
+__global__ void argmax_at_kernel(int64_t* __restrict__ ids, int64_t stride, int64_t* pos,
+                                 unsigned* done, const float* __restrict__ logits, int V, int ld) {
+  const int b = blockIdx.x;
+  const int best = block_argmax(logits + static_cast<int64_t>(b) * ld, V);
+  if (threadIdx.x == 0) {
+    const int64_t p = *pos;
+    ids[b * stride + p + 1] = best;
+    __threadfence();
+    if (atomicAdd(done, 1u) == gridDim.x - 1) {  // last block: advance the position
+      *done = 0;
+      *pos = p + 1;
+    }
+  }
+}
+
+cudaError_t launch_argmax_at(int64_t* ids, int64_t stride, int64_t* pos, unsigned* done,
+                             const float* logits, int B, int V, int ld, cudaStream_t s) {
+  if (B == 0) return cudaSuccess;
+  argmax_at_kernel<<<B, 1024, 0, s>>>(ids, stride, pos, done, logits, V, ld);
+  return cudaGetLastError();
+}
+
+__global__ void embed_at_kernel(float* __restrict__ h, const float* __restrict__ emb,
+                                const int64_t* __restrict__ ids, int64_t stride,
+                                const int64_t* pos, int H, int V, uint32_t* err) {
+  const int b = blockIdx.x;
+  const int64_t id = ids[b * stride + *pos];
+  const bool ok = id >= 0 && id < V;
+  if (!ok && threadIdx.x == 0 && err) atomicOr(err, kErrBadToken);
+  const float* src = emb + (ok ? id : 0) * static_cast<int64_t>(H);
+  float* dst = h + static_cast<int64_t>(b) * H;
+  for (int c = threadIdx.x; c < H; c += blockDim.x) dst[c] = ok ? __ldg(src + c) : 0.0f;
+}
+
+cudaError_t launch_embed_at(float* h, const float* emb, const int64_t* ids, int64_t stride,
+                            const int64_t* pos, int B, int H, int V, uint32_t* err,
+                            cudaStream_t s) {
+  if (B == 0) return cudaSuccess;
+  embed_at_kernel<<<B, 256, 0, s>>>(h, emb, ids, stride, pos, H, V, err);
+  return cudaGetLastError();
+}
+
+}  // namespace mmfree_cuda

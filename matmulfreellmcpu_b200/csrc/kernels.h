@@ -1,0 +1,98 @@
+// kernels.h -- host-side launch wrappers of the mmfree CUDA kernels (internal C++ API).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace mmfree_cuda {
+
+// How a prep row transform builds the projection input t from its inputs.
+enum PrepMode : int {
+  kPrepPlain = 0,      // t = x
+  kPrepNorm = 1,       // t = rmsnorm(x) * prew                    (attn_norm, mlp_norm, final norm)
+  kPrepSwishgate = 2,  // t = rmsnorm(x) * prew * silu(o)          (g_norm over g_proj, recurrence)
+};
+
+struct PrepArgs {
+  const float* x = nullptr;      // [M, K] rows
+  const float* o = nullptr;      // [M, K] recurrence output (kPrepSwishgate)
+  const float* prew = nullptr;   // [K] weight of the row transform
+  float* pre_out = nullptr;      // optional [M, K]: t
+  int nproj = 1;                 // projections sharing t (1..3)
+  const float* normw[3] = {};    // per projection BitLinear norm weight [K]
+  float* norm_out = nullptr;     // optional [M, K]: normalized input of projection 0
+  int8_t* planes[3] = {};        // fixed: [2][M][Kp] high bytes then low bytes of Q5.10 codes
+  int32_t* rowsum[3] = {};       // fixed: [M] sum of codes
+  float* yf[3] = {};             // float: [M][Kp] normalized activations (zero padded)
+  int M = 0, K = 0;
+  float eps = 1e-6f;
+  float qs = 1024.0f;            // 2^frac_bits
+  bool fixed = true;
+};
+
+struct MatmulArgs {
+  const void* w = nullptr;        // packed ternary weights
+  const int8_t* planes = nullptr; // fixed: [2][M][Kp]
+  const int32_t* rowsum = nullptr;
+  const float* yf = nullptr;      // float: [M][Kp]
+  int M = 0, N = 0, K = 0;
+  float scale = 1.0f;             // fixed: 1/(2^f * scale_w); float: 1/scale_w
+  float* out = nullptr;           // [M, ldo] (nullable: accumulators only)
+  int ldo = 0;
+  const float* resid = nullptr;   // optional [M, ldr]: out = resid + dequant
+  int ldr = 0;
+  int32_t* acc_out = nullptr;     // optional [M, N] raw int32 accumulators (fixed)
+  bool fixed = true;
+};
+
+// int8 ternary [n, k] (nn.Linear layout) -> tiled 2-bit format; entries outside {-1,0,1}
+// set bit 2 (kErrNotTernary) of *err (nullable) and are packed by sign.
+cudaError_t launch_repack(void* dst, const int8_t* wq, int64_t n, int64_t k, uint32_t* err,
+                          cudaStream_t s);
+cudaError_t launch_prep(const PrepArgs& a, cudaStream_t s);
+// int32 activation codes [M, K] (int16 range) -> high/low byte planes [2][M][Kp] + row sums;
+// codes outside int16 set kErrRange in *err.
+cudaError_t launch_codes_to_planes(int8_t* planes, int32_t* rowsum, const int32_t* x, int M,
+                                   int K, uint32_t* err, cudaStream_t s);
+cudaError_t launch_matmul(const MatmulArgs& a, cudaStream_t s);
+
+// HGRN token mixer (hgrn_model.cpp:109-150) over rows = nseq * len rows laid out
+// [nseq][len][H]: f = sigmoid(fraw) (lower-bounded when lb != nullptr), scan input
+// silu(i) * (1 - f) (both in place in f and i), then the recurrence of each of the nseq
+// sequences from state [nseq][H] (nullable: zero start, not written back). The reference's
+// SIMD body/tail split is taken over segments of seg_rows * H elements: the rows of one
+// reference block() call.
+cudaError_t launch_mixer(float* i, float* f, float* recur, float* state, const float* lb,
+                         int nseq, int len, int H, int seg_rows, cudaStream_t s);
+// z[t, c] = silu(y[t, c]) * y[t, I + c]  (hgrn_model.cpp:171-185), tails per seg_rows rows.
+cudaError_t launch_swiglu_split(float* z, const float* y, int rows, int I, int seg_rows,
+                                cudaStream_t s);
+// out[n] = silu(a[n]) * b[n]  (activations.cpp:9-15)
+cudaError_t launch_swiglu(float* out, const float* a, const float* b, int64_t n, cudaStream_t s);
+// rmsnorm rows (rmsnorm.cpp:11-22)
+cudaError_t launch_rmsnorm(float* y, const float* x, const float* w, int rows, int cols,
+                           float eps, cudaStream_t s);
+// rmsnorm_swishgate rows (rmsnorm_swishgate.cpp:13-30)
+cudaError_t launch_swishgate(float* out, const float* g, const float* o, const float* w, int rows,
+                             int cols, float eps, cudaStream_t s);
+// sequential scan over T (hgrn_scan.cpp:11-19); state nullable (zero start)
+cudaError_t launch_scan(float* out, const float* i, const float* f, int T, int D, float* state,
+                        cudaStream_t s);
+// h[t] = emb[ids[t]]; ids outside [0, V) raise kErrBadToken and give a zero row.
+cudaError_t launch_embed(float* h, const float* emb, const int64_t* ids, int T, int H, int V,
+                         uint32_t* err, cudaStream_t s);
+// ids[m] = first index of the maximum of logits[m, :V] (hgrn_model.cpp:271-273).
+cudaError_t launch_argmax(int64_t* ids, const float* logits, int M, int V, int ld,
+                          cudaStream_t s);
+
+// Device-resident decode loop helpers. Stream b's token at position *pos lives at
+// ids[b * stride + *pos]. embed_at gathers those B rows; argmax_at writes the greedy pick of
+// logits row b to ids[b * stride + *pos + 1] and the last block to finish advances *pos.
+cudaError_t launch_embed_at(float* h, const float* emb, const int64_t* ids, int64_t stride,
+                            const int64_t* pos, int B, int H, int V, uint32_t* err,
+                            cudaStream_t s);
+cudaError_t launch_argmax_at(int64_t* ids, int64_t stride, int64_t* pos, unsigned* done,
+                             const float* logits, int B, int V, int ld, cudaStream_t s);
+
+}  // namespace mmfree_cuda

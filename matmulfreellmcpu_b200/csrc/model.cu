@@ -1,0 +1,779 @@
+// model.cu -- device-resident HGRN-Bit forward, generate and lockstep serving.
+//
+// Control flow restates matmulfreellmCPU cpp/src/model/hgrn_model.cpp:
+//   block()            :80-195   -> Model::layers (prep / matmul / mixer kernels)
+//   layers_and_norm()  :220-237  -> Model::forward
+//   generate()         :249-347  -> Model::generate (greedy: CUDA-graph decode loop)
+//   generate_serve()   :349-454  -> Model::generate_serve (lockstep, one launch per projection)
+// Sampling (temperature > 0) follows the reference's host algorithm (:263-303, :368-406) on
+// logits copied back, so the same seed draws the same tokens.
+#include "model.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <numeric>
+#include <stdexcept>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace mmfree_cuda {
+
+namespace {
+
+void ck(cudaError_t e, const char* what) {
+  if (e != cudaSuccess)
+    throw std::runtime_error(std::string("cuda: ") + what + ": " + cudaGetErrorString(e));
+}
+#define CK(call) ck((call), #call)
+
+size_t align256(size_t n) { return (n + 255) / 256 * 256; }
+
+const char* kProjTags[6] = {"i_proj", "f_proj", "g_proj", "o_proj", "gate_proj", "down_proj"};
+
+}  // namespace
+
+Model::Model(const std::string& blob_path, int device, bool fixed, int frac_bits)
+    : device_(device), fixed_(fixed) {
+  if (frac_bits < 0 || frac_bits > 30) throw std::runtime_error("frac_bits must be in [0, 30]");
+  qs_ = static_cast<float>(1u << frac_bits);
+  CK(cudaSetDevice(device));
+  Blob blob(blob_path);
+  cfg_ = blob.config();
+  H_ = static_cast<int>(cfg_.hidden_size);
+  I_ = static_cast<int>(cfg_.intermediate_size);
+  V_ = static_cast<int>(cfg_.vocab_size);
+  L_ = static_cast<int>(cfg_.num_hidden_layers);
+  eps_ = cfg_.rms_norm_eps;
+  if (H_ <= 0 || I_ <= 0 || V_ <= 0 || L_ <= 0) throw std::runtime_error("weights: bad config");
+  if (padded_k(std::max(H_, I_)) * 4 > 227 * 1024)
+    throw std::runtime_error("hidden/intermediate size too large for the prep kernel");
+  CK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+  CK(cudaMalloc(&err_, 64));
+  CK(cudaMemset(err_, 0, 64));
+  pos_ = reinterpret_cast<int64_t*>(reinterpret_cast<char*>(err_) + 8);
+  done_ = reinterpret_cast<unsigned*>(reinterpret_cast<char*>(err_) + 16);
+
+  // ---- fp32 tensors: one arena
+  struct FpItem { std::string name; size_t n; const float** dst; };
+  std::vector<FpItem> fps;
+  layers_.resize(L_);
+  const size_t H = H_, I = I_, V = V_;
+  auto expect = [&](const std::string& name, std::vector<size_t> shape, bool i8) {
+    const BlobTensor& t = blob.get(name);
+    if (t.is_int8 != i8 || t.numel() != [&] { size_t n = 1; for (auto s : shape) n *= s; return n; }())
+      throw std::runtime_error("weights: unexpected dtype/shape for " + name);
+    return &t;
+  };
+  expect("model.embeddings", {V, H}, false);
+  fps.push_back({"model.embeddings", V * H, &emb_});
+  expect("model.norm.w", {H}, false);
+  fps.push_back({"model.norm.w", H, &final_norm_});
+  expect("lm_head.normw", {H}, false);
+  fps.push_back({"lm_head.normw", H, &lm_head_.normw});
+  const bool use_lb = cfg_.use_lower_bound && blob.has("lower_bounds");
+  if (cfg_.use_lower_bound) expect("lower_bounds", {size_t(L_), H}, false);
+  const float* lb_base = nullptr;
+  if (use_lb) fps.push_back({"lower_bounds", size_t(L_) * H, &lb_base});
+  for (int l = 0; l < L_; ++l) {
+    const std::string p = "model.layers." + std::to_string(l);
+    Layer& ly = layers_[l];
+    fps.push_back({p + ".attn_norm.w", H, &ly.attn_norm});
+    fps.push_back({p + ".mlp_norm.w", H, &ly.mlp_norm});
+    fps.push_back({p + ".g_norm.w", H, &ly.g_norm});
+    for (int j = 0; j < 6; ++j) {
+      const size_t in = j == kDown ? I : H;
+      fps.push_back({p + "." + kProjTags[j] + ".normw", in, &ly.p[j].normw});
+    }
+  }
+  size_t fp_total = 0;
+  for (auto& f : fps) {
+    expect(f.name, {f.n}, false);
+    fp_total += align256(f.n * 4);
+  }
+  CK(cudaMalloc(&fp_arena_, fp_total));
+  {
+    char* cur = reinterpret_cast<char*>(fp_arena_);
+    for (auto& f : fps) {
+      const BlobTensor& t = blob.get(f.name);
+      CK(cudaMemcpy(cur, blob.data(t), f.n * 4, cudaMemcpyHostToDevice));
+      *f.dst = reinterpret_cast<const float*>(cur);
+      cur += align256(f.n * 4);
+    }
+  }
+  for (int l = 0; l < L_; ++l) layers_[l].lb = (use_lb && l > 0) ? lb_base + size_t(l) * H : nullptr;
+
+  // ---- ternary weights: upload int8, repack to the tiled 2-bit format
+  struct WItem { std::string tag; size_t out, in; Proj* p; };
+  std::vector<WItem> ws;
+  ws.push_back({"lm_head", V, H, &lm_head_});
+  for (int l = 0; l < L_; ++l) {
+    const std::string p = "model.layers." + std::to_string(l);
+    for (int j = 0; j < 6; ++j) {
+      size_t out = H, in = H;
+      if (j == kGate) out = 2 * I;
+      if (j == kDown) in = I;
+      ws.push_back({p + "." + kProjTags[j], out, in, &layers_[l].p[j]});
+    }
+  }
+  size_t max_i8 = 0;
+  packed_bytes_ = 0;
+  for (auto& w : ws) {
+    const BlobTensor& t = blob.get(w.tag + ".wq");
+    if (!t.is_int8 || t.shape.size() != 2 || t.shape[0] != w.out || t.shape[1] != w.in)
+      throw std::runtime_error("weights: unexpected dtype/shape for " + w.tag + ".wq");
+    expect(w.tag + ".scale_w", {1}, false);
+    max_i8 = std::max(max_i8, w.out * w.in);
+    packed_bytes_ += static_cast<size_t>(packed_bytes(w.out, w.in));
+  }
+  CK(cudaMalloc(&arena_, packed_bytes_));
+  int8_t* staging = nullptr;
+  CK(cudaMalloc(&staging, max_i8));
+  {
+    char* cur = static_cast<char*>(arena_);
+    for (auto& w : ws) {
+      const BlobTensor& t = blob.get(w.tag + ".wq");
+      CK(cudaMemcpy(staging, blob.data(t), w.out * w.in, cudaMemcpyHostToDevice));
+      CK(launch_repack(cur, staging, w.out, w.in, err_, stream_));
+      CK(cudaStreamSynchronize(stream_));
+      float s;
+      std::memcpy(&s, blob.data(blob.get(w.tag + ".scale_w")), 4);
+      w.p->w = cur;
+      w.p->scale_w = s;
+      w.p->in = static_cast<int>(w.in);
+      w.p->out = static_cast<int>(w.out);
+      cur += packed_bytes(w.out, w.in);
+    }
+  }
+  cudaFree(staging);
+  uint32_t err = 0;
+  CK(cudaMemcpy(&err, err_, 4, cudaMemcpyDeviceToHost));
+  if (err & kErrNotTernary) throw std::runtime_error("weights: a wq entry is outside {-1,0,1}");
+}
+
+Model::~Model() {
+  cudaSetDevice(device_);
+  drop_graph();
+  for (cudaEvent_t e : ev_free_) cudaEventDestroy(e);
+  if (stream_) cudaStreamSynchronize(stream_);
+  cudaFree(arena_);
+  cudaFree(fp_arena_);
+  cudaFree(ws_);
+  cudaFree(state_);
+  cudaFree(loop_ids_);
+  cudaFree(err_);
+  if (pinned_) cudaFreeHost(pinned_);
+  if (stream_) cudaStreamDestroy(stream_);
+}
+
+void Model::drop_graph() {
+  if (graph_) cudaGraphExecDestroy(graph_);
+  graph_ = nullptr;
+  graph_b_ = 0;
+  graph_stride_ = 0;
+}
+
+void Model::ensure_ws(size_t rows) {
+  if (rows <= ws_rows_) return;
+  drop_graph();
+  CK(cudaStreamSynchronize(stream_));
+  cudaFree(ws_);
+  ws_ = nullptr;
+  const size_t H = H_, I = I_, V = V_;
+  const size_t Kp = static_cast<size_t>(padded_k(std::max(H_, I_)));
+  size_t sz = 0;
+  auto carve = [&](size_t bytes) { size_t o = sz; sz += align256(bytes); return o; };
+  size_t o_h = carve(rows * H * 4), o_resid = carve(rows * H * 4), o_ib = carve(rows * H * 4),
+         o_fb = carve(rows * H * 4), o_gb = carve(rows * H * 4), o_recur = carve(rows * H * 4),
+         o_y = carve(rows * 2 * I * 4), o_z = carve(rows * I * 4), o_lg = carve(rows * V * 4),
+         o_hl = carve(rows * H * 4), o_ids = carve(rows * 8);
+  size_t o_pl[3], o_rs[3], o_yf[3];
+  for (int j = 0; j < 3; ++j) {
+    o_pl[j] = fixed_ ? carve(2 * rows * Kp) : 0;
+    o_rs[j] = carve(rows * 4);
+    o_yf[j] = fixed_ ? 0 : carve(rows * Kp * 4);
+  }
+  CK(cudaMalloc(&ws_, sz));
+  char* b = static_cast<char*>(ws_);
+  h_ = reinterpret_cast<float*>(b + o_h);
+  resid_ = reinterpret_cast<float*>(b + o_resid);
+  ib_ = reinterpret_cast<float*>(b + o_ib);
+  fb_ = reinterpret_cast<float*>(b + o_fb);
+  gb_ = reinterpret_cast<float*>(b + o_gb);
+  recur_ = reinterpret_cast<float*>(b + o_recur);
+  y_ = reinterpret_cast<float*>(b + o_y);
+  z_ = reinterpret_cast<float*>(b + o_z);
+  logits_ = reinterpret_cast<float*>(b + o_lg);
+  hl_ = reinterpret_cast<float*>(b + o_hl);
+  ids_ = reinterpret_cast<int64_t*>(b + o_ids);
+  for (int j = 0; j < 3; ++j) {
+    planes_[j] = fixed_ ? reinterpret_cast<int8_t*>(b + o_pl[j]) : nullptr;
+    rowsum_[j] = reinterpret_cast<int32_t*>(b + o_rs[j]);
+    yf_[j] = fixed_ ? nullptr : reinterpret_cast<float*>(b + o_yf[j]);
+  }
+  ws_rows_ = rows;
+}
+
+void Model::float_state(size_t elems) {
+  if (elems > state_elems_) {
+    drop_graph();
+    CK(cudaStreamSynchronize(stream_));
+    cudaFree(state_);
+    state_ = nullptr;
+    CK(cudaMalloc(&state_, elems * 4));
+    state_elems_ = elems;
+  }
+  CK(cudaMemsetAsync(state_, 0, elems * 4, stream_));
+}
+
+void Model::loop_ids(size_t elems) {
+  if (elems <= loop_ids_elems_) return;
+  drop_graph();
+  CK(cudaStreamSynchronize(stream_));
+  cudaFree(loop_ids_);
+  loop_ids_ = nullptr;
+  CK(cudaMalloc(&loop_ids_, elems * 8));
+  loop_ids_elems_ = elems;
+}
+
+void Model::pinned(size_t elems) {
+  if (elems <= pinned_elems_) return;
+  CK(cudaStreamSynchronize(stream_));
+  if (pinned_) cudaFreeHost(pinned_);
+  pinned_ = nullptr;
+  CK(cudaMallocHost(&pinned_, elems * 8));
+  pinned_elems_ = elems;
+}
+
+void Model::check_errors() {
+  uint32_t err = 0;
+  CK(cudaMemcpyAsync(&err, err_, 4, cudaMemcpyDeviceToHost, stream_));
+  CK(cudaStreamSynchronize(stream_));
+  if (err) {
+    CK(cudaMemsetAsync(err_, 0, 4, stream_));
+    CK(cudaStreamSynchronize(stream_));
+    if (err & kErrBadToken) throw std::out_of_range("token id outside [0, vocab_size)");
+    throw std::runtime_error("device error flag set");
+  }
+}
+
+template <class F>
+void Model::timed(int cls, double bytes, double ops, F&& launch) {
+  if (!prof_on_) {
+    launch();
+    return;
+  }
+  auto take = [&] {
+    if (ev_free_.empty()) {
+      cudaEvent_t e;
+      CK(cudaEventCreate(&e));
+      return e;
+    }
+    cudaEvent_t e = ev_free_.back();
+    ev_free_.pop_back();
+    return e;
+  };
+  Mark m{cls, take(), take(), bytes, ops};
+  CK(cudaEventRecord(m.a, stream_));
+  launch();
+  CK(cudaEventRecord(m.b, stream_));
+  marks_.push_back(m);
+}
+
+void Model::prep(const PrepArgs& p) {
+  // algorithmic bytes: the row in (+ the gate operand), weights, planes/activations out
+  const double rows = p.M, K = p.K;
+  const double out_row = p.fixed ? 2.0 * padded_k(p.K) + 4 : 4.0 * padded_k(p.K);
+  const double bytes = rows * K * 4 * (p.o ? 2 : 1) + K * 4 * (p.nproj + (p.prew ? 1 : 0)) +
+                       rows * out_row * p.nproj;
+  timed(kClsPrep, bytes, 0, [&] { CK(launch_prep(p, stream_)); });
+}
+
+const char* Model::class_name(int c) {
+  static const char* n[kNumClasses] = {"prep", "bitlinear_matmul", "lm_head_matmul", "mixer",
+                                       "swiglu", "embed", "argmax"};
+  return (c >= 0 && c < kNumClasses) ? n[c] : "?";
+}
+
+void Model::bitlinear(const Proj& p, int plane, float* out, int M, const float* resid) {
+  MatmulArgs a;
+  a.w = p.w;
+  a.planes = planes_[plane];
+  a.rowsum = rowsum_[plane];
+  a.yf = yf_[plane];
+  a.M = M;
+  a.N = p.out;
+  a.K = p.in;
+  a.scale = fixed_ ? 1.0f / (qs_ * p.scale_w) : 1.0f / p.scale_w;
+  a.out = out;
+  a.ldo = p.out;
+  a.resid = resid;
+  a.ldr = p.out;
+  a.fixed = fixed_;
+  // algorithmic bytes (2-bit weights, activations in, outputs out) and 2*M*K*N ops
+  const double K = p.in, N = p.out;
+  const double bytes = K * N / 4 + 4.0 * M * K + 4.0 * M * N * (resid ? 2 : 1);
+  timed(&p == &lm_head_ ? kClsLmHead : kClsMatmul, bytes, 2.0 * M * K * N,
+        [&] { CK(launch_matmul(a, stream_)); });
+}
+
+template <class StateFn>
+void Model::layers(int nseq, int len, int seg_rows, StateFn state) {
+  const int rows = nseq * len;
+  for (int l = 0; l < L_; ++l) {
+    const Layer& ly = layers_[l];
+    PrepArgs p;
+    p.fixed = fixed_;
+    p.qs = qs_;
+    p.eps = eps_;
+    p.M = rows;
+    for (int j = 0; j < 3; ++j) {
+      p.planes[j] = planes_[j];
+      p.rowsum[j] = rowsum_[j];
+      p.yf[j] = yf_[j];
+    }
+    // attention: hs = rmsnorm(h) * attn_norm; i/f/g BitLinear cluster on hs
+    p.x = h_;
+    p.prew = ly.attn_norm;
+    p.K = H_;
+    p.nproj = 3;
+    p.normw[0] = ly.p[kI].normw;
+    p.normw[1] = ly.p[kF].normw;
+    p.normw[2] = ly.p[kG].normw;
+    prep(p);
+    bitlinear(ly.p[kI], 0, ib_, rows, nullptr);
+    bitlinear(ly.p[kF], 1, fb_, rows, nullptr);
+    bitlinear(ly.p[kG], 2, gb_, rows, nullptr);
+    timed(kClsMixer, 4.0 * rows * H_ * 5 + 8.0 * nseq * H_, 0, [&] {
+      CK(launch_mixer(ib_, fb_, recur_, state(l), ly.lb, nseq, len, H_, seg_rows, stream_));
+    });
+    // o_proj on g_norm(g) * silu(recurrence); resid = h + o
+    p.x = gb_;
+    p.o = recur_;
+    p.prew = ly.g_norm;
+    p.nproj = 1;
+    p.normw[0] = ly.p[kO].normw;
+    prep(p);
+    bitlinear(ly.p[kO], 0, resid_, rows, h_);
+    // mlp: gate_proj on rmsnorm(resid) * mlp_norm, swiglu, down_proj; h = resid + down
+    p.x = resid_;
+    p.o = nullptr;
+    p.prew = ly.mlp_norm;
+    p.normw[0] = ly.p[kGate].normw;
+    prep(p);
+    bitlinear(ly.p[kGate], 0, y_, rows, nullptr);
+    timed(kClsSwiglu, 12.0 * rows * I_, 0,
+          [&] { CK(launch_swiglu_split(z_, y_, rows, I_, seg_rows, stream_)); });
+    p.x = z_;
+    p.prew = nullptr;
+    p.K = I_;
+    p.normw[0] = ly.p[kDown].normw;
+    prep(p);
+    bitlinear(ly.p[kDown], 0, h_, rows, resid_);
+  }
+}
+
+void Model::head(const float* rows, int M) {
+  PrepArgs p;
+  p.fixed = fixed_;
+  p.qs = qs_;
+  p.eps = eps_;
+  p.M = M;
+  p.x = rows;
+  p.prew = final_norm_;
+  p.K = H_;
+  p.nproj = 1;
+  p.normw[0] = lm_head_.normw;
+  p.planes[0] = planes_[0];
+  p.rowsum[0] = rowsum_[0];
+  p.yf[0] = yf_[0];
+  prep(p);
+  bitlinear(lm_head_, 0, logits_, M, nullptr);
+}
+
+void Model::decode_graph_step(int B, int64_t stride) {
+  timed(kClsEmbed, 8.0 * B * H_, 0, [&] {
+    CK(launch_embed_at(h_, emb_, loop_ids_, stride, pos_, B, H_, V_, err_, stream_));
+  });
+  layers(B, 1, B, [&](int l) { return state_ + static_cast<size_t>(l) * B * H_; });
+  head(h_, B);
+  timed(kClsArgmax, 4.0 * B * V_, 0, [&] {
+    CK(launch_argmax_at(loop_ids_, stride, pos_, done_, logits_, B, V_, V_, stream_));
+  });
+}
+
+std::vector<Model::ClassStats> Model::serve_profile(size_t steps) {
+  if (serve_b_ == 0) throw std::logic_error("serve_profile without serve_begin");
+  const int B = serve_b_;
+  const int64_t stride = static_cast<int64_t>(steps) + 1;
+  loop_ids(static_cast<size_t>(stride) * B);
+  const int64_t zero = 0;
+  CK(cudaMemcpy2DAsync(loop_ids_, stride * 8, serve_last_.data(), 8, 8, B, cudaMemcpyHostToDevice,
+                       stream_));
+  CK(cudaMemcpyAsync(pos_, &zero, 8, cudaMemcpyHostToDevice, stream_));
+  marks_.clear();
+  prof_on_ = true;
+  try {
+    for (size_t s = 0; s < steps; ++s) decode_graph_step(B, stride);
+  } catch (...) {
+    prof_on_ = false;
+    throw;
+  }
+  prof_on_ = false;
+  CK(cudaStreamSynchronize(stream_));
+  std::vector<ClassStats> out(kNumClasses);
+  for (const Mark& m : marks_) {
+    float ms = 0;
+    CK(cudaEventElapsedTime(&ms, m.a, m.b));
+    ClassStats& c = out[m.cls];
+    c.ms += ms;
+    c.launches += 1;
+    c.bytes += m.bytes;
+    c.ops += m.ops;
+    ev_free_.push_back(m.a);
+    ev_free_.push_back(m.b);
+  }
+  marks_.clear();
+  pinned(static_cast<size_t>(stride) * B);
+  CK(cudaMemcpy(pinned_, loop_ids_, static_cast<size_t>(stride) * B * 8, cudaMemcpyDeviceToHost));
+  for (int b = 0; b < B; ++b) serve_last_[b] = pinned_[static_cast<size_t>(b) * stride + steps];
+  check_errors();
+  return out;
+}
+
+namespace {
+struct Sampler {
+  const Sampling& s;
+  size_t V;
+  int64_t operator()(const float* lg, std::mt19937_64& rng) const {
+    std::uniform_real_distribution<double> uni(0.0, 1.0);
+    std::vector<size_t> cand(V);
+    std::iota(cand.begin(), cand.end(), size_t(0));
+    auto hotter = [&](size_t a, size_t b) { return lg[a] > lg[b]; };
+    const size_t k = (s.top_k > 0 && static_cast<size_t>(s.top_k) < V) ? static_cast<size_t>(s.top_k) : V;
+    if (k < V) {
+      std::nth_element(cand.begin(), cand.begin() + static_cast<std::ptrdiff_t>(k), cand.end(), hotter);
+      cand.resize(k);
+    }
+    float maxl = lg[cand[0]];
+    for (size_t j = 1; j < cand.size(); ++j) maxl = std::max(maxl, lg[cand[j]]);
+    double sum = 0.0;
+    std::vector<double> p(cand.size());
+    for (size_t j = 0; j < cand.size(); ++j) {
+      p[j] = std::exp((lg[cand[j]] - maxl) / s.temperature);
+      sum += p[j];
+    }
+    const double r = uni(rng) * sum;
+    double acc = 0.0;
+    for (size_t j = 0; j < cand.size(); ++j) {
+      acc += p[j];
+      if (r <= acc) return static_cast<int64_t>(cand[j]);
+    }
+    return static_cast<int64_t>(cand.back());
+  }
+};
+}  // namespace
+
+std::vector<int64_t> Model::generate(const int64_t* ids, size_t n, size_t new_tokens,
+                                     int64_t eos_id, const Sampling& samp) {
+  CK(cudaSetDevice(device_));
+  if (n == 0) throw std::invalid_argument("generate: empty prompt");
+  for (size_t t = 0; t < n; ++t)
+    if (ids[t] < 0 || ids[t] >= V_) throw std::out_of_range("token id outside [0, vocab_size)");
+  std::vector<int64_t> stream(ids, ids + n);
+  if (new_tokens == 0) return stream;  // the prefill result is not observable
+  ensure_ws(std::max<size_t>(n, 1));
+  float_state(static_cast<size_t>(L_) * H_);
+  CK(cudaMemcpyAsync(ids_, ids, n * 8, cudaMemcpyHostToDevice, stream_));
+  CK(launch_embed(h_, emb_, ids_, static_cast<int>(n), H_, V_, err_, stream_));
+  layers(1, static_cast<int>(n), static_cast<int>(n),
+         [&](int l) { return state_ + static_cast<size_t>(l) * H_; });
+  head(h_ + (n - 1) * H_, 1);
+
+  const int64_t stride = static_cast<int64_t>(new_tokens);
+  loop_ids(new_tokens);
+  if (samp.temperature > 0.0f) {
+    // Host sampling: one logits row back per step, same draws as the reference.
+    std::mt19937_64 rng(samp.seed);
+    Sampler pick{samp, static_cast<size_t>(V_)};
+    std::vector<float> lg(V_);
+    for (size_t step = 0; step < new_tokens; ++step) {
+      if (step > 0) {
+        CK(cudaMemcpyAsync(ids_, &stream.back(), 8, cudaMemcpyHostToDevice, stream_));
+        CK(launch_embed(h_, emb_, ids_, 1, H_, V_, err_, stream_));
+        layers(1, 1, 1, [&](int l) { return state_ + static_cast<size_t>(l) * H_; });
+        head(h_, 1);
+      }
+      CK(cudaMemcpyAsync(lg.data(), logits_, V_ * 4, cudaMemcpyDeviceToHost, stream_));
+      CK(cudaStreamSynchronize(stream_));
+      const int64_t t = pick(lg.data(), rng);
+      stream.push_back(t);
+      if (t == eos_id) break;
+    }
+    check_errors();
+    return stream;
+  }
+
+  // Greedy: first token from the prefill logits, then graph replays.
+  const int64_t zero = -1;
+  CK(cudaMemcpyAsync(pos_, &zero, 8, cudaMemcpyHostToDevice, stream_));
+  CK(launch_argmax_at(loop_ids_, stride, pos_, done_, logits_, 1, V_, V_, stream_));
+  if (!graph_ || graph_b_ != 1 || graph_stride_ != stride) {
+    drop_graph();
+    CK(cudaStreamSynchronize(stream_));
+    cudaGraph_t g;
+    CK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+    decode_graph_step(1, stride);
+    CK(cudaStreamEndCapture(stream_, &g));
+    CK(cudaGraphInstantiate(&graph_, g, 0));
+    cudaGraphDestroy(g);
+    graph_b_ = 1;
+    graph_stride_ = stride;
+  }
+  pinned(new_tokens);
+  if (eos_id < 0) {
+    for (size_t step = 1; step < new_tokens; ++step) CK(cudaGraphLaunch(graph_, stream_));
+    CK(cudaMemcpyAsync(pinned_, loop_ids_, new_tokens * 8, cudaMemcpyDeviceToHost, stream_));
+    CK(cudaStreamSynchronize(stream_));
+    check_errors();
+    stream.insert(stream.end(), pinned_, pinned_ + new_tokens);
+    return stream;
+  }
+  for (size_t step = 0; step < new_tokens; ++step) {
+    if (step > 0) CK(cudaGraphLaunch(graph_, stream_));
+    CK(cudaMemcpyAsync(pinned_, loop_ids_ + step, 8, cudaMemcpyDeviceToHost, stream_));
+    CK(cudaStreamSynchronize(stream_));
+    stream.push_back(pinned_[0]);
+    if (pinned_[0] == eos_id) break;
+  }
+  check_errors();
+  return stream;
+}
+
+void Model::forward(const int64_t* ids, size_t T, float* logits, bool last_row_only) {
+  CK(cudaSetDevice(device_));
+  if (T == 0) throw std::invalid_argument("forward: empty input");
+  for (size_t t = 0; t < T; ++t)
+    if (ids[t] < 0 || ids[t] >= V_) throw std::out_of_range("token id outside [0, vocab_size)");
+  ensure_ws(T);
+  CK(cudaMemcpyAsync(ids_, ids, T * 8, cudaMemcpyHostToDevice, stream_));
+  CK(launch_embed(h_, emb_, ids_, static_cast<int>(T), H_, V_, err_, stream_));
+  layers(1, static_cast<int>(T), static_cast<int>(T), [](int) { return static_cast<float*>(nullptr); });
+  if (last_row_only) {
+    head(h_ + (T - 1) * H_, 1);
+    CK(cudaMemcpyAsync(logits, logits_, static_cast<size_t>(V_) * 4, cudaMemcpyDeviceToHost, stream_));
+  } else {
+    head(h_, static_cast<int>(T));
+    CK(cudaMemcpyAsync(logits, logits_, T * V_ * 4, cudaMemcpyDeviceToHost, stream_));
+  }
+  CK(cudaStreamSynchronize(stream_));
+  check_errors();
+}
+
+void Model::serve_begin(const std::vector<std::vector<int64_t>>& prompts, int64_t* first_ids) {
+  CK(cudaSetDevice(device_));
+  const size_t B = prompts.size();
+  if (B == 0) throw std::invalid_argument("serve: no prompts");
+  size_t max_rows = B;
+  for (const auto& p : prompts) {
+    if (p.empty()) throw std::invalid_argument("serve: empty prompt");
+    for (int64_t t : p)
+      if (t < 0 || t >= V_) throw std::out_of_range("token id outside [0, vocab_size)");
+  }
+  // prefill runs of consecutive streams with equal prompt length as one batch
+  std::vector<std::pair<size_t, size_t>> runs;  // (first stream, count)
+  for (size_t b = 0; b < B;) {
+    size_t e = b + 1;
+    while (e < B && prompts[e].size() == prompts[b].size()) ++e;
+    runs.push_back({b, e - b});
+    max_rows = std::max(max_rows, (e - b) * prompts[b].size());
+    b = e;
+  }
+  ensure_ws(max_rows);
+  float_state(static_cast<size_t>(L_) * B * H_);
+  pinned(std::max(max_rows, B));
+  for (const auto& run : runs) {
+    const size_t b0 = run.first, G = run.second;
+    const size_t T0 = prompts[b0].size();
+    for (size_t g = 0; g < G; ++g) std::memcpy(pinned_ + g * T0, prompts[b0 + g].data(), T0 * 8);
+    CK(cudaMemcpyAsync(ids_, pinned_, G * T0 * 8, cudaMemcpyHostToDevice, stream_));
+    CK(launch_embed(h_, emb_, ids_, static_cast<int>(G * T0), H_, V_, err_, stream_));
+    const size_t Bsz = B;
+    layers(static_cast<int>(G), static_cast<int>(T0), static_cast<int>(T0), [&](int l) {
+      return state_ + (static_cast<size_t>(l) * Bsz + b0) * H_;
+    });
+    // last row of every stream in the run -> hl_ [G][H]
+    CK(cudaMemcpy2DAsync(hl_, H_ * 4, h_ + (T0 - 1) * H_, T0 * H_ * 4, H_ * 4, G,
+                         cudaMemcpyDeviceToDevice, stream_));
+    head(hl_, static_cast<int>(G));
+    CK(launch_argmax(ids_, logits_, static_cast<int>(G), V_, V_, stream_));
+    CK(cudaMemcpyAsync(first_ids + b0, ids_, G * 8, cudaMemcpyDeviceToHost, stream_));
+    CK(cudaStreamSynchronize(stream_));
+  }
+  check_errors();
+  serve_b_ = static_cast<int>(B);
+  serve_last_.assign(first_ids, first_ids + B);
+}
+
+void Model::serve_step(const int64_t* in_ids, int64_t* out_ids) {
+  if (serve_b_ == 0) throw std::logic_error("serve_step without serve_begin");
+  const int B = serve_b_;
+  // one lockstep step: ids [B][2], position 0 holds the inputs
+  loop_ids(static_cast<size_t>(2) * B);
+  if (!graph_ || graph_b_ != B || graph_stride_ != 2) {
+    drop_graph();
+    CK(cudaStreamSynchronize(stream_));
+    cudaGraph_t g;
+    CK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+    decode_graph_step(B, 2);
+    CK(cudaStreamEndCapture(stream_, &g));
+    CK(cudaGraphInstantiate(&graph_, g, 0));
+    cudaGraphDestroy(g);
+    graph_b_ = B;
+    graph_stride_ = 2;
+  }
+  pinned(static_cast<size_t>(2) * B + 1);
+  for (int b = 0; b < B; ++b) pinned_[2 * b] = in_ids[b];
+  pinned_[2 * B] = 0;  // position
+  CK(cudaMemcpyAsync(loop_ids_, pinned_, static_cast<size_t>(2) * B * 8, cudaMemcpyHostToDevice, stream_));
+  CK(cudaMemcpyAsync(pos_, pinned_ + 2 * B, 8, cudaMemcpyHostToDevice, stream_));
+  CK(cudaGraphLaunch(graph_, stream_));
+  CK(cudaMemcpy2DAsync(out_ids, 8, loop_ids_ + 1, 16, 8, B, cudaMemcpyDeviceToHost, stream_));
+  CK(cudaStreamSynchronize(stream_));
+  serve_last_.assign(out_ids, out_ids + B);
+}
+
+void Model::serve_run(size_t steps, int64_t* out) {
+  if (serve_b_ == 0) throw std::logic_error("serve_run without serve_begin");
+  const int B = serve_b_;
+  const int64_t stride = static_cast<int64_t>(steps) + 1;
+  loop_ids(static_cast<size_t>(stride) * B);
+  if (!graph_ || graph_b_ != B || graph_stride_ != stride) {
+    drop_graph();
+    CK(cudaStreamSynchronize(stream_));
+    cudaGraph_t g;
+    CK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+    decode_graph_step(B, stride);
+    CK(cudaStreamEndCapture(stream_, &g));
+    CK(cudaGraphInstantiate(&graph_, g, 0));
+    cudaGraphDestroy(g);
+    graph_b_ = B;
+    graph_stride_ = stride;
+  }
+  pinned(static_cast<size_t>(stride) * B + 1);
+  const int64_t zero = 0;
+  CK(cudaMemcpy2DAsync(loop_ids_, stride * 8, serve_last_.data(), 8, 8, B, cudaMemcpyHostToDevice,
+                       stream_));
+  CK(cudaMemcpyAsync(pos_, &zero, 8, cudaMemcpyHostToDevice, stream_));
+  for (size_t s = 0; s < steps; ++s) CK(cudaGraphLaunch(graph_, stream_));
+  CK(cudaMemcpyAsync(pinned_, loop_ids_, static_cast<size_t>(stride) * B * 8, cudaMemcpyDeviceToHost,
+                     stream_));
+  CK(cudaStreamSynchronize(stream_));
+  check_errors();
+  for (int b = 0; b < B; ++b) {
+    std::memcpy(out + static_cast<size_t>(b) * steps, pinned_ + static_cast<size_t>(b) * stride + 1,
+                steps * 8);
+    serve_last_[b] = pinned_[static_cast<size_t>(b) * stride + steps];
+  }
+}
+
+void Model::serve_end() { serve_b_ = 0; }
+
+std::vector<std::vector<int64_t>> Model::generate_serve(
+    const std::vector<std::vector<int64_t>>& prompts, size_t new_tokens, int64_t eos_id,
+    const Sampling& samp) {
+  const size_t B = prompts.size();
+  std::vector<std::vector<int64_t>> streams = prompts;
+  if (B == 0) return streams;
+  std::vector<int64_t> first(B);
+  if (samp.temperature > 0.0f) {
+    // host-sampled lockstep loop (hgrn_model.cpp:368-406): per-stream RNG seeded seed + b,
+    // prefill stream by stream, then one batched step per token.
+    CK(cudaSetDevice(device_));
+    size_t max_t = B;
+    for (const auto& p : prompts) {
+      if (p.empty()) throw std::invalid_argument("serve: empty prompt");
+      for (int64_t t : p)
+        if (t < 0 || t >= V_) throw std::out_of_range("token id outside [0, vocab_size)");
+      max_t = std::max(max_t, p.size());
+    }
+    std::vector<std::mt19937_64> rng;
+    rng.reserve(B);
+    for (size_t b = 0; b < B; ++b) rng.emplace_back(samp.seed + b);
+    Sampler pick{samp, static_cast<size_t>(V_)};
+    std::vector<char> done(B, 0);
+    std::vector<float> lg(static_cast<size_t>(V_) * B);
+    ensure_ws(max_t);
+    float_state(static_cast<size_t>(L_) * B * H_);
+    for (size_t b = 0; b < B; ++b) {
+      const size_t T0 = prompts[b].size();
+      CK(cudaMemcpyAsync(ids_, prompts[b].data(), T0 * 8, cudaMemcpyHostToDevice, stream_));
+      CK(launch_embed(h_, emb_, ids_, static_cast<int>(T0), H_, V_, err_, stream_));
+      layers(1, static_cast<int>(T0), static_cast<int>(T0),
+             [&](int l) { return state_ + (static_cast<size_t>(l) * B + b) * H_; });
+      head(h_ + (T0 - 1) * H_, 1);
+      CK(cudaMemcpyAsync(lg.data(), logits_, V_ * 4, cudaMemcpyDeviceToHost, stream_));
+      CK(cudaStreamSynchronize(stream_));
+      const int64_t t0 = pick(lg.data(), rng[b]);
+      streams[b].push_back(t0);
+      if (t0 == eos_id) done[b] = 1;
+    }
+    std::vector<int64_t> last(B);
+    for (size_t step = 1; step < new_tokens; ++step) {
+      for (size_t b = 0; b < B; ++b) last[b] = streams[b].back();
+      CK(cudaMemcpyAsync(ids_, last.data(), B * 8, cudaMemcpyHostToDevice, stream_));
+      CK(launch_embed(h_, emb_, ids_, static_cast<int>(B), H_, V_, err_, stream_));
+      layers(static_cast<int>(B), 1, static_cast<int>(B),
+             [&](int l) { return state_ + static_cast<size_t>(l) * B * H_; });
+      head(h_, static_cast<int>(B));
+      CK(cudaMemcpyAsync(lg.data(), logits_, B * V_ * 4, cudaMemcpyDeviceToHost, stream_));
+      CK(cudaStreamSynchronize(stream_));
+      bool all_done = true;
+      for (size_t b = 0; b < B; ++b) {
+        if (done[b]) continue;
+        const int64_t t = pick(lg.data() + b * V_, rng[b]);
+        streams[b].push_back(t);
+        if (t == eos_id) done[b] = 1;
+        else all_done = false;
+      }
+      if (all_done) break;
+    }
+    check_errors();
+    return streams;
+  }
+
+  serve_begin(prompts, first.data());
+  std::vector<char> done(B, 0);
+  for (size_t b = 0; b < B; ++b) {
+    streams[b].push_back(first[b]);
+    if (first[b] == eos_id) done[b] = 1;
+  }
+  if (new_tokens > 1) {
+    const size_t steps = new_tokens - 1;
+    std::vector<int64_t> out(B * steps);
+    if (eos_id < 0) {
+      serve_run(steps, out.data());
+      for (size_t b = 0; b < B; ++b)
+        streams[b].insert(streams[b].end(), out.begin() + b * steps, out.begin() + (b + 1) * steps);
+    } else {
+      // a finished stream keeps its slot (its outputs are dropped), as in the reference
+      std::vector<int64_t> step_ids(B);
+      for (size_t s = 0; s < steps; ++s) {
+        serve_run(1, step_ids.data());
+        bool all_done = true;
+        for (size_t b = 0; b < B; ++b) {
+          if (done[b]) continue;
+          streams[b].push_back(step_ids[b]);
+          if (step_ids[b] == eos_id) done[b] = 1;
+          else all_done = false;
+        }
+        if (all_done) break;
+      }
+    }
+  }
+  serve_end();
+  return streams;
+}
+
+}  // namespace mmfree_cuda

@@ -1,0 +1,163 @@
+// model.h -- device-resident HGRN-Bit forward (the CUDA counterpart of mmfree::Model,
+// matmulfreellmCPU cpp/include/mmfree/model.hpp:33-120).
+//
+// Weights are uploaded once from the model.mmfree blob; every BitLinear weight is repacked
+// on the device into the tiled 2-bit format (common.cuh). Activations, the recurrent state
+// [L][B][H] and the token ids stay in HBM across steps; the per-token decode step is
+// captured in a CUDA graph and replayed with a device-side position counter, so a greedy
+// generation needs no host round trip until the ids are copied back.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <memory>
+#include <random>
+#include <string>
+#include <vector>
+
+#include "blob.h"
+#include "kernels.h"
+
+namespace mmfree_cuda {
+
+struct Sampling {  // model.hpp:27-31
+  float temperature = 0.0f;
+  int top_k = 0;
+  uint64_t seed = 0;
+};
+
+class Model {
+ public:
+  Model(const std::string& blob_path, int device, bool fixed, int frac_bits);
+  ~Model();
+  Model(const Model&) = delete;
+  Model& operator=(const Model&) = delete;
+
+  const BlobConfig& config() const { return cfg_; }
+  int device() const { return device_; }
+  cudaStream_t stream() const { return stream_; }
+  size_t weight_bytes() const { return packed_bytes_; }
+
+  // model.hpp:36-50 / hgrn_model.cpp:249-347.
+  std::vector<int64_t> generate(const int64_t* ids, size_t n, size_t new_tokens, int64_t eos_id,
+                                const Sampling& samp);
+  // model.hpp:34 / hgrn_model.cpp:239-247: logits [T, V] (host), or only the last row.
+  void forward(const int64_t* ids, size_t T, float* logits, bool last_row_only);
+  // model.hpp:52-70 / hgrn_model.cpp:349-454.
+  std::vector<std::vector<int64_t>> generate_serve(const std::vector<std::vector<int64_t>>& prompts,
+                                                   size_t new_tokens, int64_t eos_id,
+                                                   const Sampling& samp);
+
+  // Serving session, one lockstep decode step per call (host ids in, host ids out). begin
+  // prefills every prompt and returns each stream's first greedy token.
+  void serve_begin(const std::vector<std::vector<int64_t>>& prompts, int64_t* first_ids);
+  void serve_step(const int64_t* in_ids, int64_t* out_ids);
+  void serve_end();
+  int serve_batch() const { return serve_b_; }
+
+  // Greedy decode steps of a serving session with no host round trip: `steps` lockstep
+  // steps starting from the session's last tokens, ids written to out [B][steps] (host).
+  void serve_run(size_t steps, int64_t* out);
+
+  // Kernel classes of a decode step, for serve_profile.
+  enum KernelClass { kClsPrep = 0, kClsMatmul, kClsLmHead, kClsMixer, kClsSwiglu, kClsEmbed,
+                     kClsArgmax, kNumClasses };
+  struct ClassStats {
+    double ms = 0;        // summed device time of the class's launches
+    int64_t launches = 0;
+    double bytes = 0;     // algorithmic bytes moved by those launches
+    double ops = 0;       // algorithmic integer/float ops (2*M*K*N per BitLinear)
+  };
+  static const char* class_name(int c);
+  // `steps` greedy decode steps like serve_run (same kernels, not graph-captured), with a
+  // CUDA event pair around every launch; returns per-class totals.
+  std::vector<ClassStats> serve_profile(size_t steps);
+  // the stream every kernel of this model is launched on
+
+ private:
+  struct Proj {
+    const void* w = nullptr;
+    const float* normw = nullptr;
+    float scale_w = 1.0f;
+    int in = 0, out = 0;
+  };
+  struct Layer {
+    const float* attn_norm = nullptr;
+    const float* mlp_norm = nullptr;
+    const float* g_norm = nullptr;
+    const float* lb = nullptr;  // lower bound row of this layer (nullptr for layer 0)
+    Proj p[6];                  // i, f, g, o, gate, down
+  };
+  enum { kI = 0, kF, kG, kO, kGate, kDown };
+
+  void ensure_ws(size_t rows);
+  void prep(const PrepArgs& p);
+  template <class F>
+  void timed(int cls, double bytes, double ops, F&& launch);
+  void bitlinear(const Proj& p, int plane, float* out, int M, const float* resid);
+  // All layers over `rows` = nseq * len rows of h_ ([nseq][len][H]); state(l) gives the
+  // layer's state base ([nseq][H]) or nullptr; seg_rows = rows of one reference block call.
+  template <class StateFn>
+  void layers(int nseq, int len, int seg_rows, StateFn state);
+  void head(const float* rows, int M);  // final norm + lm_head into logits_
+  void check_errors();
+  void decode_graph_step(int B, int64_t stride);  // embed_at, layers (streams), head, argmax_at
+
+  BlobConfig cfg_;
+  int device_ = 0;
+  bool fixed_ = true;
+  float qs_ = 1024.0f;
+  int H_ = 0, I_ = 0, V_ = 0, L_ = 0;
+  float eps_ = 1e-6f;
+  cudaStream_t stream_ = nullptr;
+
+  // weights
+  void* arena_ = nullptr;          // packed ternary weights of every projection
+  size_t packed_bytes_ = 0;
+  float* fp_arena_ = nullptr;      // embeddings, norms, lower bounds
+  const float* emb_ = nullptr;
+  const float* final_norm_ = nullptr;
+  Proj lm_head_;
+  std::vector<Layer> layers_;
+
+  // workspace (rows = capacity)
+  size_t ws_rows_ = 0;
+  void* ws_ = nullptr;
+  float *h_ = nullptr, *resid_ = nullptr, *ib_ = nullptr, *fb_ = nullptr, *gb_ = nullptr;
+  float *recur_ = nullptr, *y_ = nullptr, *z_ = nullptr, *logits_ = nullptr, *hl_ = nullptr;
+  int8_t* planes_[3] = {};
+  int32_t* rowsum_[3] = {};
+  float* yf_[3] = {};
+  int64_t* ids_ = nullptr;
+
+  // state and decode loop
+  float* state_ = nullptr;
+  size_t state_elems_ = 0;
+  int64_t* loop_ids_ = nullptr;    // [B][stride]
+  size_t loop_ids_elems_ = 0;
+  int64_t* pos_ = nullptr;         // device position counter
+  unsigned* done_ = nullptr;       // argmax_at completion counter
+  uint32_t* err_ = nullptr;        // device error flags
+  int64_t* pinned_ = nullptr;      // pinned staging for ids
+  size_t pinned_elems_ = 0;
+
+  cudaGraphExec_t graph_ = nullptr;  // captured decode step
+  int graph_b_ = 0;
+  int64_t graph_stride_ = 0;
+
+  bool prof_on_ = false;
+  struct Mark { int cls; cudaEvent_t a, b; double bytes, ops; };
+  std::vector<Mark> marks_;
+  std::vector<cudaEvent_t> ev_free_;
+
+  int serve_b_ = 0;                // active serving session batch (0 = none)
+  std::vector<int64_t> serve_last_;
+
+  void float_state(size_t elems);
+  void loop_ids(size_t elems);
+  void pinned(size_t elems);
+  void drop_graph();
+};
+
+}  // namespace mmfree_cuda

@@ -1,0 +1,164 @@
+"""GPU parity of the model path (generate / forward / generate_serve / serving session)
+against the reference's own outputs (golden fixtures) and the CPU oracle.
+
+FixedQ510 must match bit for bit (ids and logits). Float must match the logits within
+max|d| <= 1e-3 * (max - min) of the reference logits.
+"""
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import pytest
+
+from conftest import bits_equal, golden
+from matmulfreellmcpu_b200 import _lib, api
+from matmulfreellmcpu_b200 import blob as B
+
+pytestmark = pytest.mark.gpu
+
+
+def float_close(got, ref, rel=1e-3):
+    span = float(ref.max() - ref.min())
+    return float(np.abs(got - ref).max()) <= rel * span
+
+
+@pytest.fixture(scope="module")
+def models(cuda, blob_cache):
+    cache = {}
+
+    def get(name, mode):
+        key = (name, mode)
+        if key not in cache:
+            cache[key] = api.Model(B.cached_blob(name, 0, blob_cache), mode)
+        return cache[key]
+    yield get
+    for m in cache.values():
+        m.close()
+
+
+@pytest.mark.parametrize("name", ["tiny", "ragged", "small"])
+def test_small_models_golden(models, name):
+    g = golden(f"model_{name}.npz")
+    prompts = [g[f"serve_prompt{k}"] for k in range(3)]
+    m = models(name, "fixed")
+    stream = m.generate(g["prompt"], 9)
+    assert np.array_equal(stream, g["fixed_stream"])
+    assert bits_equal(m.forward_last(stream), g["fixed_logits"])
+    assert bits_equal(m.forward(g["prompt"]), g["fixed_prefix_logits"])
+    for k, s in enumerate(m.generate_serve(prompts, 6)):
+        assert np.array_equal(s, g[f"fixed_serve{k}"])
+    mf = models(name, "float")
+    assert float_close(mf.forward_last(g["float_stream"]), g["float_logits"])
+    assert float_close(mf.forward(g["prompt"]), g["float_prefix_logits"])
+    assert np.array_equal(mf.generate(g["prompt"], 9), g["float_stream"])
+
+
+def test_serve_identical_prompts_match_generate(models):
+    """model.hpp:58-59: B identical prompts + greedy give identical streams = generate()."""
+    m = models("small", "fixed")
+    p = B.seeded_ids(11, 42, 2048)
+    single = m.generate(p, 12)
+    for s in m.generate_serve([p] * 5, 12):
+        assert np.array_equal(s, single)
+
+
+def test_serve_session_matches_generate_serve(models):
+    m = models("small", "fixed")
+    prompts = [B.seeded_ids(9, 70 + k, 2048) for k in range(4)]
+    ref = m.generate_serve(prompts, 8)
+    first = m.serve_begin(prompts)
+    got = [[f] for f in first]
+    last = first
+    for _ in range(3):  # step-wise with host ids
+        last = m.serve_step(last)
+        for b in range(4):
+            got[b].append(last[b])
+    rest = m.serve_run(4)  # device loop
+    m.serve_end()
+    for b in range(4):
+        assert np.array_equal(np.concatenate([prompts[b], got[b], rest[b]]), ref[b])
+
+
+def test_ragged_prompt_lengths_and_zero_tokens(models, orc, blob_cache):
+    m = models("ragged", "fixed")
+    om = orc.model(B.Blob.open(B.cached_blob("ragged", 0, blob_cache)))
+    prompts = [B.seeded_ids(n, 300 + n, 300) for n in (3, 3, 7, 1, 7)]
+    for gen in (0, 1, 5):
+        got = m.generate_serve(prompts, gen)
+        ref = om.generate_serve(prompts, gen)
+        for a, b in zip(got, ref):
+            assert np.array_equal(a, b)
+    assert np.array_equal(m.generate(prompts[2], 0), prompts[2])
+
+
+def test_eos_stops_streams(models):
+    m = models("small", "fixed")
+    p = B.seeded_ids(10, 5, 2048)
+    full = m.generate(p, 10)
+    eos = int(full[p.size + 3])
+    cut = m.generate(p, 10, eos_id=eos)
+    first = p.size + int(np.argmax(full[p.size:] == eos))
+    assert np.array_equal(cut, full[:first + 1])
+    streams = m.generate_serve([p, B.seeded_ids(10, 6, 2048)], 10, eos_id=eos)
+    assert np.array_equal(streams[0], cut)
+
+
+def test_sampling_matches_reference(models, blob_cache):
+    """temperature/top-k sampling draws the same tokens as the reference for the same seed."""
+    import oracle
+    if not os.path.exists(oracle.REF_SO):
+        pytest.fail("prebuilt reference library missing (oracle/_ref travels with the repo)")
+    R = oracle.Reference()
+    path = B.cached_blob("small", 0, blob_cache)
+    rm = R.model(path, 1)
+    m = models("small", "fixed")
+    p = B.seeded_ids(6, 9, 2048)
+    for temp, k, seed in ((0.8, 0, 1), (1.5, 40, 7)):
+        assert np.array_equal(m.generate(p, 12, temperature=temp, top_k=k, seed=seed),
+                              rm.generate(p, 12, temperature=temp, top_k=k, seed=seed))
+        ps = [p, B.seeded_ids(4, 10, 2048)]
+        for a, b in zip(m.generate_serve(ps, 6, temperature=temp, top_k=k, seed=seed),
+                        rm.generate_serve(ps, 6, temperature=temp, top_k=k, seed=seed)):
+            assert np.array_equal(a, b)
+    rm.close()
+
+
+def test_bad_token_ids(models):
+    m = models("tiny", "fixed")
+    for bad in ([1, 512], [-1]):
+        with pytest.raises(_lib.MmfreeError) as e:
+            m.generate(bad, 3)
+        assert e.value.code == _lib.E_RANGE
+    with pytest.raises(_lib.MmfreeError) as e:
+        m.serve_step([1, 2, 3])
+    assert e.value.code in (_lib.E_STATE, _lib.E_INVALID)
+
+
+def test_missing_blob(cuda, tmp_path):
+    with pytest.raises(_lib.MmfreeError) as e:
+        api.Model(str(tmp_path / "nope.mmfree"))
+    assert e.value.code == _lib.E_IO
+
+
+def test_config0_370m_golden(models):
+    """Benchmark configuration 0 (370M, 16 ids, 32 greedy tokens) bit for bit."""
+    g = golden("config_370M.npz")
+    m = models("370M", "fixed")
+    stream = m.generate(g["prompt"], 32)
+    assert np.array_equal(stream, g["fixed_stream"])
+    assert bits_equal(m.forward_last(stream), g["fixed_logits"])
+    mf = models("370M", "float")
+    assert float_close(mf.forward_last(g["float_stream"]), g["float_logits"])
+
+
+@pytest.mark.slow
+def test_config2_1p3b_golden(models):
+    """Benchmark configuration 2 (1.3B, 128-id prompt, 256 greedy tokens) bit for bit."""
+    g = golden("config_1.3B.npz")
+    m = models("1.3B", "fixed")
+    stream = m.generate(g["prompt"], 256)
+    assert np.array_equal(stream, g["fixed_stream"])
+    assert bits_equal(m.forward_last(stream), g["fixed_logits"])
+    mf = models("1.3B", "float")
+    assert float_close(mf.forward_last(g["float_stream"]), g["float_logits"])
