@@ -134,6 +134,13 @@ int mmfree_cuda_forward(mmfree_cuda_model* m, const int64_t* ids, size_t T, floa
 int mmfree_cuda_forward_last(mmfree_cuda_model* m, const int64_t* ids, size_t T,
                              float* logits);
 
+/* Model::forward plus an intermediate trace for parity debugging (the counterpart of the
+ * reference spec's capture hooks, tools/reference.py:108-117): logits [T, vocab_size] and
+ * trace [(1 + 3 L), T, hidden_size] = embeddings, then per layer the recurrence output,
+ * the residual after o_proj and the layer output. */
+int mmfree_cuda_forward_trace(mmfree_cuda_model* m, const int64_t* ids, size_t T, float* logits,
+                              float* trace);
+
 /* Replaces Model::generate_serve (model.hpp:52-70): B prompts (host pointers + lengths);
  * out is [B, out_stride], stream b's full ids in out[b*out_stride ...], length out_lens[b]. */
 int mmfree_cuda_generate_serve(mmfree_cuda_model* m, size_t B, const int64_t* const* prompts,

@@ -41,6 +41,7 @@ SIGNATURES = {
     "mmfree_cuda_generate": (I, [VP, VP, SZ, SZ, I64, F, I, U64, VP, SZ, C.POINTER(SZ)]),
     "mmfree_cuda_forward": (I, [VP, VP, SZ, VP]),
     "mmfree_cuda_forward_last": (I, [VP, VP, SZ, VP]),
+    "mmfree_cuda_forward_trace": (I, [VP, VP, SZ, VP, VP]),
     "mmfree_cuda_generate_serve": (I, [VP, SZ, VP, VP, SZ, I64, F, I, U64, VP, SZ, VP]),
     "mmfree_cuda_serve_begin": (I, [VP, SZ, VP, VP, VP]),
     "mmfree_cuda_serve_step": (I, [VP, VP, VP]),

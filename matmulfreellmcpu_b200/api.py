@@ -124,6 +124,17 @@ class Model:
         check(lib().mmfree_cuda_forward(self._h, ids.ctypes.data, ids.size, lg.ctypes.data))
         return lg
 
+    def forward_trace(self, ids):
+        """(logits [T, V], trace [1 + 3L, T, H]): embeddings, then per layer the recurrence
+        output, the residual after o_proj and the layer output."""
+        ids = _i64(ids)
+        c = self.config
+        lg = np.empty((ids.size, c.vocab_size), np.float32)
+        tr = np.empty((1 + 3 * c.num_hidden_layers, ids.size, c.hidden_size), np.float32)
+        check(lib().mmfree_cuda_forward_trace(self._h, ids.ctypes.data, ids.size, lg.ctypes.data,
+                                              tr.ctypes.data))
+        return lg, tr
+
     def forward_last(self, ids) -> np.ndarray:
         ids = _i64(ids)
         lg = np.empty(self.config.vocab_size, np.float32)

@@ -91,6 +91,7 @@ char* scratch(size_t bytes) {
     const size_t grow = bytes < (size_t(1) << 20) ? (size_t(1) << 20) : bytes;
     ck(cudaMalloc(&s.base, grow), "cudaMalloc(scratch)");
     ck(cudaMemset(s.base, 0, 256), "cudaMemset(scratch)");
+    ck(cudaDeviceSynchronize(), "cudaDeviceSynchronize");  // order before any caller stream
     s.bytes = grow;
   }
   return static_cast<char*>(s.base);
@@ -399,6 +400,14 @@ int mmfree_cuda_forward_last(mmfree_cuda_model* m, const int64_t* ids, size_t T,
   return guard([&] {
     need(m && ids && logits, "null pointer");
     m->impl->forward(ids, T, logits, true);
+  });
+}
+
+int mmfree_cuda_forward_trace(mmfree_cuda_model* m, const int64_t* ids, size_t T, float* logits,
+                              float* trace) {
+  return guard([&] {
+    need(m && ids && logits && trace, "null pointer");
+    m->impl->forward_trace(ids, T, logits, trace);
   });
 }
 

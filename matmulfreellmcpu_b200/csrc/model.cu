@@ -51,7 +51,7 @@ Model::Model(const std::string& blob_path, int device, bool fixed, int frac_bits
     throw std::runtime_error("hidden/intermediate size too large for the prep kernel");
   CK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
   CK(cudaMalloc(&err_, 64));
-  CK(cudaMemset(err_, 0, 64));
+  CK(cudaMemsetAsync(err_, 0, 64, stream_));
   pos_ = reinterpret_cast<int64_t*>(reinterpret_cast<char*>(err_) + 8);
   done_ = reinterpret_cast<unsigned*>(reinterpret_cast<char*>(err_) + 16);
 
@@ -97,7 +97,9 @@ Model::Model(const std::string& blob_path, int device, bool fixed, int frac_bits
     char* cur = reinterpret_cast<char*>(fp_arena_);
     for (auto& f : fps) {
       const BlobTensor& t = blob.get(f.name);
-      CK(cudaMemcpy(cur, blob.data(t), f.n * 4, cudaMemcpyHostToDevice));
+      // stream-ordered: a blocking cudaMemcpy from pageable memory may return before its
+      // DMA lands, and nothing orders the legacy stream before this non-blocking stream
+      CK(cudaMemcpyAsync(cur, blob.data(t), f.n * 4, cudaMemcpyHostToDevice, stream_));
       *f.dst = reinterpret_cast<const float*>(cur);
       cur += align256(f.n * 4);
     }
@@ -134,9 +136,8 @@ Model::Model(const std::string& blob_path, int device, bool fixed, int frac_bits
     char* cur = static_cast<char*>(arena_);
     for (auto& w : ws) {
       const BlobTensor& t = blob.get(w.tag + ".wq");
-      CK(cudaMemcpy(staging, blob.data(t), w.out * w.in, cudaMemcpyHostToDevice));
+      CK(cudaMemcpyAsync(staging, blob.data(t), w.out * w.in, cudaMemcpyHostToDevice, stream_));
       CK(launch_repack(cur, staging, w.out, w.in, err_, stream_));
-      CK(cudaStreamSynchronize(stream_));
       float s;
       std::memcpy(&s, blob.data(blob.get(w.tag + ".scale_w")), 4);
       w.p->w = cur;
@@ -146,9 +147,10 @@ Model::Model(const std::string& blob_path, int device, bool fixed, int frac_bits
       cur += packed_bytes(w.out, w.in);
     }
   }
-  cudaFree(staging);
   uint32_t err = 0;
-  CK(cudaMemcpy(&err, err_, 4, cudaMemcpyDeviceToHost));
+  CK(cudaMemcpyAsync(&err, err_, 4, cudaMemcpyDeviceToHost, stream_));
+  CK(cudaStreamSynchronize(stream_));
+  cudaFree(staging);
   if (err & kErrNotTernary) throw std::runtime_error("weights: a wq entry is outside {-1,0,1}");
 }
 
@@ -371,7 +373,37 @@ void Model::layers(int nseq, int len, int seg_rows, StateFn state) {
     p.normw[0] = ly.p[kDown].normw;
     prep(p);
     bitlinear(ly.p[kDown], 0, h_, rows, resid_);
+    if (trace_) {  // recurrence output, residual after o_proj, layer output
+      const size_t th = static_cast<size_t>(rows) * H_;
+      float* tr = trace_ + th * (1 + 3 * static_cast<size_t>(l));
+      CK(cudaMemcpyAsync(tr, recur_, th * 4, cudaMemcpyDeviceToHost, stream_));
+      CK(cudaMemcpyAsync(tr + th, resid_, th * 4, cudaMemcpyDeviceToHost, stream_));
+      CK(cudaMemcpyAsync(tr + 2 * th, h_, th * 4, cudaMemcpyDeviceToHost, stream_));
+    }
   }
+}
+
+void Model::forward_trace(const int64_t* ids, size_t T, float* logits, float* trace) {
+  CK(cudaSetDevice(device_));
+  if (T == 0) throw std::invalid_argument("forward: empty input");
+  for (size_t t = 0; t < T; ++t)
+    if (ids[t] < 0 || ids[t] >= V_) throw std::out_of_range("token id outside [0, vocab_size)");
+  ensure_ws(T);
+  CK(cudaMemcpyAsync(ids_, ids, T * 8, cudaMemcpyHostToDevice, stream_));
+  CK(launch_embed(h_, emb_, ids_, static_cast<int>(T), H_, V_, err_, stream_));
+  CK(cudaMemcpyAsync(trace, h_, T * H_ * 4, cudaMemcpyDeviceToHost, stream_));
+  trace_ = trace;
+  try {
+    layers(1, static_cast<int>(T), static_cast<int>(T), [](int) { return static_cast<float*>(nullptr); });
+  } catch (...) {
+    trace_ = nullptr;
+    throw;
+  }
+  trace_ = nullptr;
+  head(h_, static_cast<int>(T));
+  CK(cudaMemcpyAsync(logits, logits_, T * V_ * 4, cudaMemcpyDeviceToHost, stream_));
+  CK(cudaStreamSynchronize(stream_));
+  check_errors();
 }
 
 void Model::head(const float* rows, int M) {
@@ -436,7 +468,9 @@ std::vector<Model::ClassStats> Model::serve_profile(size_t steps) {
   }
   marks_.clear();
   pinned(static_cast<size_t>(stride) * B);
-  CK(cudaMemcpy(pinned_, loop_ids_, static_cast<size_t>(stride) * B * 8, cudaMemcpyDeviceToHost));
+  CK(cudaMemcpyAsync(pinned_, loop_ids_, static_cast<size_t>(stride) * B * 8, cudaMemcpyDeviceToHost,
+                     stream_));
+  CK(cudaStreamSynchronize(stream_));
   for (int b = 0; b < B; ++b) serve_last_[b] = pinned_[static_cast<size_t>(b) * stride + steps];
   check_errors();
   return out;

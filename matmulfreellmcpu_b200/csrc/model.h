@@ -44,6 +44,10 @@ class Model {
                                 const Sampling& samp);
   // model.hpp:34 / hgrn_model.cpp:239-247: logits [T, V] (host), or only the last row.
   void forward(const int64_t* ids, size_t T, float* logits, bool last_row_only);
+  // forward plus a host trace of (1 + 3L) x [T, H]: embeddings, then per layer the
+  // recurrence output, the residual after o_proj and the layer output (debugging parity,
+  // like the reference's capture hooks, tools/reference.py:108-117).
+  void forward_trace(const int64_t* ids, size_t T, float* logits, float* trace);
   // model.hpp:52-70 / hgrn_model.cpp:349-454.
   std::vector<std::vector<int64_t>> generate_serve(const std::vector<std::vector<int64_t>>& prompts,
                                                    size_t new_tokens, int64_t eos_id,
@@ -146,6 +150,7 @@ class Model {
   int graph_b_ = 0;
   int64_t graph_stride_ = 0;
 
+  float* trace_ = nullptr;         // forward_trace destination (host), else nullptr
   bool prof_on_ = false;
   struct Mark { int cls; cudaEvent_t a, b; double bytes, ops; };
   std::vector<Mark> marks_;

@@ -87,7 +87,8 @@ class Oracle:
                                     C.c_int, C.c_int, VP]
         L.orc_hgrn_scan.argtypes = [F32P, F32P, F32P, SZ, SZ, VP]
         L.orc_rmsnorm_swishgate.argtypes = [F32P, F32P, F32P, F32P, SZ, SZ, C.c_float]
-        for n in ("orc_model_forward", "orc_model_generate", "orc_model_generate_serve"):
+        for n in ("orc_model_forward", "orc_model_generate", "orc_model_generate_serve",
+                  "orc_model_forward_trace"):
             getattr(L, n).restype = C.c_int
 
     # -- primitives
@@ -203,6 +204,18 @@ class OracleModel:
         if rc:
             raise ValueError("oracle forward rejected its input")
         return lg
+
+    def forward_trace(self, ids, act_quant=1, frac_bits=10):
+        """(logits [T,V], trace [1+3L, T, H]: embeddings, then per layer recur/resid/h)."""
+        ids = np.ascontiguousarray(ids, np.int64)
+        lg = np.empty((ids.size, self.V), np.float32)
+        tr = np.empty((1 + 3 * self.L, ids.size, self.H), np.float32)
+        rc = self.o.lib.orc_model_forward_trace(C.byref(self.s), act_quant, frac_bits,
+                                                ids.ctypes.data_as(VP), ids.size,
+                                                lg.ctypes.data_as(VP), tr.ctypes.data_as(VP))
+        if rc:
+            raise ValueError("oracle forward rejected its input")
+        return lg, tr
 
     def generate(self, ids, gen, act_quant=1, frac_bits=10):
         """Returns (full id stream, last-step logits)."""

@@ -270,6 +270,9 @@ static void run_proj(const orc_proj* p, float* out, const float* x, size_t rows,
 }
 
 /* hgrn_model.cpp:80-195. stream_state: the T rows are T streams, each one step. */
+/* optional per-layer trace: [recur, resid, h] x [t, H] per layer, after h0 = embeddings */
+static float* g_trace = NULL;
+
 static void block(const orc_model* m, scratch* s, float* h, size_t t, size_t l, float* rstate,
                   int stream_state, int aq, int frac) {
   const size_t H = m->hidden, I = m->inter, th = t * H;
@@ -306,6 +309,12 @@ static void block(const orc_model* m, scratch* s, float* h, size_t t, size_t l, 
   orc_swiglu(s->z, s->gate, s->yh, t * I);
   run_proj(&L->proj[ORC_DOWN], s->oout, s->z, t, eps, aq, frac);
   for (size_t n = 0; n < th; ++n) h[n] = s->resid[n] + s->oout[n];
+  if (g_trace) {
+    float* tr = g_trace + th + l * 3 * th;
+    memcpy(tr, s->recur, th * 4);
+    memcpy(tr + th, s->resid, th * 4);
+    memcpy(tr + 2 * th, h, th * 4);
+  }
 }
 
 static void embed(const orc_model* m, float* h, const int64_t* ids, size_t t) {
@@ -348,6 +357,19 @@ int orc_model_forward(const orc_model* m, int aq, int frac, const int64_t* ids, 
   free(h);
   scratch_free(&s);
   return 0;
+}
+
+/* orc_model_forward plus trace (1 + 3L) x [t, H]: embeddings, then per layer the
+ * recurrence output, the residual after o_proj and the layer output. */
+int orc_model_forward_trace(const orc_model* m, int aq, int frac, const int64_t* ids, size_t t,
+                            float* logits, float* trace) {
+  if (t == 0 || check_ids(m, ids, t)) return -1;
+  for (size_t r = 0; r < t; ++r)
+    memcpy(trace + r * m->hidden, m->embeddings + (size_t)ids[r] * m->hidden, m->hidden * 4);
+  g_trace = trace;
+  int rc = orc_model_forward(m, aq, frac, ids, t, logits);
+  g_trace = NULL;
+  return rc;
 }
 
 /* hgrn_model.cpp:249-347 (greedy, no EOS). */

@@ -68,6 +68,8 @@ typedef struct {
 /* Full-prefix forward from zero state; logits [T, V]. */
 int orc_model_forward(const orc_model* m, int act_quant, int frac_bits, const int64_t* ids,
                       size_t t, float* logits);
+int orc_model_forward_trace(const orc_model* m, int act_quant, int frac_bits, const int64_t* ids,
+                            size_t t, float* logits, float* trace);
 /* Greedy generate (prefill + decode with carried state); out holds n + gen ids. */
 int orc_model_generate(const orc_model* m, int act_quant, int frac_bits, const int64_t* ids,
                        size_t n, size_t gen, int64_t* out, float* last_logits);

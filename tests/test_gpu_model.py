@@ -54,6 +54,19 @@ def test_small_models_golden(models, name):
     assert np.array_equal(mf.generate(g["prompt"], 9), g["float_stream"])
 
 
+@pytest.mark.parametrize("name", ["small", "370M"])
+def test_layer_trace_matches_oracle(models, orc, blob_cache, name):
+    """Every layer's recurrence output, residual and output, bit for bit (fixed mode)."""
+    om = orc.model(B.Blob.open(B.cached_blob(name, 0, blob_cache)))
+    ids = B.seeded_ids(9, 77, B.CONFIGS[name]["vocab_size"])
+    lg, tr = models(name, "fixed").forward_trace(ids)
+    olg, otr = om.forward_trace(ids, 1)
+    for i in range(tr.shape[0]):
+        layer, what = (i - 1) // 3, ("recur", "resid", "h")[(i - 1) % 3] if i else "embed"
+        assert bits_equal(tr[i], otr[i]), f"layer {layer} {what} differs"
+    assert bits_equal(lg, olg)
+
+
 def test_serve_identical_prompts_match_generate(models):
     """model.hpp:58-59: B identical prompts + greedy give identical streams = generate()."""
     m = models("small", "fixed")
