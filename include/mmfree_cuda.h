@@ -71,6 +71,37 @@ int mmfree_cuda_bitlinear(float* out, const float* x, const float* norm_weight,
                           size_t out_dim, float eps, float* norm_out, int act_quant,
                           int frac_bits, int32_t* acc_out, void* stream);
 
+/* Size of the static device scratch used by mmfree_cuda_bitlinear_noalloc (4 MiB). */
+#define MMFREE_CUDA_NOALLOC_SCRATCH_BYTES (4u << 20)
+
+/* mmfree_cuda_bitlinear for callers that cannot allocate device memory. It has no
+ * counterpart in the reference (whose CPU kernels keep their scratch in static host
+ * buffers, bitlinear.cpp:49-53).
+ *
+ * Who needs it: code that runs where cudaMalloc is unavailable or forbidden -- a plugin
+ * inside a host process whose allocator owns the whole device (a serving framework's
+ * memory pool, a pre-partitioned GPU), a latency-critical decode loop that must never
+ * block on an allocation, or work issued while a stream is being captured into a CUDA
+ * graph, where cudaMalloc is not a legal call. mmfree_cuda_bitlinear grows a library-owned
+ * scratch arena with cudaMalloc on first use of a larger shape; this variant instead uses
+ * a fixed array compiled into the library (one per device that loads it, held until the
+ * process exits) and calls no allocating routine on its success path.
+ *
+ * Same arguments, semantics and results as mmfree_cuda_bitlinear. Limits and rules:
+ *   - scratch need: FixedQ510 2*rows*ceil64(in_dim) + 4*rows bytes, Float
+ *     4*rows*ceil64(in_dim) bytes (each rounded up to 256); a call needing more than
+ *     MMFREE_CUDA_NOALLOC_SCRATCH_BYTES fails with MMFREE_E_INVALID and allocates nothing;
+ *   - the first call on a device looks up that device's copy of the array
+ *     (cudaGetSymbolAddress, which can load the module): make it before any stream capture;
+ *   - every call on a device shares the one array, which keeps the last call's contents;
+ *     nothing in it has to start at zero (each call writes all it reads), but calls whose
+ *     kernels overlap on the GPU (different streams, or different host threads) race on it.
+ */
+int mmfree_cuda_bitlinear_noalloc(float* out, const float* x, const float* norm_weight,
+                                  const void* wpacked, float scale_w, size_t rows,
+                                  size_t in_dim, size_t out_dim, float eps, float* norm_out,
+                                  int act_quant, int frac_bits, int32_t* acc_out, void* stream);
+
 /* Replaces mmfree::bitlinear_cluster (kernels.hpp:50-53, bitlinear.cpp:119-159): k <= 3
  * FixedQ510 projections sharing x, each with its own norm weight, packed weight, scale and
  * output. outs / norm_weights / wpacked are HOST arrays of k device pointers, scale_w a

@@ -27,6 +27,7 @@ SIGNATURES = {
     "mmfree_cuda_repack_ternary": (I, [VP, VP, SZ, SZ, VP]),
     "mmfree_cuda_pack_ternary_host": (I, [VP, VP, SZ, SZ]),
     "mmfree_cuda_bitlinear": (I, [VP, VP, VP, VP, F, SZ, SZ, SZ, F, VP, I, I, VP, VP]),
+    "mmfree_cuda_bitlinear_noalloc": (I, [VP, VP, VP, VP, F, SZ, SZ, SZ, F, VP, I, I, VP, VP]),
     "mmfree_cuda_bitlinear_cluster": (I, [VP, VP, VP, VP, VP, I, SZ, SZ, SZ, F, I, VP, VP]),
     "mmfree_cuda_ternary_matmul": (I, [VP, VP, VP, SZ, SZ, SZ, VP]),
     "mmfree_cuda_rmsnorm": (I, [VP, VP, VP, SZ, SZ, F, VP]),

@@ -233,6 +233,80 @@ int mmfree_cuda_bitlinear(float* out, const float* x, const float* norm_weight,
   });
 }
 
+// ---- allocation-free BitLinear -------------------------------------------------------------
+// Scratch compiled into the library: each device that loads this module holds one copy until
+// the process exits. Host code must not use the symbol as an address (it names a host-side
+// stand-in); the device address comes from cudaGetSymbolAddress, looked up once per device
+// with that device current.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[MMFREE_CUDA_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+std::once_flag g_noalloc_once[64];
+cudaError_t g_noalloc_status[64];
+char* g_noalloc_addr[64];
+}  // namespace
+
+int mmfree_cuda_bitlinear_noalloc(float* out, const float* x, const float* norm_weight,
+                                  const void* wpacked, float scale_w, size_t rows,
+                                  size_t in_dim, size_t out_dim, float eps, float* norm_out,
+                                  int act_quant, int frac_bits, int32_t* acc_out, void* stream) {
+  return guard([&] {
+    need(act_quant == MMFREE_ACT_FLOAT || act_quant == MMFREE_ACT_FIXED_Q510, "bad act_quant");
+    check_dims(rows, in_dim, out_dim);
+    need(frac_bits >= 0 && frac_bits <= 30, "frac_bits must be in [0, 30]");
+    need(out && x && norm_weight && wpacked, "null output, input, norm weight or weights");
+    if (rows == 0) return;
+    const bool fixed = act_quant == MMFREE_ACT_FIXED_Q510;
+    const size_t kp = static_cast<size_t>(padded_k(static_cast<int64_t>(in_dim)));
+    const size_t planes_bytes = fixed ? a256(2 * rows * kp) : a256(rows * kp * 4);
+    const size_t need_bytes = planes_bytes + (fixed ? a256(rows * 4) : 0);
+    need(need_bytes <= MMFREE_CUDA_NOALLOC_SCRATCH_BYTES,
+         "bitlinear_noalloc: rows x in_dim needs more scratch than "
+         "MMFREE_CUDA_NOALLOC_SCRATCH_BYTES (use mmfree_cuda_bitlinear or fewer rows per call)");
+    int dev = 0;
+    ck(cudaGetDevice(&dev), "cudaGetDevice");
+    need(dev >= 0 && dev < 64, "device index above 63");
+    std::call_once(g_noalloc_once[dev], [dev] {
+      g_noalloc_status[dev] =
+          cudaGetSymbolAddress(reinterpret_cast<void**>(&g_noalloc_addr[dev]), g_noalloc_scratch);
+    });
+    ck(g_noalloc_status[dev], "cudaGetSymbolAddress(noalloc scratch)");
+    char* base = g_noalloc_addr[dev];
+    cudaStream_t st = as_stream(stream);
+    PrepArgs p;
+    p.x = x;
+    p.nproj = 1;
+    p.normw[0] = norm_weight;
+    p.norm_out = norm_out;
+    p.M = static_cast<int>(rows);
+    p.K = static_cast<int>(in_dim);
+    p.eps = eps;
+    p.qs = static_cast<float>(1u << frac_bits);
+    p.fixed = fixed;
+    if (fixed) {
+      p.planes[0] = reinterpret_cast<int8_t*>(base);
+      p.rowsum[0] = reinterpret_cast<int32_t*>(base + planes_bytes);
+    } else {
+      p.yf[0] = reinterpret_cast<float*>(base);
+    }
+    ck(launch_prep(p, st), "prep kernel");
+    MatmulArgs a;
+    a.w = wpacked;
+    a.planes = p.planes[0];
+    a.rowsum = p.rowsum[0];
+    a.yf = p.yf[0];
+    a.M = static_cast<int>(rows);
+    a.N = static_cast<int>(out_dim);
+    a.K = static_cast<int>(in_dim);
+    a.scale = fixed ? 1.0f / (p.qs * scale_w) : 1.0f / scale_w;
+    a.out = out;
+    a.ldo = static_cast<int>(out_dim);
+    a.acc_out = fixed ? acc_out : nullptr;
+    a.fixed = fixed;
+    ck(launch_matmul(a, st), "matmul kernel");
+  });
+}
+
 int mmfree_cuda_bitlinear_cluster(float* const* outs, const float* x,
                                   const float* const* norm_weights,
                                   const void* const* wpacked, const float* scale_w, int k,
