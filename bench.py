@@ -214,10 +214,12 @@ def run_ours(a, rank, world, local):
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(local) as clk:
+        torch.cuda.nvtx.range_push("timed")  # lets ncu --nvtx-include "timed/" capture it
         ev0.record(stream)
         model.serve_run(K)
         ev1.record(stream)
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
     barrier(world)
     ms = allmax(ev0.elapsed_time(ev1), world)
     value = N_STREAMS * K / (ms / 1e3)
@@ -254,7 +256,8 @@ def run_ours(a, rank, world, local):
 
     # b = 1 decode (configuration 2 shape: 128-id prompt, 255 decode steps), rank 0
     b1 = None
-    if rank == 0:
+    b1_steps = max(1, min(a.b1_steps, B1_GEN - 1))
+    if rank == 0 and a.b1_steps > 0:
         from matmulfreellmcpu_b200.blob import seeded_ids
         model.serve_begin([seeded_ids(B1_PROMPT, 0)])
         model.serve_run(3)
@@ -263,14 +266,14 @@ def run_ours(a, rank, world, local):
         torch.cuda.synchronize()
         f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         f0.record(stream)
-        model.serve_run(B1_GEN - 1)
+        model.serve_run(b1_steps)
         f1.record(stream)
         torch.cuda.synchronize()
         b1_ms = f0.elapsed_time(f1)
         prof1 = model.serve_profile(8)
         model.serve_end()
-        b1 = {"decode_tok_s": (B1_GEN - 1) / (b1_ms / 1e3), "steps": B1_GEN - 1,
-              "ms_per_token": b1_ms / (B1_GEN - 1),
+        b1 = {"decode_tok_s": b1_steps / (b1_ms / 1e3), "steps": b1_steps,
+              "ms_per_token": b1_ms / b1_steps,
               "kernel_ms_per_token": {k: v["ms"] / 8 for k, v in prof1.items()}}
         mm = prof1["bitlinear_matmul"]
         b1["bitlinear_hbm_gbs"] = mm["bytes"] / (mm["ms"] / 1e3) / 1e9 if mm["ms"] else None
@@ -331,15 +334,77 @@ def run_ours(a, rank, world, local):
     model.close()
 
 
+SWEEP_M = (1, 16, 64, 512, 4096)
+SWEEP_KN = ((1024, 1024), (1024, 5632), (2048, 2048), (2048, 11264), (5632, 2048),
+            (2560, 13824), (6912, 2560))
+
+
+def run_op(a):
+    """Configuration 1: the isolated BitLinear op (mmfree_cuda_bitlinear) per (M, K, N).
+    Inputs as in the config (N(0,1) activations with 1% x20 outliers, ternary p=(.3,.4,.3),
+    scale 20); weights rotate over enough packed copies to exceed L2 (>= 512 MB), so every
+    timed call streams its weights from HBM. One JSON line per shape."""
+    import torch
+
+    from matmulfreellmcpu_b200 import api
+    peaks, src = load_peaks()
+    dev = torch.device("cuda", 0)
+    shapes = []
+    if a.op == "sweep":
+        shapes = [(m, k, n) for (k, n) in SWEEP_KN for m in SWEEP_M]
+    else:
+        shapes = [tuple(int(v) for v in a.op.split(","))]
+    for M, K, N in shapes:
+        rng = np.random.default_rng(M + K + N)
+        x = rng.standard_normal((M, K)).astype(np.float32)
+        x[rng.random((M, K)) < 0.01] *= np.float32(20.0)
+        wq = torch.from_numpy(rng.choice(np.array([-1, 0, 1], np.int8), size=(N, K),
+                                         p=[0.3, 0.4, 0.3])).to(dev)
+        wp0 = api.repack_ternary(wq)
+        copies = max(1, -(-(512 << 20) // wp0.numel()))
+        wps = [wp0] + [wp0.clone() for _ in range(copies - 1)]
+        xd = torch.from_numpy(x).to(dev)
+        nw = torch.ones(K, device=dev)
+        s = torch.cuda.current_stream()
+        for i in range(3):
+            api.bitlinear(xd, nw, wps[i % copies], 20.0, N, act_quant=a.mode)
+        reps = max(1, a.op_reps)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for i in range(reps):
+            api.bitlinear(xd, nw, wps[i % copies], 20.0, N, act_quant=a.mode)
+        e1.record(s)
+        torch.cuda.synchronize()
+        us = 1e3 * e0.elapsed_time(e1) / reps
+        byts = K * N / 4 + 4 * K + 4 * M * K + 4 * M * N + 4
+        ops = 2.0 * M * K * N
+        gbs = byts / us / 1e3
+        print(json.dumps({"metric": "BitLinear op (config 1)", "M": M, "K": K, "N": N,
+                          "mode": a.mode, "us_per_call": us, "hbm_gbs": gbs,
+                          "hbm_frac": gbs / float(peaks["hbm_gbs"]), "tops": ops / us / 1e6,
+                          "weight_copies": copies, "reps": reps, "peak_source": src}),
+              flush=True)
+        del wps, wp0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--op", default=None,
+                    help="configuration 1 instead: 'sweep' or 'M,K,N' (isolated BitLinear)")
+    ap.add_argument("--op-reps", type=int, default=50)
     ap.add_argument("--steps", type=int, default=500)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--mode", choices=["fixed", "float"], default="fixed")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--b1-steps", type=int, default=B1_GEN - 1,
+                    help="decode steps of the b=1 figure (0 skips it)")
     a = ap.parse_args()
+    if a.op:
+        run_op(a)
+        return
     if a.impl == "reference":
         # rank 0 alone times the CPU reference; the other ranks exit without work
         rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))

@@ -66,6 +66,7 @@ enum : uint32_t {
   kErrBadToken = 1u,     // a token id outside [0, vocab)
   kErrNotTernary = 2u,   // a weight outside {-1, 0, +1} given to the repack kernel
   kErrRange = 4u,        // an activation code outside int16 given to the ternary matmul
+  kErrTimeout = 8u,      // a bounded wait inside a kernel gave up
 };
 
 // Epilogue selectors of the BitLinear matmul kernels.

@@ -22,7 +22,7 @@ namespace mmfree_cuda {
 namespace {
 constexpr int kPrepThreads = 256;
 constexpr int kMatmulThreads = 128;
-constexpr int kMaxDynSmem = 227 * 1024;
+constexpr int kMaxDynSmem = 224 * 1024;  // below the 227 KB opt-in, leaving room for static smem
 }  // namespace
 
 // ------------------------------------------------------------------------------ repack
@@ -326,8 +326,24 @@ static cudaError_t launch_matmul_mt(const MatmulArgs& a, cudaStream_t s) {
   return cudaGetLastError();
 }
 
+static int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int& c = cached[dev & 63];
+  if (c == 0) cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev);
+  return c > 0 ? c : 148;
+}
+
 cudaError_t launch_matmul(const MatmulArgs& a, cudaStream_t s) {
   if (a.M <= 0 || a.N <= 0) return cudaSuccess;
+  if (a.fixed && a.allow_tc && a.M >= kTcMinRows) {
+    int splits = tc_splits(a, sm_count());
+    if (splits > 1 && (!a.tc_accum || a.tc_accum_words < static_cast<size_t>(a.M) * a.N ||
+                       !a.tc_tiles || a.tc_tiles_words < static_cast<size_t>(tc_tile_count(a.M, a.N))))
+      splits = 1;
+    return launch_matmul_tc(a, a.tc_accum, a.tc_tiles, splits, a.err, s);
+  }
   if (a.M == 1) return launch_matmul_mt<1>(a, s);
   if (a.M == 2) return launch_matmul_mt<2>(a, s);
   if (a.M <= 4) return launch_matmul_mt<4>(a, s);

@@ -44,7 +44,65 @@ struct MatmulArgs {
   int ldr = 0;
   int32_t* acc_out = nullptr;     // optional [M, N] raw int32 accumulators (fixed)
   bool fixed = true;
+  // tensor-core path (FixedQ510, M >= kTcMinRows): opt-in, plus an optional split-K
+  // workspace (zeroed once; every launch leaves it zeroed) and a device error word
+  bool allow_tc = false;
+  uint32_t* tc_accum = nullptr;   // >= M*N words for split-K
+  size_t tc_accum_words = 0;
+  uint32_t* tc_tiles = nullptr;   // one counter per output tile
+  size_t tc_tiles_words = 0;
+  uint32_t* err = nullptr;
 };
+
+constexpr int kTcMinRows = 16;
+
+// ---- fused few-row decode kernels (decode.cu)
+enum DecPro : int {
+  kDecProNorm2 = 0,  // rmsnorm(x) * prew, then each projection's BitLinear norm
+  kDecProSwish = 1,  // rmsnorm(x) * prew * silu(o), then the BitLinear norm
+  kDecProPlain = 2,  // the BitLinear norm of x
+};
+enum DecEpi : int {
+  kDecEpiMixer = 0,   // i/f/g -> gate, lower bound, scan input, one recurrence step
+  kDecEpiResid = 1,   // out = resid + dequant
+  kDecEpiSwiglu = 2,  // gate_proj: out[c] = silu(y[c]) * y[I + c]
+  kDecEpiLogits = 3,  // lm_head logits, greedy argmax into ids[t*stride + *pos + 1]
+};
+constexpr int kDecMaxRows = 4;
+
+struct DecArgs {
+  const float* x = nullptr;       // [M, K]
+  const float* o = nullptr;       // [M, K] recurrence output (kDecProSwish)
+  const float* prew = nullptr;    // [K] first norm weight
+  const float* normw[3] = {};     // projection norm weights [K]
+  const void* w[3] = {};          // packed weights (N x K each)
+  float scale[3] = {1.0f, 1.0f, 1.0f};
+  int M = 0, K = 0, N = 0;
+  float eps = 1e-6f, qs = 1024.0f;
+  float* out[2] = {};             // mixer: recurrence, g; resid/swiglu/logits: out[0]
+  const float* resid = nullptr;   // [M, N]
+  float* state = nullptr;         // [M, N] recurrent state (mixer)
+  const float* lb = nullptr;      // [N] lower bound or nullptr (mixer)
+  int64_t seg = 1;                // element count of one reference vector call (tails)
+  int64_t* ids = nullptr;         // logits: token ids [M][stride], position *pos
+  int64_t stride = 0;
+  int64_t* pos = nullptr;
+  unsigned* done = nullptr;
+  float* part_v = nullptr;        // logits: per-CTA partial maxima [grid][kDecMaxRows]
+  int* part_i = nullptr;
+};
+int dec_units(const DecArgs& a, int epi);
+cudaError_t launch_dec(const DecArgs& a, int pro, int epi, int grid, cudaStream_t s, bool pdl);
+
+// tcgen05 BitLinear matmul (tc_matmul.cu)
+int tc_token_tile(int M);
+int tc_splits(const MatmulArgs& a, int sm_count);
+cudaError_t launch_matmul_tc(const MatmulArgs& a, uint32_t* accum, uint32_t* tiles, int splits,
+                             uint32_t* err, cudaStream_t s);
+// output tiles of the tcgen05 path (split-K counters needed)
+inline int64_t tc_tile_count(int M, int N) {
+  return ((N + 127) / 128) * static_cast<int64_t>((M + tc_token_tile(M) - 1) / tc_token_tile(M));
+}
 
 // int8 ternary [n, k] (nn.Linear layout) -> tiled 2-bit format; entries outside {-1,0,1}
 // set bit 2 (kErrNotTernary) of *err (nullable) and are packed by sign.

@@ -11,6 +11,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <numeric>
 #include <stdexcept>
@@ -50,6 +51,13 @@ Model::Model(const std::string& blob_path, int device, bool fixed, int frac_bits
   if (padded_k(std::max(H_, I_)) * 4 > 227 * 1024)
     throw std::runtime_error("hidden/intermediate size too large for the prep kernel");
   CK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+  CK(cudaDeviceGetAttribute(&sms_, cudaDevAttrMultiProcessorCount, device));
+  {
+    const char* env = std::getenv("MMFREE_FUSED_DECODE");
+    fused_ok_ = !(env && env[0] == '0');
+  }
+  CK(cudaMalloc(&dec_part_v_, sizeof(float) * kDecMaxRows * 2 * 1024));
+  CK(cudaMalloc(&dec_part_i_, sizeof(int) * kDecMaxRows * 2 * 1024));
   CK(cudaMalloc(&err_, 64));
   CK(cudaMemsetAsync(err_, 0, 64, stream_));
   pos_ = reinterpret_cast<int64_t*>(reinterpret_cast<char*>(err_) + 8);
@@ -165,6 +173,8 @@ Model::~Model() {
   cudaFree(state_);
   cudaFree(loop_ids_);
   cudaFree(err_);
+  cudaFree(dec_part_v_);
+  cudaFree(dec_part_i_);
   if (pinned_) cudaFreeHost(pinned_);
   if (stream_) cudaStreamDestroy(stream_);
 }
@@ -190,6 +200,12 @@ void Model::ensure_ws(size_t rows) {
          o_fb = carve(rows * H * 4), o_gb = carve(rows * H * 4), o_recur = carve(rows * H * 4),
          o_y = carve(rows * 2 * I * 4), o_z = carve(rows * I * 4), o_lg = carve(rows * V * 4),
          o_hl = carve(rows * H * 4), o_ids = carve(rows * 8);
+  // split-K workspace of the tensor-core matmul (decode-sized row counts)
+  const size_t maxn = std::max({V, 2 * I, H});
+  const size_t acc_rows = std::min<size_t>(rows, 512);
+  tc_accum_words_ = fixed_ ? acc_rows * maxn : 0;
+  tc_tiles_words_ = fixed_ ? static_cast<size_t>(tc_tile_count(static_cast<int>(rows), static_cast<int>(maxn))) : 0;
+  const size_t o_acc = carve(tc_accum_words_ * 4), o_tiles = carve(tc_tiles_words_ * 4);
   size_t o_pl[3], o_rs[3], o_yf[3];
   for (int j = 0; j < 3; ++j) {
     o_pl[j] = fixed_ ? carve(2 * rows * Kp) : 0;
@@ -209,6 +225,9 @@ void Model::ensure_ws(size_t rows) {
   logits_ = reinterpret_cast<float*>(b + o_lg);
   hl_ = reinterpret_cast<float*>(b + o_hl);
   ids_ = reinterpret_cast<int64_t*>(b + o_ids);
+  tc_accum_ = reinterpret_cast<uint32_t*>(b + o_acc);
+  tc_tiles_ = reinterpret_cast<uint32_t*>(b + o_tiles);
+  CK(cudaMemsetAsync(b + o_acc, 0, o_tiles + tc_tiles_words_ * 4 - o_acc, stream_));
   for (int j = 0; j < 3; ++j) {
     planes_[j] = fixed_ ? reinterpret_cast<int8_t*>(b + o_pl[j]) : nullptr;
     rowsum_[j] = reinterpret_cast<int32_t*>(b + o_rs[j]);
@@ -313,6 +332,12 @@ void Model::bitlinear(const Proj& p, int plane, float* out, int M, const float* 
   a.resid = resid;
   a.ldr = p.out;
   a.fixed = fixed_;
+  a.allow_tc = true;
+  a.tc_accum = tc_accum_;
+  a.tc_accum_words = tc_accum_words_;
+  a.tc_tiles = tc_tiles_;
+  a.tc_tiles_words = tc_tiles_words_;
+  a.err = err_;
   // algorithmic bytes (2-bit weights, activations in, outputs out) and 2*M*K*N ops
   const double K = p.in, N = p.out;
   const double bytes = K * N / 4 + 4.0 * M * K + 4.0 * M * N * (resid ? 2 : 1);
@@ -428,11 +453,107 @@ void Model::decode_graph_step(int B, int64_t stride) {
   timed(kClsEmbed, 8.0 * B * H_, 0, [&] {
     CK(launch_embed_at(h_, emb_, loop_ids_, stride, pos_, B, H_, V_, err_, stream_));
   });
+  if (fused_decode(B)) {
+    fused_step(B, stride);
+    return;
+  }
   layers(B, 1, B, [&](int l) { return state_ + static_cast<size_t>(l) * B * H_; });
   head(h_, B);
   timed(kClsArgmax, 4.0 * B * V_, 0, [&] {
     CK(launch_argmax_at(loop_ids_, stride, pos_, done_, logits_, B, V_, V_, stream_));
   });
+}
+
+bool Model::fused_decode(int B) const {
+  return fixed_ && fused_ok_ && B <= kDecMaxRows && I_ % 32 == 0;
+}
+
+// One decode step of B <= 4 streams with the fused kernels of decode.cu: four launches per
+// layer plus the head, each launched as a programmatic dependent of the previous one.
+void Model::fused_step(int B, int64_t stride) {
+  auto dec = [&](DecArgs& a, int pro, int epi, int cls, double wbytes) {
+    const int units = dec_units(a, epi);
+    const int grid = std::max(1, std::min(units, 2 * sms_));
+    a.M = B;
+    a.eps = eps_;
+    a.qs = qs_;
+    const double bytes = wbytes + 4.0 * B * a.K * (pro == kDecProSwish ? 2 : 1) + 4.0 * B * a.N;
+    const double ops = 2.0 * B * a.K * a.N * (epi == kDecEpiMixer ? 3 : 1);
+    timed(cls, bytes, ops, [&] { CK(launch_dec(a, pro, epi, grid, stream_, true)); });
+  };
+  auto wb = [](const Proj& p) { return static_cast<double>(packed_bytes(p.out, p.in)); };
+  const size_t BH = static_cast<size_t>(B) * H_;
+  for (int l = 0; l < L_; ++l) {
+    const Layer& ly = layers_[l];
+    DecArgs k1;
+    k1.x = h_;
+    k1.prew = ly.attn_norm;
+    for (int j = 0; j < 3; ++j) {
+      k1.normw[j] = ly.p[j].normw;
+      k1.w[j] = ly.p[j].w;
+      k1.scale[j] = 1.0f / (qs_ * ly.p[j].scale_w);
+    }
+    k1.K = H_;
+    k1.N = H_;
+    k1.out[0] = recur_;
+    k1.out[1] = gb_;
+    k1.state = state_ + static_cast<size_t>(l) * BH;
+    k1.lb = ly.lb;
+    k1.seg = static_cast<int64_t>(BH);
+    dec(k1, kDecProNorm2, kDecEpiMixer, kClsMatmul, wb(ly.p[kI]) + wb(ly.p[kF]) + wb(ly.p[kG]));
+
+    DecArgs k2;
+    k2.x = gb_;
+    k2.o = recur_;
+    k2.prew = ly.g_norm;
+    k2.normw[0] = ly.p[kO].normw;
+    k2.w[0] = ly.p[kO].w;
+    k2.scale[0] = 1.0f / (qs_ * ly.p[kO].scale_w);
+    k2.K = H_;
+    k2.N = H_;
+    k2.out[0] = resid_;
+    k2.resid = h_;
+    dec(k2, kDecProSwish, kDecEpiResid, kClsMatmul, wb(ly.p[kO]));
+
+    DecArgs k3;
+    k3.x = resid_;
+    k3.prew = ly.mlp_norm;
+    k3.normw[0] = ly.p[kGate].normw;
+    k3.w[0] = ly.p[kGate].w;
+    k3.scale[0] = 1.0f / (qs_ * ly.p[kGate].scale_w);
+    k3.K = H_;
+    k3.N = 2 * I_;
+    k3.out[0] = z_;
+    k3.seg = static_cast<int64_t>(B) * I_;
+    dec(k3, kDecProNorm2, kDecEpiSwiglu, kClsMatmul, wb(ly.p[kGate]));
+
+    DecArgs k4;
+    k4.x = z_;
+    k4.normw[0] = ly.p[kDown].normw;
+    k4.w[0] = ly.p[kDown].w;
+    k4.scale[0] = 1.0f / (qs_ * ly.p[kDown].scale_w);
+    k4.K = I_;
+    k4.N = H_;
+    k4.out[0] = h_;
+    k4.resid = resid_;
+    dec(k4, kDecProPlain, kDecEpiResid, kClsMatmul, wb(ly.p[kDown]));
+  }
+  DecArgs hd;
+  hd.x = h_;
+  hd.prew = final_norm_;
+  hd.normw[0] = lm_head_.normw;
+  hd.w[0] = lm_head_.w;
+  hd.scale[0] = 1.0f / (qs_ * lm_head_.scale_w);
+  hd.K = H_;
+  hd.N = V_;
+  hd.out[0] = logits_;
+  hd.ids = loop_ids_;
+  hd.stride = stride;
+  hd.pos = pos_;
+  hd.done = done_;
+  hd.part_v = dec_part_v_;
+  hd.part_i = dec_part_i_;
+  dec(hd, kDecProNorm2, kDecEpiLogits, kClsLmHead, wb(lm_head_));
 }
 
 std::vector<Model::ClassStats> Model::serve_profile(size_t steps) {

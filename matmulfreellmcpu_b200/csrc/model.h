@@ -107,6 +107,12 @@ class Model {
   void head(const float* rows, int M);  // final norm + lm_head into logits_
   void check_errors();
   void decode_graph_step(int B, int64_t stride);  // embed_at, layers (streams), head, argmax_at
+  bool fused_decode(int B) const;                 // use the fused kernels of decode.cu?
+  void fused_step(int B, int64_t stride);
+  int sms_ = 148;
+  bool fused_ok_ = true;           // MMFREE_FUSED_DECODE=0 selects the unfused decode step
+  float* dec_part_v_ = nullptr;    // fused head: per-CTA argmax partials
+  int* dec_part_i_ = nullptr;
 
   BlobConfig cfg_;
   int device_ = 0;
@@ -134,6 +140,9 @@ class Model {
   int32_t* rowsum_[3] = {};
   float* yf_[3] = {};
   int64_t* ids_ = nullptr;
+  uint32_t* tc_accum_ = nullptr;   // split-K partial sums (kept zero between launches)
+  uint32_t* tc_tiles_ = nullptr;
+  size_t tc_accum_words_ = 0, tc_tiles_words_ = 0;
 
   // state and decode loop
   float* state_ = nullptr;

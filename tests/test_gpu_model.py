@@ -67,6 +67,30 @@ def test_layer_trace_matches_oracle(models, orc, blob_cache, name):
     assert bits_equal(lg, olg)
 
 
+def test_fused_and_unfused_decode_agree(cuda, blob_cache, monkeypatch):
+    """The fused few-row decode kernels (<= 4 streams) and the general per-op path give
+    identical ids (both are bit-exact restatements)."""
+    path = B.cached_blob("small", 0, blob_cache)
+    prompts = [B.seeded_ids(6, 500 + k, 2048) for k in range(3)]
+    out = {}
+    for flag in ("0", "1"):
+        monkeypatch.setenv("MMFREE_FUSED_DECODE", flag)
+        with api.Model(path, "fixed") as m:
+            out[flag] = (m.generate(prompts[0], 10), m.generate_serve(prompts, 7))
+    assert np.array_equal(out["0"][0], out["1"][0])
+    for a, b in zip(out["0"][1], out["1"][1]):
+        assert np.array_equal(a, b)
+
+
+def test_serve_many_streams_matches_oracle(models, orc, blob_cache):
+    """20 lockstep streams: decode rows go through the tensor-core matmul (ragged tile)."""
+    m = models("small", "fixed")
+    om = orc.model(B.Blob.open(B.cached_blob("small", 0, blob_cache)))
+    prompts = [B.seeded_ids(5, 900 + k, 2048) for k in range(20)]
+    for a, b in zip(m.generate_serve(prompts, 5), om.generate_serve(prompts, 5)):
+        assert np.array_equal(a, b)
+
+
 def test_serve_identical_prompts_match_generate(models):
     """model.hpp:58-59: B identical prompts + greedy give identical streams = generate()."""
     m = models("small", "fixed")
