@@ -265,10 +265,12 @@ def run_ours(a, rank, world, local):
         model.serve_begin([seeded_ids(B1_PROMPT, 0)])
         torch.cuda.synchronize()
         f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.nvtx.range_push("b1")
         f0.record(stream)
         model.serve_run(b1_steps)
         f1.record(stream)
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
         b1_ms = f0.elapsed_time(f1)
         prof1 = model.serve_profile(8)
         model.serve_end()

@@ -17,10 +17,11 @@
 // grid-wide synchronisation is needed. The arithmetic is that of exact.cuh / kernels.cu
 // (bit-identical to the reference in FixedQ510).
 //
-// Launches use programmatic dependent launch: a kernel first asks L2 to prefetch its weight
-// rows (one bulk prefetch per contiguous range), then waits for its predecessor
-// (griddepcontrol.wait) before reading activations, and lets its own dependent launch early
-// (griddepcontrol.launch_dependents). Weight streaming of layer l+1 thus overlaps layer l.
+// Launches use programmatic dependent launch. Everything a kernel needs that its
+// predecessor does not produce -- the weights of its first unit (into registers), its norm
+// weights (into shared memory), the lower bounds and recurrent state of its columns, an L2
+// prefetch of its other weights -- is fetched before griddepcontrol.wait, while the
+// predecessor still runs; after the wait only the activation rows are read.
 #include "common.cuh"
 #include "exact.cuh"
 #include "kernels.h"
@@ -44,20 +45,29 @@ __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
-// sum of squares of s[0..K) in the reference order, for the row handled by this 8-lane
-// group of warp 0 (all 32 lanes participate; every 8-lane group gets its own row's sum)
-__device__ __forceinline__ float chain8(const float* s, int K) {
-  const int j = threadIdx.x & 7;
-  const int n8 = K >> 3;
-  float acc = 0.0f;
-#pragma unroll 8
-  for (int i = 0; i < n8; ++i) {
-    const float v = s[8 * i + j];
-    acc = __fmaf_rn(v, v, acc);
-  }
-  float sum = hsum8_lanes(acc, 0xffffffffu);
-  for (int c = n8 * 8; c < K; ++c) sum = __fadd_rn(sum, __fmul_rn(s[c], s[c]));
-  return sum;
+constexpr uint32_t kStageSpin = 1u << 24;  // bounded wait for the staged weights
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+// bulk global -> shared copy completing on an mbarrier (no multicast)
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
 }
 
 }  // namespace
@@ -68,28 +78,65 @@ __global__ void __launch_bounds__(kDecThreads) dec_kernel(DecArgs a) {
   const int K = a.K, M = a.M, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t kc = packed_chunks(K), kp = kc * kChunkK;
   const int K4 = (K + 3) & ~3;
-  float* xs = reinterpret_cast<float*>(dsm);                                   // [MT][K4]
-  int8_t* pl = reinterpret_cast<int8_t*>(dsm + static_cast<size_t>(MT) * K4 * 4);  // [NP][MT][2][kp]
+  constexpr int kNorms = (PRO == kDecProPlain ? 0 : 1) + NP;  // prew + projection norms
+  float* xs = reinterpret_cast<float*>(dsm);                              // [MT][K4]
+  float* nws = xs + static_cast<size_t>(MT) * K4;                         // [kNorms][K4]
+  int8_t* pl = reinterpret_cast<int8_t*>(nws + static_cast<size_t>(kNorms) * K4);  // [NP][MT][2][kp]
   uint32_t* red = reinterpret_cast<uint32_t*>(pl + static_cast<size_t>(NP) * MT * 2 * kp);
   __shared__ float s_r[MT];
   __shared__ int s_rowsum[NP][MT];
-  __shared__ int s_red[kDecWarps];
 
-  // ---- units of this CTA: a 32-row group, or for SwiGLU the pair (g, g + I/32)
+  // units of this CTA: a 32-row group, or for SwiGLU the pair (g, g + I/32)
   const int ngroups = static_cast<int>(packed_groups(a.N));
   const int units = EPI == kDecEpiSwiglu ? ngroups / 2 : ngroups;
   const int half = ngroups / 2;  // SwiGLU: I/32 (the launcher requires I % 32 == 0)
+  auto wrow = [&](int u, int j) -> const uint4* {
+    const int g = EPI == kDecEpiSwiglu ? u + j * half : u;
+    const void* wj = EPI == kDecEpiSwiglu ? a.w[0] : a.w[j];
+    return static_cast<const uint4*>(wj) + static_cast<int64_t>(g) * kc * 32 + lane;
+  };
 
-  // ---- 1. warm L2 with this CTA's weights (independent of the predecessor kernel)
+  // ---- 1. independent of the predecessor: first-unit weights (bulk copy into shared memory),
+  //         L2 prefetch of the other units, norm weights, lower bounds and state
+  const int u0 = blockIdx.x;
+  const bool stage = a.stage && u0 < units;
+  uint4* wst = reinterpret_cast<uint4*>(red + kDecWarps * NW * MT * 32);  // [NW][kc][32] uint4
+  __shared__ __align__(8) uint64_t s_bar;
   if (tid == 0) {
     const uint32_t gbytes = static_cast<uint32_t>(kc * kChunkBytes);
-    for (int u = blockIdx.x; u < units; u += gridDim.x)
-      for (int j = 0; j < NW; ++j) {
-        const int g = EPI == kDecEpiSwiglu ? u + j * half : u;
-        const void* wj = EPI == kDecEpiSwiglu ? a.w[0] : a.w[j];
-        prefetch_l2(static_cast<const unsigned char*>(wj) + static_cast<int64_t>(g) * gbytes, gbytes);
-      }
+    if (stage) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&s_bar)));
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(&s_bar)),
+                   "r"(gbytes * NW)
+                   : "memory");
+      for (int j = 0; j < NW; ++j) bulk_g2s(wst + j * kc * 32, wrow(u0, j) - lane, gbytes, &s_bar);
+    } else if (u0 < units) {
+      for (int j = 0; j < NW; ++j) prefetch_l2(wrow(u0, j) - lane, gbytes);
+    }
+    for (int u = u0 + gridDim.x; u < units; u += gridDim.x)
+      for (int j = 0; j < NW; ++j) prefetch_l2(wrow(u, j) - lane, gbytes);
   }
+  {
+    int slot = 0;
+    if (PRO != kDecProPlain) {
+      for (int c = tid; c < K; c += kDecThreads) nws[c] = __ldg(a.prew + c);
+      slot = 1;
+    }
+    for (int j = 0; j < NP; ++j)
+      for (int c = tid; c < K; c += kDecThreads) nws[(slot + j) * K4 + c] = __ldg(a.normw[j] + c);
+  }
+  float lb_pre = 0.0f, st_pre[MT];
+  if (EPI == kDecEpiMixer && warp == 0 && u0 < units) {
+    const int n = u0 * 32 + lane;
+    if (n < a.N) {
+      if (a.lb) lb_pre = __ldg(a.lb + n);
+#pragma unroll
+      for (int t = 0; t < MT; ++t) st_pre[t] = t < M ? a.state[static_cast<int64_t>(t) * a.N + n] : 0.0f;
+    }
+  }
+
   // ---- 2. the predecessor's outputs are needed from here on
   grid_dep_wait();
   grid_dep_launch();
@@ -97,13 +144,15 @@ __global__ void __launch_bounds__(kDecThreads) dec_kernel(DecArgs a) {
   // ---- 3. prologue: rows into shared memory, exact norms, Q5.10 byte planes
   for (int t = 0; t < MT; ++t) {
     const int tr = t < M ? t : M - 1;
-    for (int c = tid; c < K; c += kDecThreads) xs[t * K4 + c] = a.x[static_cast<int64_t>(tr) * K + c];
+    const float* xr = a.x + static_cast<int64_t>(tr) * K;
+    for (int c = tid; c < K; c += kDecThreads) xs[t * K4 + c] = __ldcg(xr + c);
   }
   __syncthreads();
   const int myrow = (lane >> 3) < MT ? (lane >> 3) : MT - 1;  // warp 0: 8 lanes per row
+  const float* nproj = nws + (PRO == kDecProPlain ? 0 : K4);    // projection norm weights
   if (PRO != kDecProPlain) {
     if (warp == 0) {
-      const float r = rstd_of(chain8(xs + myrow * K4, K), static_cast<float>(K), a.eps);
+      const float r = rstd_of(sumsq_exact8(xs + myrow * K4, K, 0xffffffffu), static_cast<float>(K), a.eps);
       if ((lane & 7) == 0 && (lane >> 3) < MT) s_r[lane >> 3] = r;
     }
     __syncthreads();
@@ -111,42 +160,58 @@ __global__ void __launch_bounds__(kDecThreads) dec_kernel(DecArgs a) {
       const float r1 = s_r[t];
       const int tr = t < M ? t : M - 1;
       for (int c = tid; c < K; c += kDecThreads) {
-        float v = norm_x(xs[t * K4 + c], r1, a.prew[c]);
-        if (PRO == kDecProSwish) v = __fmul_rn(v, silu_x(a.o[static_cast<int64_t>(tr) * K + c], in_body(c, K)));
+        float v = norm_x(xs[t * K4 + c], r1, nws[c]);
+        if (PRO == kDecProSwish)
+          v = __fmul_rn(v, silu_x(__ldcg(a.o + static_cast<int64_t>(tr) * K + c), in_body(c, K)));
         xs[t * K4 + c] = v;
       }
     }
     __syncthreads();
   }
   if (warp == 0) {
-    const float r = rstd_of(chain8(xs + myrow * K4, K), static_cast<float>(K), a.eps);
+    const float r = rstd_of(sumsq_exact8(xs + myrow * K4, K, 0xffffffffu), static_cast<float>(K), a.eps);
     if ((lane & 7) == 0 && (lane >> 3) < MT) s_r[lane >> 3] = r;
   }
   __syncthreads();
-  for (int j = 0; j < NP; ++j)
-    for (int t = 0; t < MT; ++t) {
-      const float r2 = s_r[t];
-      int local = 0;
-      int8_t* hi = pl + (static_cast<int64_t>(j) * MT + t) * 2 * kp;
-      int8_t* lo = hi + kp;
-      for (int c = tid; c < kp; c += kDecThreads) {
-        int32_t q = 0;
-        if (c < K) q = quant_x(norm_x(xs[t * K4 + c], r2, a.normw[j][c]), a.qs, in_body(c, K));
-        local += q;
-        hi[c] = static_cast<int8_t>(q >> 8);
-        lo[c] = static_cast<int8_t>(q & 0xff);
-      }
+  {
+    int local[NP][MT];
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) local += __shfl_xor_sync(0xffffffffu, local, o);
-      if (lane == 0) s_red[warp] = local;
-      __syncthreads();
-      if (tid == 0) {
-        int tot = 0;
-        for (int w = 0; w < kDecWarps; ++w) tot += s_red[w];
-        s_rowsum[j][t] = tot;
+    for (int j = 0; j < NP; ++j)
+#pragma unroll
+      for (int t = 0; t < MT; ++t) local[j][t] = 0;
+    for (int c = tid; c < kp; c += kDecThreads) {
+#pragma unroll
+      for (int t = 0; t < MT; ++t) {
+        const float xv = c < K ? xs[t * K4 + c] : 0.0f;
+        const float r2 = s_r[t];
+#pragma unroll
+        for (int j = 0; j < NP; ++j) {
+          int32_t q = 0;
+          if (c < K) q = quant_x(norm_x(xv, r2, nproj[j * K4 + c]), a.qs, in_body(c, K));
+          local[j][t] += q;
+          int8_t* hi = pl + (static_cast<int64_t>(j) * MT + t) * 2 * kp;
+          hi[c] = static_cast<int8_t>(q >> 8);
+          hi[kp + c] = static_cast<int8_t>(q & 0xff);
+        }
       }
-      __syncthreads();
     }
+#pragma unroll
+    for (int j = 0; j < NP; ++j)
+#pragma unroll
+      for (int t = 0; t < MT; ++t) {
+        int v = local[j][t];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) red[(j * MT + t) * kDecWarps + warp] = static_cast<uint32_t>(v);
+      }
+    __syncthreads();
+    if (tid < NP * MT) {
+      int tot = 0;
+      for (int w = 0; w < kDecWarps; ++w) tot += static_cast<int>(red[tid * kDecWarps + w]);
+      s_rowsum[tid / MT][tid % MT] = tot;
+    }
+    __syncthreads();
+  }
 
   // ---- 4. matmul over this CTA's units; lane = output row, warps split the k-chunks
   float best_v[MT];
@@ -154,7 +219,7 @@ __global__ void __launch_bounds__(kDecThreads) dec_kernel(DecArgs a) {
 #pragma unroll
   for (int t = 0; t < MT; ++t) { best_v[t] = -FLT_MAX; best_i[t] = 0x7fffffff; }
 
-  for (int u = blockIdx.x; u < units; u += gridDim.x) {
+  for (int u = u0; u < units; u += gridDim.x) {
     int acc_hi[NW][MT][4], acc_lo[NW][MT][4];
 #pragma unroll
     for (int j = 0; j < NW; ++j)
@@ -162,14 +227,7 @@ __global__ void __launch_bounds__(kDecThreads) dec_kernel(DecArgs a) {
       for (int t = 0; t < MT; ++t)
 #pragma unroll
         for (int q = 0; q < 4; ++q) acc_hi[j][t][q] = acc_lo[j][t][q] = 0;
-    for (int64_t c = warp; c < kc; c += kDecWarps) {
-      uint4 wv[NW];
-#pragma unroll
-      for (int j = 0; j < NW; ++j) {
-        const int g = EPI == kDecEpiSwiglu ? u + j * half : u;
-        const void* wj = EPI == kDecEpiSwiglu ? a.w[0] : a.w[j];
-        wv[j] = __ldg(static_cast<const uint4*>(wj) + (static_cast<int64_t>(g) * kc + c) * 32 + lane);
-      }
+    auto chunk = [&](const uint4 (&wv)[NW], int64_t c) {
 #pragma unroll
       for (int j = 0; j < NW; ++j) {
         const int pj = NP == 1 ? 0 : j;
@@ -191,6 +249,16 @@ __global__ void __launch_bounds__(kDecThreads) dec_kernel(DecArgs a) {
           }
         }
       }
+    };
+    bool from_smem = false;
+    if (stage && u == u0) {  // the staged first unit (bounded wait; global loads if it times out)
+      for (uint32_t i = 0; i < kStageSpin && !from_smem; ++i) from_smem = mbar_test(&s_bar, 0);
+    }
+    for (int64_t c = warp; c < kc; c += kDecWarps) {
+      uint4 wv[NW];
+#pragma unroll
+      for (int j = 0; j < NW; ++j) wv[j] = from_smem ? wst[(j * kc + c) * 32 + lane] : __ldg(wrow(u, j) + c * 32);
+      chunk(wv, c);
     }
     // combine the 4 byte-shift groups, then the warps, in shared memory
 #pragma unroll
@@ -213,11 +281,14 @@ __global__ void __launch_bounds__(kDecThreads) dec_kernel(DecArgs a) {
 #pragma unroll
         for (int t = 0; t < MT; ++t) {
           uint32_t v = 0;
+#pragma unroll
           for (int w = 0; w < kDecWarps; ++w) v += red[((w * NW + j) * MT + t) * 32 + lane];
           acc[j][t] = static_cast<int32_t>(v - static_cast<uint32_t>(s_rowsum[NP == 1 ? 0 : j][t]));
         }
       const int n = u * 32 + lane;  // output column (first group of the unit)
-      for (int t = 0; t < M && t < MT; ++t) {
+#pragma unroll
+      for (int t = 0; t < MT; ++t) {
+        if (t >= M) break;
         if (EPI == kDecEpiMixer) {
           if (n < a.N) {
             const float iv = __fmul_rn(__int2float_rn(acc[0][t]), a.scale[0]);
@@ -225,10 +296,11 @@ __global__ void __launch_bounds__(kDecThreads) dec_kernel(DecArgs a) {
             const float gv = __fmul_rn(__int2float_rn(acc[NW > 2 ? 2 : 0][t]), a.scale[NW > 2 ? 2 : 0]);
             const int64_t e = static_cast<int64_t>(t) * a.N + n;
             const bool body = in_body(e % a.seg, a.seg);
+            const bool first = u == u0;
             float fv = sigmoid_x(fr, body);
-            if (a.lb) fv = lower_bound_x(fv, a.lb[n]);
+            if (a.lb) fv = lower_bound_x(fv, first ? lb_pre : __ldg(a.lb + n));
             const float sv = swiglu_x(iv, __fadd_rn(1.0f, -fv), body);
-            const float st = hgrn_step_x(fv, a.state[e], sv);
+            const float st = hgrn_step_x(fv, first ? st_pre[t] : a.state[e], sv);
             a.state[e] = st;
             a.out[0][e] = st;  // recurrence output
             a.out[1][e] = gv;  // g_proj output (normed by K2)
@@ -236,7 +308,7 @@ __global__ void __launch_bounds__(kDecThreads) dec_kernel(DecArgs a) {
         } else if (EPI == kDecEpiResid) {
           if (n < a.N) {
             const int64_t e = static_cast<int64_t>(t) * a.N + n;
-            a.out[0][e] = __fadd_rn(a.resid[e], __fmul_rn(__int2float_rn(acc[0][t]), a.scale[0]));
+            a.out[0][e] = __fadd_rn(__ldcg(a.resid + e), __fmul_rn(__int2float_rn(acc[0][t]), a.scale[0]));
           }
         } else if (EPI == kDecEpiSwiglu) {
           const int I = a.N / 2;
@@ -302,7 +374,8 @@ __global__ void __launch_bounds__(kDecThreads) dec_kernel(DecArgs a) {
         // the reference scan (hgrn_model.cpp:271-273) starts from index 0 and never moves
         // away from a NaN there; NaNs elsewhere never win (NaN comparisons are false)
         const float l0 = __ldcg(a.out[0] + static_cast<int64_t>(t) * a.N);
-        if (lane == 0) a.ids[t * a.stride + p + 1] = isnan(l0) ? 0 : (bv == -FLT_MAX && bi == 0x7fffffff ? 0 : bi);
+        if (lane == 0)
+          a.ids[t * a.stride + p + 1] = isnan(l0) ? 0 : (bi == 0x7fffffff ? 0 : bi);
       }
       if (lane == 0) {
         *a.done = 0;
@@ -316,9 +389,15 @@ template <int MT, int NP, int NW, int PRO, int EPI>
 static cudaError_t launch_dec_t(const DecArgs& a, int grid, cudaStream_t s, bool pdl) {
   const int64_t kp = padded_k(a.K);
   const int K4 = (a.K + 3) & ~3;
-  const size_t smem = static_cast<size_t>(MT) * K4 * 4 + static_cast<size_t>(NP) * MT * 2 * kp +
-                      static_cast<size_t>(kDecWarps) * NW * MT * 32 * 4;
+  constexpr int kNorms = (PRO == kDecProPlain ? 0 : 1) + NP;
+  size_t smem = static_cast<size_t>(MT + kNorms) * K4 * 4 + static_cast<size_t>(NP) * MT * 2 * kp +
+                static_cast<size_t>(kDecWarps) * NW * MT * 32 * 4;
   if (smem > 224 * 1024) return cudaErrorInvalidValue;
+  // stage the first unit's weights in shared memory when they fit
+  DecArgs b = a;
+  const size_t staged = static_cast<size_t>(NW) * padded_k(a.K) / kChunkK * kChunkBytes;
+  b.stage = smem + staged <= 224 * 1024 ? 1 : 0;
+  if (b.stage) smem += staged;
   // the opt-in limit covers static + dynamic shared memory: raise it to what this launch needs
   static size_t attr[64] = {0};
   int dev = 0;
@@ -340,10 +419,10 @@ static cudaError_t launch_dec_t(const DecArgs& a, int grid, cudaStream_t s, bool
   attrs[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attrs;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, dec_kernel<MT, NP, NW, PRO, EPI>, a);
+  return cudaLaunchKernelEx(&cfg, dec_kernel<MT, NP, NW, PRO, EPI>, b);
 }
 
-// units of work and a grid of at most two CTAs per SM
+// units of work (the launcher uses at most two CTAs per SM)
 int dec_units(const DecArgs& a, int epi) {
   const int ng = static_cast<int>(packed_groups(a.N));
   return epi == kDecEpiSwiglu ? ng / 2 : ng;

@@ -140,4 +140,38 @@ __device__ __forceinline__ float hsum8_lanes(float v, unsigned mask = 0xffffffff
   return __shfl_sync(mask, s, 0, 8);
 }
 
+// Lane j (= threadIdx.x & 7) of an 8-lane group runs chain j of the AVX2 sum of squares
+// (simd.hpp:69-89) over s[0..K): acc_j = fma(s[8i+j], s[8i+j], acc_j) for i < K/8, in order.
+// The loads are issued in batches of 8 one batch ahead of the FMAs, so the serial chain
+// waits only on the FMA latency. Returns this lane's partial (combine with hsum8_lanes).
+__device__ __forceinline__ float sumsq_chain_lane(const float* s, int K) {
+  const int j = threadIdx.x & 7;
+  const int n8 = K >> 3;
+  float acc = 0.0f;
+  float cur[8], nxt[8];
+  int i = 0;
+#pragma unroll
+  for (int u = 0; u < 8; ++u) cur[u] = (u < n8) ? s[8 * u + j] : 0.0f;
+  for (; i + 8 <= n8; i += 8) {
+    const bool more = i + 8 < n8;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) nxt[u] = (more && i + 8 + u < n8) ? s[8 * (i + 8 + u) + j] : 0.0f;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) acc = __fmaf_rn(cur[u], cur[u], acc);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) cur[u] = nxt[u];
+  }
+#pragma unroll
+  for (int u = 0; u < 8; ++u)
+    if (i + u < n8) acc = __fmaf_rn(cur[u], cur[u], acc);
+  return acc;
+}
+
+// Full reference sum of squares of s[0..K) for the 8-lane group (every lane gets it).
+__device__ __forceinline__ float sumsq_exact8(const float* s, int K, unsigned mask) {
+  float sum = hsum8_lanes(sumsq_chain_lane(s, K), mask);
+  for (int c = (K >> 3) * 8; c < K; ++c) sum = __fadd_rn(sum, __fmul_rn(s[c], s[c]));
+  return sum;
+}
+
 }  // namespace mmfree_cuda

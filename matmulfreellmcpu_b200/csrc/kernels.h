@@ -90,6 +90,7 @@ struct DecArgs {
   unsigned* done = nullptr;
   float* part_v = nullptr;        // logits: per-CTA partial maxima [grid][kDecMaxRows]
   int* part_i = nullptr;
+  int stage = 0;                  // set by the launcher: first unit staged in shared memory
 };
 int dec_units(const DecArgs& a, int epi);
 cudaError_t launch_dec(const DecArgs& a, int pro, int epi, int grid, cudaStream_t s, bool pdl);
