@@ -64,56 +64,83 @@ cudaError_t launch_repack(void* dst, const int8_t* wq, int64_t n, int64_t k, uin
 }
 
 // ------------------------------------------------------------------------------ prep
-// sum of squares of s[0..K) in the reference order (simd.hpp:69-89): lanes 0..7 of warp 0
-// each run one serial FMA chain, then the AVX2 horizontal tree, then the unfused tail.
-__device__ __forceinline__ float chain_sumsq(const float* s, int K) {
-  const int j = threadIdx.x & 7;
-  const int n8 = K >> 3;
-  float acc = 0.0f;
-#pragma unroll 8
-  for (int i = 0; i < n8; ++i) {
-    const float v = s[8 * i + j];
-    acc = __fmaf_rn(v, v, acc);
-  }
-  float sum = hsum8_lanes(acc, 0xffu);
-  for (int c = n8 * 8; c < K; ++c) sum = __fadd_rn(sum, __fmul_rn(s[c], s[c]));
-  return sum;
-}
-
-__device__ __forceinline__ int block_sum_int(int v, int* red) {
+// Copies up to 6 arrays of K floats (those with a non-null dst) from global into shared
+// memory; every thread issues the loads of a whole batch (kBatch elements of each array)
+// before its first store, so one memory latency covers the batch instead of one per element.
+template <int kBatch>
+__device__ __forceinline__ void stage_arrays(float* const (&dst)[6], const float* const (&src)[6],
+                                             int K) {
+  for (int c0 = threadIdx.x; c0 < K; c0 += kBatch * blockDim.x) {
+    float v[6][kBatch];
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  int t = 0;
-  if (threadIdx.x == 0)
-    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t += red[w];
-  __syncthreads();
-  return t;
+    for (int s = 0; s < 6; ++s)
+#pragma unroll
+      for (int i = 0; i < kBatch; ++i) {
+        const int c = c0 + i * static_cast<int>(blockDim.x);
+        v[s][i] = (dst[s] != nullptr && c < K) ? __ldg(src[s] + c) : 0.0f;
+      }
+#pragma unroll
+    for (int s = 0; s < 6; ++s)
+#pragma unroll
+      for (int i = 0; i < kBatch; ++i) {
+        const int c = c0 + i * static_cast<int>(blockDim.x);
+        if (dst[s] != nullptr && c < K) dst[s][c] = v[s][i];
+      }
+  }
 }
 
-__global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepArgs a, int mode) {
-  extern __shared__ float srow[];  // the row being normalized, K floats
+// Shared-memory floats of one prep CTA: the row, plus (when staged) every per-element input.
+static int64_t prep_smem_floats(const PrepArgs& a, int mode, bool staged) {
+  int arrays = 1;
+  if (staged) arrays += (mode != kPrepPlain ? 1 : 0) + (mode == kPrepSwishgate ? 1 : 0) + a.nproj;
+  return static_cast<int64_t>(arrays) * a.K;
+}
+
+__global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepArgs a, int mode, int staged) {
+  extern __shared__ float sbuf[];
+  float* srow = sbuf;  // the row being normalized, K floats
   __shared__ float s_rstd;
-  __shared__ int s_red[kPrepThreads / 32];
+  __shared__ int s_red[3][kPrepThreads / 32];
   const int m = blockIdx.x, K = a.K, tid = threadIdx.x;
   const int64_t Kp = padded_k(K);
   const float* x = a.x + static_cast<int64_t>(m) * K;
-  for (int c = tid; c < K; c += blockDim.x) srow[c] = x[c];
+  const float* orow = a.o ? a.o + static_cast<int64_t>(m) * K : nullptr;
+
+  // stage the inputs: with `staged` every pass below reads shared memory only
+  // (slots: row, row-transform weight, recurrence output, projection norm weights)
+  const float* prew = a.prew;
+  const float* nw[3] = {a.normw[0], a.normw[1], a.normw[2]};
+  {
+    const bool use1 = staged && mode != kPrepPlain, use2 = staged && mode == kPrepSwishgate;
+    float* p1 = sbuf + K;
+    float* p2 = p1 + (use1 ? K : 0);
+    float* p3 = p2 + (use2 ? K : 0);
+    float* const dst[6] = {srow, use1 ? p1 : nullptr, use2 ? p2 : nullptr,
+                           staged && a.nproj > 0 ? p3 : nullptr,
+                           staged && a.nproj > 1 ? p3 + K : nullptr,
+                           staged && a.nproj > 2 ? p3 + 2 * K : nullptr};
+    const float* const src[6] = {x, a.prew, orow, a.normw[0], a.normw[1], a.normw[2]};
+    stage_arrays<8>(dst, src, K);
+    if (use1) prew = p1;
+    if (use2) orow = p2;
+    if (staged) {
+      nw[0] = p3;
+      nw[1] = p3 + K;
+      nw[2] = p3 + 2 * K;
+    }
+  }
   __syncthreads();
 
   if (mode != kPrepPlain) {
     if (tid < 8) {
-      const float r = rstd_of(chain_sumsq(srow, K), static_cast<float>(K), a.eps);
+      const float r = rstd_of(sumsq_exact8(srow, K, 0xffu), static_cast<float>(K), a.eps);
       if (tid == 0) s_rstd = r;
     }
     __syncthreads();
     const float r1 = s_rstd;
-    const float* o = a.o + static_cast<int64_t>(m) * K;
     for (int c = tid; c < K; c += blockDim.x) {
-      float t = norm_x(srow[c], r1, a.prew[c]);
-      if (mode == kPrepSwishgate) t = __fmul_rn(t, silu_x(o[c], in_body(c, K)));
+      float t = norm_x(srow[c], r1, prew[c]);
+      if (mode == kPrepSwishgate) t = __fmul_rn(t, silu_x(orow[c], in_body(c, K)));
       srow[c] = t;
       if (a.pre_out) a.pre_out[static_cast<int64_t>(m) * K + c] = t;
     }
@@ -122,33 +149,47 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepArgs a, int mode
   if (a.nproj == 0) return;
 
   if (tid < 8) {
-    const float r = rstd_of(chain_sumsq(srow, K), static_cast<float>(K), a.eps);
+    const float r = rstd_of(sumsq_exact8(srow, K, 0xffu), static_cast<float>(K), a.eps);
     if (tid == 0) s_rstd = r;
   }
   __syncthreads();
   const float r2 = s_rstd;
 
-  for (int j = 0; j < a.nproj; ++j) {
-    const float* nw = a.normw[j];
-    int local = 0;
-    for (int c = tid; c < Kp; c += blockDim.x) {
+  int local[3] = {0, 0, 0};
+  for (int c = tid; c < Kp; c += blockDim.x) {
+    const float xv = c < K ? srow[c] : 0.0f;
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      if (j >= a.nproj) break;
       float y = 0.0f;
       if (c < K) {
-        y = norm_x(srow[c], r2, nw[c]);
+        y = norm_x(xv, r2, nw[j][c]);
         if (j == 0 && a.norm_out) a.norm_out[static_cast<int64_t>(m) * K + c] = y;
       }
       if (a.fixed) {
         const int32_t q = c < K ? quant_x(y, a.qs, in_body(c, K)) : 0;
-        local += q;
+        local[j] += q;
         a.planes[j][static_cast<int64_t>(m) * Kp + c] = static_cast<int8_t>(q >> 8);
         a.planes[j][(static_cast<int64_t>(a.M) + m) * Kp + c] = static_cast<int8_t>(q & 0xff);
       } else {
         a.yf[j][static_cast<int64_t>(m) * Kp + c] = y;
       }
     }
-    if (a.fixed) {
-      const int total = block_sum_int(local, s_red);
-      if (tid == 0) a.rowsum[j][m] = total;
+  }
+  if (a.fixed) {
+    const int warp = tid >> 5, lane = tid & 31;
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      int v = local[j];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0) s_red[j][warp] = v;
+    }
+    __syncthreads();
+    if (tid < a.nproj) {
+      int total = 0;
+      for (int w = 0; w < kPrepThreads / 32; ++w) total += s_red[tid][w];
+      a.rowsum[tid][m] = total;
     }
   }
 }
@@ -164,13 +205,32 @@ static void raise_smem_limit(const void* fn) {
 
 cudaError_t launch_prep(const PrepArgs& a, cudaStream_t s) {
   if (a.M <= 0) return cudaSuccess;
-  const size_t smem = static_cast<size_t>(a.K) * sizeof(float);
-  if (smem > kMaxDynSmem) return cudaErrorInvalidValue;
-  if (smem > 48 * 1024) raise_smem_limit(reinterpret_cast<const void*>(prep_kernel));
   int mode = kPrepPlain;
   if (a.prew) mode = a.o ? kPrepSwishgate : kPrepNorm;
-  prep_kernel<<<a.M, kPrepThreads, smem, s>>>(a, mode);
+  if (a.nproj < 0 || a.nproj > 3) return cudaErrorInvalidValue;
+  int staged = 1;
+  size_t smem = static_cast<size_t>(prep_smem_floats(a, mode, true)) * sizeof(float);
+  if (smem > kMaxDynSmem) {  // very long rows: stage the row only
+    staged = 0;
+    smem = static_cast<size_t>(prep_smem_floats(a, mode, false)) * sizeof(float);
+  }
+  if (smem > kMaxDynSmem) return cudaErrorInvalidValue;
+  if (smem > 48 * 1024) raise_smem_limit(reinterpret_cast<const void*>(prep_kernel));
+  prep_kernel<<<a.M, kPrepThreads, smem, s>>>(a, mode, staged);
   return cudaGetLastError();
+}
+
+__device__ __forceinline__ int block_sum_int(int v, int* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  int t = 0;
+  if (threadIdx.x == 0)
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t += red[w];
+  __syncthreads();
+  return t;
 }
 
 __global__ void __launch_bounds__(kPrepThreads) codes_kernel(int8_t* __restrict__ planes,

@@ -52,6 +52,7 @@ struct MatmulArgs {
   uint32_t* tc_tiles = nullptr;   // one counter per output tile
   size_t tc_tiles_words = 0;
   uint32_t* err = nullptr;
+  bool pdl = false;               // launch as a programmatic dependent of the previous kernel
 };
 
 constexpr int kTcMinRows = 16;

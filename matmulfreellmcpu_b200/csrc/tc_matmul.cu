@@ -4,37 +4,47 @@
 // rows n, the same integer result as matmul_fixed_kernel (kernels.cu) and the reference's
 // CpuBackend (ternary_backend.hpp:96-103), so every output is bit-identical.
 //
-// Per CTA: a tile of 128 weight rows x BN tokens, K in blocks of 128.
-//   A (weights)  tiled 2-bit codes u = w + 1 are loaded by the 128 threads (thread = row,
-//                16 B per 64-k chunk, a warp reads one contiguous 512-B line), expanded to u8
-//                in registers and written to TENSOR MEMORY with tcgen05.st (row = TMEM lane,
-//                4 codes per 32-bit column). The 4x-expanded operand never uses shared
-//                memory bandwidth.
-//   B (acts)     the high-byte (s8) and low-byte (u8) planes of the Q5.10 codes, BN rows x
-//                128 B per k-block, copied with cp.async into shared memory in the
-//                128-byte-swizzled K-major layout the MMA descriptor names.
-//   MMA          one thread issues tcgen05.mma.cta_group::1.kind::i8 with A from TMEM:
-//                D_hi += u x hi (u8 x s8), D_lo += u x lo (u8 x u8), M=128, N=BN, K=32 per
-//                instruction, int32 accumulators in TMEM; tcgen05.commit signals an mbarrier
-//                per pipeline stage.
-//   epilogue     tcgen05.ld of D_hi/D_lo; acc = 256*D_hi + D_lo - sum_k q[t, k] (exact in
-//                int32); split-K partials are combined with integer atomics (exact, order
-//                free) and the last CTA of a tile applies dequant (+ residual).
-// Every wait on an mbarrier is bounded; on timeout the CTA sets an error flag, stops issuing
-// work, waits (bounded) for its own MMAs and still frees its tensor memory.
+// Per CTA: a tile of 128 weight rows (4 packed 32-row groups) x BN tokens, K in blocks of
+// 128, split-K over blockIdx.z. Warp-specialised, every hand-off through an mbarrier ring:
+//   warp 4  weight producer    one bulk async copy per group and k-block (the packed format
+//                              keeps a group's chunks contiguous) into an 8-stage ring; the
+//                              weights depend on no earlier kernel, so this runs ahead of
+//                              griddepcontrol.wait and overlaps the predecessor kernel
+//   warp 5  activation producer after griddepcontrol.wait, TMA (cp.async.bulk.tensor.2d)
+//                              loads of the high-byte (s8) and low-byte (u8) planes of the
+//                              Q5.10 codes, BN rows x 128 B per plane and k-block, written
+//                              with the 128-byte swizzle the MMA descriptor names
+//   warps 0-3 expanders        warp w expands group w's 2-bit codes u = w + 1 to u8 and
+//                              writes them to TENSOR MEMORY (lane = weight row, 4 codes per
+//                              32-bit column) with tcgen05.st; a 4-stage TMEM ring
+//   warp 6  MMA issuer         tcgen05.mma.cta_group::1.kind::i8 with A from TMEM:
+//                              D_hi += u x hi (u8 x s8), D_lo += u x lo (u8 x u8), M=128,
+//                              N=BN, K=32 per instruction, int32 accumulators in TMEM;
+//                              tcgen05.commit releases the ring stages
+//   epilogue (warps 0-3)       tcgen05.ld of D_hi/D_lo; acc = 256*D_hi + D_lo - sum_k q[t, k]
+//                              (exact in int32); split-K partials are combined with integer
+//                              atomics (exact, order free) and the last CTA of a tile
+//                              applies dequant (+ residual).
+// Every wait on an mbarrier is bounded; on timeout the CTA sets an error flag, the other roles
+// stop, producers wait (bounded) for their copies in flight, the MMA issuer's final commit
+// covers its MMAs, and the tensor memory is freed.
 #include "common.cuh"
 #include "kernels.h"
 
+#include <cuda.h>
 #include <cstdint>
 
 namespace mmfree_cuda {
 
 namespace {
 
-constexpr int kTcThreads = 128;
-constexpr int kStages = 4;           // pipeline depth (A in TMEM, B in shared memory)
-constexpr int kPrefetch = 2;         // B k-blocks in flight ahead of the current one
+constexpr int kTcThreads = 224;      // 7 warps (roles above)
+constexpr int kWWarp = 4, kBWarp = 5, kMmaWarp = 6;
+constexpr int kWStages = 8;          // weight k-blocks in shared memory
+constexpr int kBStages = 4;          // activation k-blocks in shared memory
+constexpr int kAStages = 4;          // expanded weight k-blocks in tensor memory (32 columns)
 constexpr int kKBlock = 128;         // k per pipeline stage (2 packed chunks)
+constexpr int kWBlock = 4 * 2 * kChunkBytes;  // bytes of one weight k-block (4 groups)
 constexpr uint32_t kSpinLimit = 1u << 26;  // bounded mbarrier waits
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -65,20 +75,46 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   return false;
 }
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
-               "r"(src_bytes)
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// arrive and add `bytes` to the transaction count the phase waits for
+__device__ __forceinline__ void mbar_arrive_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                : "memory");
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+// L2 policy for data read once per launch (the weights): evict first, so that the stream
+// does not displace activations and kernel code
+__device__ __forceinline__ uint64_t l2_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+// bulk global -> shared copy completing on an mbarrier (no multicast), with an L2 policy
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                         uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+      : "memory");
+}
+// 2-D tiled TMA load (no multicast); x is a multiple of 128 bytes
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void named_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
-__device__ __forceinline__ void fence_proxy_async() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
@@ -157,207 +193,293 @@ struct TcArgs {
   int splits;         // k-block ranges per tile (grid.z)
 };
 
+namespace {
+
+// Smem layout of one CTA (offsets from a 1024-byte aligned base): the activation ring first
+// (1024-aligned stages, as the 128-byte swizzle wants), then the weight ring.
 template <int BN>
-__global__ void __launch_bounds__(kTcThreads, 1) tc_matmul_kernel(TcArgs p) {
+struct TcLayout {
+  static constexpr int kBPlane = BN * 128;               // one plane of one k-block
+  static constexpr int kBStage = 2 * kBPlane;            // high + low plane
+  static constexpr int kWOff = kBStages * kBStage;
+  static constexpr int kBytes = kWOff + kWStages * kWBlock;
+  // at least 80 KB, so that no more than two CTAs (2 x 256 TMEM columns) share an SM and
+  // tcgen05.alloc never waits for a CTA of this kernel
+  static constexpr int kDyn = (kBytes + 1024) < 80 * 1024 ? 80 * 1024 : (kBytes + 1024);
+};
+
+__device__ __forceinline__ bool cta_failed(const uint32_t* f) {
+  return *reinterpret_cast<const volatile uint32_t*>(f) != 0;
+}
+
+// bounded wait that gives up early once another role of the CTA has failed
+__device__ __forceinline__ bool role_wait(uint64_t* bar, uint32_t parity, uint32_t* s_fail) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255) == 255 && cta_failed(s_fail)) return false;
+  }
+  return false;
+}
+
+}  // namespace
+
+template <int BN>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    tc_matmul_kernel(const __grid_constant__ CUtensorMap bmap, TcArgs p) {
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 64, "BN must be 16..64, a multiple of 16");
-  constexpr int kCols = kStages * 32 + 2 * BN;                 // A stages + D_hi + D_lo
+  constexpr int kCols = kAStages * 32 + 2 * BN;  // A stages + D_hi + D_lo
   constexpr int kAllocCols = kCols <= 128 ? 128 : (kCols <= 256 ? 256 : 512);
   static_assert(kAllocCols <= 256, "two CTAs per SM must fit in the 512 TMEM columns");
-  constexpr int kBStage = BN * 128;                            // bytes of one plane per stage
+  using L = TcLayout<BN>;
 
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  // align the B stages to the 1024-byte swizzle atom
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  unsigned char* b_hi = smem;                                  // [kStages][BN][128]
-  unsigned char* b_lo = smem + kStages * kBStage;              // [kStages][BN][128]
-  __shared__ uint64_t bars[kStages + 1];  // one per stage + a drain barrier
+  unsigned char* bst = smem;             // [kBStages][2][BN][128], 128-byte swizzled rows
+  unsigned char* wst = smem + L::kWOff;  // [kWStages][4 groups][2 chunks][512]
+  __shared__ uint64_t wfull[kWStages], wempty[kWStages], bfull[kBStages], bempty[kBStages];
+  __shared__ uint64_t afull[kAStages], aempty[kAStages], dfull;
   __shared__ uint32_t tmem_base_sh;
   __shared__ uint32_t s_fail;
   __shared__ uint32_t s_last;
+  __shared__ int s_rowsum[BN];
 
   const MatmulArgs& a = p.m;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n0 = blockIdx.x * 128, t0 = blockIdx.y * BN;
-  const int64_t kc = packed_chunks(a.K), kp = kc * kChunkK;
+  const int64_t kc = packed_chunks(a.K);
   const int nkb = static_cast<int>((kc + 1) / 2);
   const int kb0 = static_cast<int>(static_cast<int64_t>(nkb) * blockIdx.z / p.splits);
   const int kb1 = static_cast<int>(static_cast<int64_t>(nkb) * (blockIdx.z + 1) / p.splits);
   const int nk = kb1 - kb0;
 
   if (tid == 0) {
-    for (int s = 0; s <= kStages; ++s) mbar_init(&bars[s], 1);
+    for (int s = 0; s < kWStages; ++s) { mbar_init(&wfull[s], 1); mbar_init(&wempty[s], 4); }
+    for (int s = 0; s < kBStages; ++s) { mbar_init(&bfull[s], 1); mbar_init(&bempty[s], 1); }
+    for (int s = 0; s < kAStages; ++s) { mbar_init(&afull[s], 4); mbar_init(&aempty[s], 1); }
+    mbar_init(&dfull, 1);
     s_fail = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    // the next kernel may start its own weight streaming now (it reads no output of ours
+    // before its griddepcontrol.wait)
+    grid_dep_launch();
   }
-  if (warp == 0) {
+  if (warp == kMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(&tmem_base_sh)),
                  "r"(kAllocCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
+  if (warp == kBWarp && lane == 0)
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&bmap)) : "memory");
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_base_sh;
-  const uint32_t tmem_a = tmem;                          // columns [0, 32*kStages)
-  const uint32_t tmem_dhi = tmem + kStages * 32;         // BN columns
-  const uint32_t tmem_dlo = tmem_dhi + BN;               // BN columns
-  const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+  const uint32_t tmem_a = tmem;                   // columns [0, 32*kAStages)
+  const uint32_t tmem_dhi = tmem + kAStages * 32; // BN columns
+  const uint32_t tmem_dlo = tmem_dhi + BN;        // BN columns
 
-  // this thread's weight row and its packed row pointer (16 B per 64-k chunk)
-  const int wrow_group = (n0 >> 5) + warp;
-  const bool wrow_ok = wrow_group < packed_groups(a.N);
-  const uint4* wrow = static_cast<const uint4*>(a.w) + static_cast<int64_t>(wrow_group) * kc * 32 + lane;
-
-  // B copy: each k-block needs 2 planes x BN rows x 8 chunks of 16 B
-  auto issue_b = [&](int kb, int s) {
-    constexpr int kChunks = 2 * BN * 8;
-    for (int i = tid; i < kChunks; i += kTcThreads) {
-      const int plane = i / (BN * 8), rem = i % (BN * 8), r = rem >> 3, c = rem & 7;
-      const int trow = min(t0 + r, a.M - 1);  // rows past M repeat row M-1 (never stored)
-      const int64_t kbyte = static_cast<int64_t>(kb) * kKBlock + c * 16;
-      const int8_t* src = a.planes + (static_cast<int64_t>(plane) * a.M + trow) * kp +
-                          (kbyte < kp ? kbyte : 0);
-      unsigned char* dst = (plane ? b_lo : b_hi) + s * kBStage + r * 128 + ((c ^ (r & 7)) << 4);
-      cp_async16(dst, src, kbyte < kp ? 16u : 0u);  // zero-fill past the padded row end
-    }
-  };
-
-  bool fail = false;
-  // prologue: B for the first kPrefetch k-blocks
-  for (int j = 0; j < kPrefetch; ++j) {
-    if (j < nk) issue_b(kb0 + j, j % kStages);
-    cp_async_commit();
-  }
-  uint4 wnext[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
-  auto load_w = [&](int kb, uint4 (&w)[2]) {
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int64_t c = static_cast<int64_t>(kb) * 2 + h;
-      w[h] = (wrow_ok && c < kc) ? __ldg(wrow + c * 32) : make_uint4(0x55555555u, 0x55555555u,
-                                                                       0x55555555u, 0x55555555u);
-    }
-  };
-  if (nk > 0) load_w(kb0, wnext);
-
-  for (int i = 0; i < nk && !fail; ++i) {
-    const int kb = kb0 + i, s = i % kStages;
-    uint4 wcur[2] = {wnext[0], wnext[1]};
-    if (i + 1 < nk) load_w(kb + 1, wnext);
-    // refill B stage of k-block i + kPrefetch once the MMAs that read it (i + kPrefetch -
-    // kStages) are done
-    const int ip = i + kPrefetch;
-    if (ip < nk) {
-      const int used = ip - kStages;
-      if (used >= 0 && !mbar_wait(&bars[used % kStages], (used / kStages) & 1)) fail = true;
-      issue_b(kb0 + ip, ip % kStages);
-    }
-    cp_async_commit();
-    // A stage s was read by the MMAs of k-block i - kStages
-    if (i >= kStages && !mbar_wait(&bars[s], ((i - kStages) / kStages) & 1)) fail = true;
-    tc_fence_after();
-    // expand 2 x 64 codes to u8 and store them to TMEM columns s*32 + [0, 32)
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const uint32_t wd[4] = {wcur[h].x, wcur[h].y, wcur[h].z, wcur[h].w};
-      uint32_t r[16];
-#pragma unroll
-      for (int w4 = 0; w4 < 4; ++w4)
-#pragma unroll
-        for (int q = 0; q < 4; ++q) r[4 * w4 + q] = (wd[w4] >> (2 * q)) & 0x03030303u;
-      tmem_st16(tmem_a + lane_base + static_cast<uint32_t>(s * 32 + h * 16), r);
-    }
-    tmem_st_wait();
-    cp_async_wait<kPrefetch>();  // this k-block's B copies have landed
-    fence_proxy_async();          // make them visible to the tensor core (async proxy)
-    if (fail) s_fail = 1;
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0 && s_fail == 0) {
-      tc_fence_after();
-      const uint32_t hi_base = smem_u32(b_hi + s * kBStage);
-      const uint32_t lo_base = smem_u32(b_lo + s * kBStage);
-#pragma unroll
-      for (int j = 0; j < kKBlock / 32; ++j) {
-        const uint32_t acc = (i > 0 || j > 0) ? 1u : 0u;
-        const uint32_t a_addr = tmem_a + static_cast<uint32_t>(s * 32 + j * 8);
-        mma_i8_ts(tmem_dhi, a_addr, smem_desc_sw128(hi_base + j * 32), idesc_i8(true, BN), acc);
-        mma_i8_ts(tmem_dlo, a_addr, smem_desc_sw128(lo_base + j * 32), idesc_i8(false, BN), acc);
+  if (warp == kWWarp) {
+    // ---- weight producer: 4 groups x (1 or 2) chunks per k-block, contiguous per group
+    if (lane == 0) {
+      const int64_t ngroups = packed_groups(a.N);
+      const unsigned char* wbase = static_cast<const unsigned char*>(a.w);
+      const uint64_t pol = l2_evict_first();
+      int i = 0;
+      for (; i < nk; ++i) {
+        const int s = i % kWStages;
+        // from here on progress depends on the activations: wait for the predecessor first,
+        // so that the bounded waits never include its run time
+        if (i == kWStages) grid_dep_wait();
+        if (i >= kWStages && !role_wait(&wempty[s], ((i / kWStages) - 1) & 1, &s_fail)) break;
+        const int64_t c0 = 2 * static_cast<int64_t>(kb0 + i);
+        const uint32_t bytes = c0 + 1 < kc ? 2 * kChunkBytes : kChunkBytes;
+        uint32_t total = 0;
+        for (int g = 0; g < 4; ++g)
+          if ((n0 >> 5) + g < ngroups) total += bytes;
+        mbar_arrive_tx(&wfull[s], total);
+        for (int g = 0; g < 4; ++g) {
+          const int64_t gg = (n0 >> 5) + g;
+          if (gg < ngroups)
+            bulk_g2s(wst + s * kWBlock + g * 2 * kChunkBytes, wbase + (gg * kc + c0) * kChunkBytes,
+                     bytes, &wfull[s], pol);
+        }
       }
-      mma_commit(&bars[s]);
+      if (i < nk) {  // failed: note it, then let the copies already issued land
+        atomicOr(&s_fail, 1u);
+        for (int j = i - kWStages > 0 ? i - kWStages : 0; j < i; ++j)
+          mbar_wait(&wfull[j % kWStages], (j / kWStages) & 1);
+      }
     }
-    __syncthreads();
-    fail = s_fail != 0;
-  }
-  cp_async_wait<0>();
-
-  // wait for the last MMAs (their commit covers every earlier MMA of this thread)
-  if (nk > 0 && !fail) {
-    const int last = nk - 1;
-    if (!mbar_wait(&bars[last % kStages], (last / kStages) & 1)) fail = true;
-  }
-  // one decision for the whole CTA: the epilogue's tcgen05.ld is warp-collective
-  fail = __syncthreads_or(fail) != 0;
-  tc_fence_after();
-  if (fail) {
-    if (tid == 0) {
-      if (p.err) atomicOr(p.err, kErrTimeout);
-      // drain: a commit arrives once every MMA this thread issued has finished
-      mma_commit(&bars[kStages]);
-      mbar_wait(&bars[kStages], 0);
+  } else if (warp == kBWarp) {
+    // ---- activation producer: TMA loads of the high / low byte planes (after the
+    //      predecessor kernel has written them)
+    if (lane == 0) {
+      grid_dep_wait();
+      int i = 0;
+      for (; i < nk; ++i) {
+        const int s = i % kBStages;
+        if (i >= kBStages && !role_wait(&bempty[s], ((i / kBStages) - 1) & 1, &s_fail)) break;
+        const int x = (kb0 + i) * kKBlock;
+        unsigned char* dst = bst + s * L::kBStage;
+        mbar_arrive_tx(&bfull[s], static_cast<uint32_t>(L::kBStage));
+        tma_load_2d(dst, &bmap, x, t0, &bfull[s]);                  // high plane rows
+        tma_load_2d(dst + L::kBPlane, &bmap, x, a.M + t0, &bfull[s]);  // low plane rows
+      }
+      if (i < nk) {
+        atomicOr(&s_fail, 1u);
+        for (int j = i - kBStages > 0 ? i - kBStages : 0; j < i; ++j)
+          mbar_wait(&bfull[j % kBStages], (j / kBStages) & 1);
+      }
     }
-  } else if (nk > 0) {
-    // epilogue: thread = weight row n, columns = tokens
-    const int n = n0 + tid;
-    const bool n_ok = n < a.N;
+  } else if (warp == kMmaWarp) {
+    // ---- MMA issuer: per k-block 4 k-steps x (high, low) planes
+    if (lane == 0) {
+      grid_dep_wait();
+      for (int i = 0; i < nk; ++i) {
+        const int sa = i % kAStages, sb = i % kBStages;
+        if (!role_wait(&afull[sa], (i / kAStages) & 1, &s_fail) ||
+            !role_wait(&bfull[sb], (i / kBStages) & 1, &s_fail)) {
+          atomicOr(&s_fail, 1u);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t hi_base = smem_u32(bst + sb * L::kBStage);
+        const uint32_t lo_base = hi_base + L::kBPlane;
 #pragma unroll
-    for (int c0 = 0; c0 < BN; c0 += 16) {
-      uint32_t dh[16], dl[16];
-      tmem_ld16(tmem_dhi + lane_base + c0, dh);
-      tmem_ld16(tmem_dlo + lane_base + c0, dl);
+        for (int j = 0; j < kKBlock / 32; ++j) {
+          const uint32_t acc = (i > 0 || j > 0) ? 1u : 0u;
+          const uint32_t a_addr = tmem_a + static_cast<uint32_t>(sa * 32 + j * 8);
+          mma_i8_ts(tmem_dhi, a_addr, smem_desc_sw128(hi_base + j * 32), idesc_i8(true, BN), acc);
+          mma_i8_ts(tmem_dlo, a_addr, smem_desc_sw128(lo_base + j * 32), idesc_i8(false, BN), acc);
+        }
+        mma_commit(&aempty[sa]);
+        mma_commit(&bempty[sb]);
+      }
+      // arrives once every MMA issued above has completed (also on failure)
+      mma_commit(&dfull);
+    }
+    __syncwarp();
+  } else {
+    // ---- warps 0-3: expand the 2-bit codes of group `warp` (TMEM lanes 32*warp..+31) into
+    //      u8 TMEM columns, then the epilogue
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    bool ok = true;
+    for (int i = 0; i < nk; ++i) {
+      const int sw = i % kWStages, sa = i % kAStages;
+      if (!role_wait(&wfull[sw], (i / kWStages) & 1, &s_fail)) { ok = false; break; }
+      const uint4* src = reinterpret_cast<const uint4*>(wst + sw * kWBlock + warp * 2 * kChunkBytes) + lane;
+      const uint4 wv[2] = {src[0], src[kChunkBytes / 16]};
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&wempty[sw]);
+      if (i == kAStages) grid_dep_wait();  // later stages wait on MMAs that need activations
+      if (i >= kAStages && !role_wait(&aempty[sa], ((i / kAStages) - 1) & 1, &s_fail)) { ok = false; break; }
+      tc_fence_after();
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t wd[4] = {wv[h].x, wv[h].y, wv[h].z, wv[h].w};
+        uint32_t r[16];
+#pragma unroll
+        for (int w4 = 0; w4 < 4; ++w4)
+#pragma unroll
+          for (int q = 0; q < 4; ++q) r[4 * w4 + q] = (wd[w4] >> (2 * q)) & 0x03030303u;
+        tmem_st16(tmem_a + lane_base + static_cast<uint32_t>(sa * 32 + h * 16), r);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&afull[sa]);
+    }
+    if (!ok) atomicOr(&s_fail, 1u);
+    // epilogue: row sums, residuals and the split-K workspace belong to earlier kernels.
+    // The code runs once per CTA, so every instruction is a cold instruction-cache miss:
+    // the loops over 16-token groups stay rolled. Loads of a group are issued before its
+    // stores (a store may alias them) and the next group's residuals are fetched while the
+    // current group is written.
+    grid_dep_wait();
+    const int n = n0 + tid;  // thread = weight row n, columns = tokens
+    const bool n_ok = n < a.N;
+    if (tid < BN) s_rowsum[tid] = t0 + tid < a.M ? a.rowsum[t0 + tid] : 0;
+    const bool direct = p.splits == 1;
+    const bool add_resid = a.resid && a.out;
+    auto load16 = [&](int c0, float (&r)[16]) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int t = t0 + c0 + j;
+        r[j] = (add_resid && n_ok && t < a.M) ? a.resid[static_cast<int64_t>(t) * a.ldr + n] : 0.0f;
+      }
+    };
+    float rv[16];
+    if (direct) load16(0, rv);
+    const bool done = mbar_wait(&dfull, 0);
+    tc_fence_after();
+    if (!done) atomicOr(&s_fail, 1u);
+    named_sync(1, 128);  // row sums staged; the decision below is uniform over the 4 warps
+    const bool fail = s_fail != 0;
+    // dequant (+ residual) of 16 finished int32 accumulators of tokens t0 + c0 + [0, 16)
+    auto emit16 = [&](int c0, const uint32_t (&v)[16], const float (&r)[16]) {
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int t = t0 + c0 + j;
         if (!n_ok || t >= a.M) continue;
-        const uint32_t part = (dh[j] << 8) + dl[j];  // 256*D_hi + D_lo, wrapping like int32
-        if (p.splits == 1) {
-          const int32_t acc = static_cast<int32_t>(part - static_cast<uint32_t>(a.rowsum[t]));
-          if (a.acc_out) a.acc_out[static_cast<int64_t>(t) * a.N + n] = acc;
-          if (a.out) {
-            float v = __fmul_rn(__int2float_rn(acc), a.scale);
-            if (a.resid) v = __fadd_rn(a.resid[static_cast<int64_t>(t) * a.ldr + n], v);
-            a.out[static_cast<int64_t>(t) * a.ldo + n] = v;
-          }
-        } else {
-          atomicAdd(p.accum + static_cast<int64_t>(t) * a.N + n, part);
+        const int32_t acc = static_cast<int32_t>(v[j] - static_cast<uint32_t>(s_rowsum[c0 + j]));
+        if (a.acc_out) a.acc_out[static_cast<int64_t>(t) * a.N + n] = acc;
+        if (a.out) {
+          float o = __fmul_rn(__int2float_rn(acc), a.scale);
+          if (a.resid) o = __fadd_rn(r[j], o);
+          a.out[static_cast<int64_t>(t) * a.ldo + n] = o;
         }
       }
-    }
-    if (p.splits > 1) {
-      __threadfence();
-      __syncthreads();
-      if (tid == 0) {
-        const uint32_t tile = blockIdx.y * gridDim.x + blockIdx.x;
-        s_last = atomicAdd(p.tiles + tile, 1u) == static_cast<uint32_t>(p.splits - 1);
-        if (s_last) p.tiles[tile] = 0;
+    };
+    if (fail) {
+      if (tid == 0 && p.err) atomicOr(p.err, kErrTimeout);
+    } else if (nk > 0) {
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        uint32_t dh[16], dl[16], part[16];
+        tmem_ld16(tmem_dhi + lane_base + c0, dh);
+        tmem_ld16(tmem_dlo + lane_base + c0, dl);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) part[j] = (dh[j] << 8) + dl[j];  // 256*D_hi + D_lo (mod 2^32)
+        if (direct) {
+          float rn[16];
+          if (c0 + 16 < BN) load16(c0 + 16, rn);
+          emit16(c0, part, rv);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) rv[j] = rn[j];
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (n_ok && t0 + c0 + j < a.M) atomicAdd(p.accum + static_cast<int64_t>(t0 + c0 + j) * a.N + n, part[j]);
+        }
       }
-      __syncthreads();
-      if (s_last) {
+      if (!direct) {
         __threadfence();
-        for (int j = 0; j < BN; ++j) {
-          const int t = t0 + j;
-          if (!n_ok || t >= a.M) continue;
-          uint32_t* cell = p.accum + static_cast<int64_t>(t) * a.N + n;
-          const uint32_t sum = __ldcg(cell);
-          *cell = 0;  // leave the workspace zeroed for the next launch
-          const int32_t acc = static_cast<int32_t>(sum - static_cast<uint32_t>(a.rowsum[t]));
-          if (a.acc_out) a.acc_out[static_cast<int64_t>(t) * a.N + n] = acc;
-          if (a.out) {
-            float v = __fmul_rn(__int2float_rn(acc), a.scale);
-            if (a.resid) v = __fadd_rn(a.resid[static_cast<int64_t>(t) * a.ldr + n], v);
-            a.out[static_cast<int64_t>(t) * a.ldo + n] = v;
+        named_sync(1, 128);
+        if (tid == 0) {
+          const uint32_t tile = blockIdx.y * gridDim.x + blockIdx.x;
+          s_last = atomicAdd(p.tiles + tile, 1u) == static_cast<uint32_t>(p.splits - 1);
+          if (s_last) p.tiles[tile] = 0;
+        }
+        named_sync(1, 128);
+        if (s_last) {
+          __threadfence();
+#pragma unroll 1
+          for (int c0 = 0; c0 < BN; c0 += 16) {
+            uint32_t sum[16];
+            float r16[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int t = t0 + c0 + j;
+              sum[j] = (n_ok && t < a.M) ? __ldcg(p.accum + static_cast<int64_t>(t) * a.N + n) : 0u;
+            }
+            load16(c0, r16);
+#pragma unroll
+            for (int j = 0; j < 16; ++j)  // leave the workspace zeroed for the next launch
+              if (n_ok && t0 + c0 + j < a.M) p.accum[static_cast<int64_t>(t0 + c0 + j) * a.N + n] = 0;
+            emit16(c0, sum, r16);
           }
         }
       }
@@ -365,38 +487,80 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_matmul_kernel(TcArgs p) {
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == kMmaWarp) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                  "r"(kAllocCols)
                  : "memory");
   }
 }
 
-// At least 80 KB per CTA, so that no more than two CTAs (2 x 256 TMEM columns) share an SM
-// and tcgen05.alloc never waits for another CTA's columns.
-template <int BN>
-static size_t tc_smem_bytes() {
-  const size_t need = 1024 + 2 * kStages * BN * 128;
-  return need < 80 * 1024 ? 80 * 1024 : need;
+// ---- host side
+
+namespace {
+
+// cuTensorMapEncodeTiled, resolved through the runtime (no link against the driver library)
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<EncodeTiledFn>(nullptr);
+    return reinterpret_cast<EncodeTiledFn>(f);
+  }();
+  return fn;
 }
 
+// The planes [2][M][Kp] as one 2-D u8 tensor of 2M rows x Kp bytes; a box is BN rows x 128 B
+// (one k-block), written to shared memory with the 128-byte swizzle; reads past row 2M or
+// column Kp return zeros.
+cudaError_t planes_map(CUtensorMap* map, const int8_t* planes, int M, int64_t kp, int bn) {
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) return cudaErrorNotSupported;
+  if ((reinterpret_cast<uintptr_t>(planes) & 15) != 0) return cudaErrorMisalignedAddress;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(kp), 2 * static_cast<cuuint64_t>(M)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(kp)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kKBlock), static_cast<cuuint32_t>(bn)};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(planes), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+}  // namespace
+
 template <int BN>
-static cudaError_t launch_tc_bn(const TcArgs& p, cudaStream_t s) {
-  const size_t smem = tc_smem_bytes<BN>();
+static cudaError_t launch_tc_bn(const TcArgs& p, bool pdl, cudaStream_t s) {
+  using L = TcLayout<BN>;
+  CUtensorMap map;
+  cudaError_t e = planes_map(&map, p.m.planes, p.m.M, padded_k(p.m.K), BN);
+  if (e != cudaSuccess) return e;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_set[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(tc_matmul_kernel<BN>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
+    e = cudaFuncSetAttribute(tc_matmul_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kDyn);
     if (e != cudaSuccess) return e;
     attr_set[dev & 63] = true;
   }
-  dim3 grid(static_cast<unsigned>(ceil_div(p.m.N, 128)), static_cast<unsigned>(ceil_div(p.m.M, BN)),
-            static_cast<unsigned>(p.splits));
-  tc_matmul_kernel<BN><<<grid, kTcThreads, smem, s>>>(p);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(ceil_div(p.m.N, 128)), static_cast<unsigned>(ceil_div(p.m.M, BN)),
+                     static_cast<unsigned>(p.splits));
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = L::kDyn;
+  cfg.stream = s;
+  cudaLaunchAttribute attrs[1];
+  attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attrs;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, tc_matmul_kernel<BN>, map, p);
 }
 
 int tc_token_tile(int M) { return M <= 16 ? 16 : (M <= 32 ? 32 : 64); }
@@ -413,11 +577,13 @@ int tc_splits(const MatmulArgs& a, int sm_count) {
 cudaError_t launch_matmul_tc(const MatmulArgs& a, uint32_t* accum, uint32_t* tiles, int splits,
                              uint32_t* err, cudaStream_t s) {
   if (a.M <= 0 || a.N <= 0) return cudaSuccess;
+  const int nkb = static_cast<int>((packed_chunks(a.K) + 1) / 2);
+  if (splits < 1 || splits > nkb) return cudaErrorInvalidValue;  // every split owns a k-block
   TcArgs p{a, accum, tiles, err, splits};
   switch (tc_token_tile(a.M)) {
-    case 16: return launch_tc_bn<16>(p, s);
-    case 32: return launch_tc_bn<32>(p, s);
-    default: return launch_tc_bn<64>(p, s);
+    case 16: return launch_tc_bn<16>(p, a.pdl, s);
+    case 32: return launch_tc_bn<32>(p, a.pdl, s);
+    default: return launch_tc_bn<64>(p, a.pdl, s);
   }
 }
 
