@@ -69,6 +69,32 @@ enum : uint32_t {
   kErrTimeout = 8u,      // a bounded wait inside a kernel gave up
 };
 
+// Programmatic dependent launch. A kernel launched with launch_k(..., pdl = true) may start
+// while its predecessor in the stream still runs: before grid_dep_wait() it may only read
+// data no earlier kernel writes (weights, norm weights) and write nothing global; after it,
+// every earlier kernel has finished and its writes are visible. grid_dep_launch() lets the
+// next kernel start its own prologue.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                            cudaStream_t s, bool pdl, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // Epilogue selectors of the BitLinear matmul kernels.
 enum Epilogue : int {
   kEpiStore = 0,   // out[m, n] = acc * scale

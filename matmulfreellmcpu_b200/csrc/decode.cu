@@ -35,12 +35,6 @@ namespace {
 constexpr int kDecThreads = 256;
 constexpr int kDecWarps = kDecThreads / 32;
 
-__device__ __forceinline__ void grid_dep_wait() {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-}
-__device__ __forceinline__ void grid_dep_launch() {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
 __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }

@@ -64,23 +64,23 @@ cudaError_t launch_repack(void* dst, const int8_t* wq, int64_t n, int64_t k, uin
 }
 
 // ------------------------------------------------------------------------------ prep
-// Copies up to 6 arrays of K floats (those with a non-null dst) from global into shared
+// Copies up to NA arrays of K floats (those with a non-null dst) from global into shared
 // memory; every thread issues the loads of a whole batch (kBatch elements of each array)
 // before its first store, so one memory latency covers the batch instead of one per element.
-template <int kBatch>
-__device__ __forceinline__ void stage_arrays(float* const (&dst)[6], const float* const (&src)[6],
+template <int kBatch, int NA>
+__device__ __forceinline__ void stage_arrays(float* const (&dst)[NA], const float* const (&src)[NA],
                                              int K) {
   for (int c0 = threadIdx.x; c0 < K; c0 += kBatch * blockDim.x) {
-    float v[6][kBatch];
+    float v[NA][kBatch];
 #pragma unroll
-    for (int s = 0; s < 6; ++s)
+    for (int s = 0; s < NA; ++s)
 #pragma unroll
       for (int i = 0; i < kBatch; ++i) {
         const int c = c0 + i * static_cast<int>(blockDim.x);
         v[s][i] = (dst[s] != nullptr && c < K) ? __ldg(src[s] + c) : 0.0f;
       }
 #pragma unroll
-    for (int s = 0; s < 6; ++s)
+    for (int s = 0; s < NA; ++s)
 #pragma unroll
       for (int i = 0; i < kBatch; ++i) {
         const int c = c0 + i * static_cast<int>(blockDim.x);
@@ -115,12 +115,17 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepArgs a, int mode
     float* p1 = sbuf + K;
     float* p2 = p1 + (use1 ? K : 0);
     float* p3 = p2 + (use2 ? K : 0);
-    float* const dst[6] = {srow, use1 ? p1 : nullptr, use2 ? p2 : nullptr,
-                           staged && a.nproj > 0 ? p3 : nullptr,
-                           staged && a.nproj > 1 ? p3 + K : nullptr,
-                           staged && a.nproj > 2 ? p3 + 2 * K : nullptr};
-    const float* const src[6] = {x, a.prew, orow, a.normw[0], a.normw[1], a.normw[2]};
-    stage_arrays<8>(dst, src, K);
+    // weights first: no earlier kernel writes them, so they load while the predecessor runs
+    float* const dw[4] = {use1 ? p1 : nullptr, staged && a.nproj > 0 ? p3 : nullptr,
+                          staged && a.nproj > 1 ? p3 + K : nullptr,
+                          staged && a.nproj > 2 ? p3 + 2 * K : nullptr};
+    const float* const sw[4] = {a.prew, a.normw[0], a.normw[1], a.normw[2]};
+    stage_arrays<8>(dw, sw, K);
+    grid_dep_launch();
+    grid_dep_wait();
+    float* const dr[2] = {srow, use2 ? p2 : nullptr};
+    const float* const sr[2] = {x, orow};
+    stage_arrays<8>(dr, sr, K);
     if (use1) prew = p1;
     if (use2) orow = p2;
     if (staged) {
@@ -216,8 +221,7 @@ cudaError_t launch_prep(const PrepArgs& a, cudaStream_t s) {
   }
   if (smem > kMaxDynSmem) return cudaErrorInvalidValue;
   if (smem > 48 * 1024) raise_smem_limit(reinterpret_cast<const void*>(prep_kernel));
-  prep_kernel<<<a.M, kPrepThreads, smem, s>>>(a, mode, staged);
-  return cudaGetLastError();
+  return launch_k(prep_kernel, dim3(a.M), dim3(kPrepThreads), smem, s, a.pdl, a, mode, staged);
 }
 
 __device__ __forceinline__ int block_sum_int(int v, int* red) {
@@ -269,6 +273,8 @@ cudaError_t launch_codes_to_planes(int8_t* planes, int32_t* rowsum, const int32_
 // k-chunks round robin and reduce through shared memory. Lane r owns output row 32g + r.
 template <int MT>
 __global__ void __launch_bounds__(kMatmulThreads) matmul_fixed_kernel(MatmulArgs a) {
+  grid_dep_launch();
+  grid_dep_wait();
   const int g = blockIdx.x, m0 = blockIdx.y * MT;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t kc = packed_chunks(a.K), kp = kc * kChunkK;
@@ -331,6 +337,8 @@ __global__ void __launch_bounds__(kMatmulThreads) matmul_fixed_kernel(MatmulArgs
 
 template <int MT>
 __global__ void __launch_bounds__(kMatmulThreads) matmul_float_kernel(MatmulArgs a) {
+  grid_dep_launch();
+  grid_dep_wait();
   const int g = blockIdx.x, m0 = blockIdx.y * MT;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t kc = packed_chunks(a.K), kp = kc * kChunkK;
@@ -381,9 +389,8 @@ __global__ void __launch_bounds__(kMatmulThreads) matmul_float_kernel(MatmulArgs
 template <int MT>
 static cudaError_t launch_matmul_mt(const MatmulArgs& a, cudaStream_t s) {
   dim3 grid(static_cast<unsigned>(packed_groups(a.N)), static_cast<unsigned>(ceil_div(a.M, MT)));
-  if (a.fixed) matmul_fixed_kernel<MT><<<grid, kMatmulThreads, 0, s>>>(a);
-  else matmul_float_kernel<MT><<<grid, kMatmulThreads, 0, s>>>(a);
-  return cudaGetLastError();
+  if (a.fixed) return launch_k(matmul_fixed_kernel<MT>, grid, dim3(kMatmulThreads), 0, s, a.pdl, a);
+  return launch_k(matmul_float_kernel<MT>, grid, dim3(kMatmulThreads), 0, s, a.pdl, a);
 }
 
 static int sm_count() {
@@ -415,6 +422,8 @@ cudaError_t launch_matmul(const MatmulArgs& a, cudaStream_t s) {
 // of element e is taken within its segment of seg elements (one reference block() call).
 __global__ void gate_kernel(float* __restrict__ i, float* __restrict__ f,
                             const float* __restrict__ lb, int64_t n, int64_t seg, int H) {
+  grid_dep_launch();
+  grid_dep_wait();
   const int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   if (e >= n) return;
   const bool body = in_body(e % seg, seg);
@@ -430,6 +439,8 @@ __global__ void gate_kernel(float* __restrict__ i, float* __restrict__ f,
 __global__ void scan_kernel(float* __restrict__ out, const float* __restrict__ s,
                             const float* __restrict__ f, float* __restrict__ state, int nseq,
                             int T, int H) {
+  grid_dep_launch();
+  grid_dep_wait();
   const int64_t lane = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   if (lane >= static_cast<int64_t>(nseq) * H) return;
   const int64_t q = lane / H, c = lane % H;
@@ -445,15 +456,15 @@ __global__ void scan_kernel(float* __restrict__ out, const float* __restrict__ s
 }
 
 cudaError_t launch_mixer(float* i, float* f, float* recur, float* state, const float* lb,
-                         int nseq, int len, int H, int seg_rows, cudaStream_t s) {
+                         int nseq, int len, int H, int seg_rows, cudaStream_t s, bool pdl) {
   const int64_t n = static_cast<int64_t>(nseq) * len * H;
   if (n == 0) return cudaSuccess;
-  gate_kernel<<<static_cast<unsigned>(ceil_div(n, 256)), 256, 0, s>>>(
-      i, f, lb, n, static_cast<int64_t>(seg_rows) * H, H);
+  cudaError_t e = launch_k(gate_kernel, dim3(static_cast<unsigned>(ceil_div(n, 256))), dim3(256), 0, s,
+                           pdl, i, f, lb, n, static_cast<int64_t>(seg_rows) * H, H);
+  if (e != cudaSuccess) return e;
   const int64_t lanes = static_cast<int64_t>(nseq) * H;
-  scan_kernel<<<static_cast<unsigned>(ceil_div(lanes, 128)), 128, 0, s>>>(recur, i, f, state, nseq,
-                                                                         len, H);
-  return cudaGetLastError();
+  return launch_k(scan_kernel, dim3(static_cast<unsigned>(ceil_div(lanes, 128))), dim3(128), 0, s, pdl,
+                  recur, static_cast<const float*>(i), static_cast<const float*>(f), state, nseq, len, H);
 }
 
 cudaError_t launch_scan(float* out, const float* i, const float* f, int T, int D, float* state,
@@ -466,6 +477,8 @@ cudaError_t launch_scan(float* out, const float* i, const float* f, int T, int D
 // ------------------------------------------------------------------------------ swiglu
 __global__ void swiglu_split_kernel(float* __restrict__ z, const float* __restrict__ y,
                                     int64_t n, int64_t seg, int I) {
+  grid_dep_launch();
+  grid_dep_wait();
   const int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   if (e >= n) return;
   const int64_t t = e / I, c = e % I;
@@ -474,12 +487,11 @@ __global__ void swiglu_split_kernel(float* __restrict__ z, const float* __restri
 }
 
 cudaError_t launch_swiglu_split(float* z, const float* y, int rows, int I, int seg_rows,
-                                cudaStream_t s) {
+                                cudaStream_t s, bool pdl) {
   const int64_t n = static_cast<int64_t>(rows) * I;
   if (n == 0) return cudaSuccess;
-  swiglu_split_kernel<<<static_cast<unsigned>(ceil_div(n, 256)), 256, 0, s>>>(
-      z, y, n, static_cast<int64_t>(seg_rows) * I, I);
-  return cudaGetLastError();
+  return launch_k(swiglu_split_kernel, dim3(static_cast<unsigned>(ceil_div(n, 256))), dim3(256), 0, s,
+                  pdl, z, y, n, static_cast<int64_t>(seg_rows) * I, I);
 }
 
 __global__ void swiglu_kernel(float* __restrict__ out, const float* __restrict__ a,
@@ -601,6 +613,8 @@ cudaError_t launch_argmax(int64_t* ids, const float* logits, int M, int V, int l
 
 __global__ void argmax_at_kernel(int64_t* __restrict__ ids, int64_t stride, int64_t* pos,
                                  unsigned* done, const float* __restrict__ logits, int V, int ld) {
+  grid_dep_launch();
+  grid_dep_wait();
   const int b = blockIdx.x;
   const int best = block_argmax(logits + static_cast<int64_t>(b) * ld, V);
   if (threadIdx.x == 0) {
@@ -615,15 +629,16 @@ __global__ void argmax_at_kernel(int64_t* __restrict__ ids, int64_t stride, int6
 }
 
 cudaError_t launch_argmax_at(int64_t* ids, int64_t stride, int64_t* pos, unsigned* done,
-                             const float* logits, int B, int V, int ld, cudaStream_t s) {
+                             const float* logits, int B, int V, int ld, cudaStream_t s, bool pdl) {
   if (B == 0) return cudaSuccess;
-  argmax_at_kernel<<<B, 1024, 0, s>>>(ids, stride, pos, done, logits, V, ld);
-  return cudaGetLastError();
+  return launch_k(argmax_at_kernel, dim3(B), dim3(1024), 0, s, pdl, ids, stride, pos, done, logits, V, ld);
 }
 
 __global__ void embed_at_kernel(float* __restrict__ h, const float* __restrict__ emb,
                                 const int64_t* __restrict__ ids, int64_t stride,
                                 const int64_t* pos, int H, int V, uint32_t* err) {
+  grid_dep_launch();
+  grid_dep_wait();
   const int b = blockIdx.x;
   const int64_t id = ids[b * stride + *pos];
   const bool ok = id >= 0 && id < V;
@@ -635,10 +650,9 @@ __global__ void embed_at_kernel(float* __restrict__ h, const float* __restrict__
 
 cudaError_t launch_embed_at(float* h, const float* emb, const int64_t* ids, int64_t stride,
                             const int64_t* pos, int B, int H, int V, uint32_t* err,
-                            cudaStream_t s) {
+                            cudaStream_t s, bool pdl) {
   if (B == 0) return cudaSuccess;
-  embed_at_kernel<<<B, 256, 0, s>>>(h, emb, ids, stride, pos, H, V, err);
-  return cudaGetLastError();
+  return launch_k(embed_at_kernel, dim3(B), dim3(256), 0, s, pdl, h, emb, ids, stride, pos, H, V, err);
 }
 
 }  // namespace mmfree_cuda

@@ -29,6 +29,7 @@ struct PrepArgs {
   float eps = 1e-6f;
   float qs = 1024.0f;            // 2^frac_bits
   bool fixed = true;
+  bool pdl = false;              // launch as a programmatic dependent of the previous kernel
 };
 
 struct MatmulArgs {
@@ -124,10 +125,10 @@ cudaError_t launch_matmul(const MatmulArgs& a, cudaStream_t s);
 // SIMD body/tail split is taken over segments of seg_rows * H elements: the rows of one
 // reference block() call.
 cudaError_t launch_mixer(float* i, float* f, float* recur, float* state, const float* lb,
-                         int nseq, int len, int H, int seg_rows, cudaStream_t s);
+                         int nseq, int len, int H, int seg_rows, cudaStream_t s, bool pdl = false);
 // z[t, c] = silu(y[t, c]) * y[t, I + c]  (hgrn_model.cpp:171-185), tails per seg_rows rows.
 cudaError_t launch_swiglu_split(float* z, const float* y, int rows, int I, int seg_rows,
-                                cudaStream_t s);
+                                cudaStream_t s, bool pdl = false);
 // out[n] = silu(a[n]) * b[n]  (activations.cpp:9-15)
 cudaError_t launch_swiglu(float* out, const float* a, const float* b, int64_t n, cudaStream_t s);
 // rmsnorm rows (rmsnorm.cpp:11-22)
@@ -151,8 +152,9 @@ cudaError_t launch_argmax(int64_t* ids, const float* logits, int M, int V, int l
 // logits row b to ids[b * stride + *pos + 1] and the last block to finish advances *pos.
 cudaError_t launch_embed_at(float* h, const float* emb, const int64_t* ids, int64_t stride,
                             const int64_t* pos, int B, int H, int V, uint32_t* err,
-                            cudaStream_t s);
+                            cudaStream_t s, bool pdl = false);
 cudaError_t launch_argmax_at(int64_t* ids, int64_t stride, int64_t* pos, unsigned* done,
-                             const float* logits, int B, int V, int ld, cudaStream_t s);
+                             const float* logits, int B, int V, int ld, cudaStream_t s,
+                             bool pdl = false);
 
 }  // namespace mmfree_cuda

@@ -55,6 +55,8 @@ Model::Model(const std::string& blob_path, int device, bool fixed, int frac_bits
   {
     const char* env = std::getenv("MMFREE_FUSED_DECODE");
     fused_ok_ = !(env && env[0] == '0');
+    const char* penv = std::getenv("MMFREE_PDL");
+    pdl_ = !(penv && penv[0] == '0');
   }
   CK(cudaMalloc(&dec_part_v_, sizeof(float) * kDecMaxRows * 2 * 1024));
   CK(cudaMalloc(&dec_part_i_, sizeof(int) * kDecMaxRows * 2 * 1024));
@@ -308,7 +310,9 @@ void Model::prep(const PrepArgs& p) {
   const double out_row = p.fixed ? 2.0 * padded_k(p.K) + 4 : 4.0 * padded_k(p.K);
   const double bytes = rows * K * 4 * (p.o ? 2 : 1) + K * 4 * (p.nproj + (p.prew ? 1 : 0)) +
                        rows * out_row * p.nproj;
-  timed(kClsPrep, bytes, 0, [&] { CK(launch_prep(p, stream_)); });
+  PrepArgs q = p;
+  q.pdl = pdl_;
+  timed(kClsPrep, bytes, 0, [&] { CK(launch_prep(q, stream_)); });
 }
 
 const char* Model::class_name(int c) {
@@ -338,6 +342,7 @@ void Model::bitlinear(const Proj& p, int plane, float* out, int M, const float* 
   a.tc_tiles = tc_tiles_;
   a.tc_tiles_words = tc_tiles_words_;
   a.err = err_;
+  a.pdl = pdl_;
   // algorithmic bytes (2-bit weights, activations in, outputs out) and 2*M*K*N ops
   const double K = p.in, N = p.out;
   const double bytes = K * N / 4 + 4.0 * M * K + 4.0 * M * N * (resid ? 2 : 1);
@@ -373,7 +378,7 @@ void Model::layers(int nseq, int len, int seg_rows, StateFn state) {
     bitlinear(ly.p[kF], 1, fb_, rows, nullptr);
     bitlinear(ly.p[kG], 2, gb_, rows, nullptr);
     timed(kClsMixer, 4.0 * rows * H_ * 5 + 8.0 * nseq * H_, 0, [&] {
-      CK(launch_mixer(ib_, fb_, recur_, state(l), ly.lb, nseq, len, H_, seg_rows, stream_));
+      CK(launch_mixer(ib_, fb_, recur_, state(l), ly.lb, nseq, len, H_, seg_rows, stream_, pdl_));
     });
     // o_proj on g_norm(g) * silu(recurrence); resid = h + o
     p.x = gb_;
@@ -391,7 +396,7 @@ void Model::layers(int nseq, int len, int seg_rows, StateFn state) {
     prep(p);
     bitlinear(ly.p[kGate], 0, y_, rows, nullptr);
     timed(kClsSwiglu, 12.0 * rows * I_, 0,
-          [&] { CK(launch_swiglu_split(z_, y_, rows, I_, seg_rows, stream_)); });
+          [&] { CK(launch_swiglu_split(z_, y_, rows, I_, seg_rows, stream_, pdl_)); });
     p.x = z_;
     p.prew = nullptr;
     p.K = I_;
@@ -451,7 +456,7 @@ void Model::head(const float* rows, int M) {
 
 void Model::decode_graph_step(int B, int64_t stride) {
   timed(kClsEmbed, 8.0 * B * H_, 0, [&] {
-    CK(launch_embed_at(h_, emb_, loop_ids_, stride, pos_, B, H_, V_, err_, stream_));
+    CK(launch_embed_at(h_, emb_, loop_ids_, stride, pos_, B, H_, V_, err_, stream_, pdl_));
   });
   if (fused_decode(B)) {
     fused_step(B, stride);
@@ -460,7 +465,7 @@ void Model::decode_graph_step(int B, int64_t stride) {
   layers(B, 1, B, [&](int l) { return state_ + static_cast<size_t>(l) * B * H_; });
   head(h_, B);
   timed(kClsArgmax, 4.0 * B * V_, 0, [&] {
-    CK(launch_argmax_at(loop_ids_, stride, pos_, done_, logits_, B, V_, V_, stream_));
+    CK(launch_argmax_at(loop_ids_, stride, pos_, done_, logits_, B, V_, V_, stream_, pdl_));
   });
 }
 

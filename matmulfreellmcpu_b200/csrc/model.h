@@ -111,6 +111,7 @@ class Model {
   void fused_step(int B, int64_t stride);
   int sms_ = 148;
   bool fused_ok_ = true;           // MMFREE_FUSED_DECODE=0 selects the unfused decode step
+  bool pdl_ = true;                // MMFREE_PDL=0: plain stream order between kernels
   float* dec_part_v_ = nullptr;    // fused head: per-CTA argmax partials
   int* dec_part_i_ = nullptr;
 
