@@ -17,11 +17,21 @@
 // grid-wide synchronisation is needed. The arithmetic is that of exact.cuh / kernels.cu
 // (bit-identical to the reference in FixedQ510).
 //
-// Launches use programmatic dependent launch. Everything a kernel needs that its
-// predecessor does not produce -- the weights of its first unit (into registers), its norm
-// weights (into shared memory), the lower bounds and recurrent state of its columns, an L2
-// prefetch of its other weights -- is fetched before griddepcontrol.wait, while the
-// predecessor still runs; after the wait only the activation rows are read.
+// Two drivers run the same phase body (dec_body):
+//   dec_kernel          one launch per phase, as a programmatic dependent of the previous
+//                       launch. Everything a phase needs that its predecessor does not produce
+//                       -- the weights of its first unit (bulk-copied into shared memory), its
+//                       norm weights, the lower bounds and recurrent state of its columns, an L2
+//                       prefetch of its other weights -- is fetched before griddepcontrol.wait;
+//                       after the wait only the activation rows are read.
+//   dec_persist_kernel  the whole decode step (every layer's four phases and the head) in one
+//                       cooperative launch of one CTA per SM. Between phases a split grid
+//                       barrier: a CTA arrives when its part of phase p is written and waits
+//                       for all arrivals only after staging phase p+1's weights, so the staging
+//                       overlaps the other CTAs' tail of phase p. Each phase also starts an L2
+//                       prefetch of the next phase's weights. Data written inside the launch is
+//                       read through L2 only (ld.global.cg): the L1 caches of other SMs are not
+//                       coherent with it.
 #include "common.cuh"
 #include "exact.cuh"
 #include "kernels.h"
@@ -40,6 +50,7 @@ __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
 }
 
 constexpr uint32_t kStageSpin = 1u << 24;  // bounded wait for the staged weights
+constexpr uint32_t kBarSpin = 1u << 22;    // bounded wait at a grid barrier (a phase takes microseconds)
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -66,9 +77,28 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
 
 }  // namespace
 
-template <int MT, int NP, int NW, int PRO, int EPI>
-__global__ void __launch_bounds__(kDecThreads) dec_kernel(DecArgs a) {
-  extern __shared__ __align__(16) unsigned char dsm[];
+// L2 prefetch of the weights a CTA will read in phase n
+__device__ __forceinline__ void prefetch_phase(const DecArgs& n, int cta, int ncta) {
+  const int64_t kc = packed_chunks(n.K);
+  const uint32_t gbytes = static_cast<uint32_t>(kc * kChunkBytes);
+  const int ngroups = static_cast<int>(packed_groups(n.N));
+  const bool pair = n.epi == kDecEpiSwiglu;
+  const int units = pair ? ngroups / 2 : ngroups;
+  const int nw = n.epi == kDecEpiMixer ? 3 : (pair ? 2 : 1);
+  for (int u = cta; u < units; u += ncta)
+    for (int j = 0; j < nw; ++j) {
+      const int g = pair ? u + j * (ngroups / 2) : u;
+      const void* wj = pair ? n.w[0] : n.w[j];
+      prefetch_l2(static_cast<const unsigned char*>(wj) + static_cast<int64_t>(g) * gbytes, gbytes);
+    }
+}
+
+// One phase for CTA `cta` of `ncta`: units cta, cta + ncta, ... `wait` is called by every
+// thread once the phase's constants are staged; it returns false when the step must stop.
+// Returns false when it stopped.
+template <int MT, int NP, int NW, int PRO, int EPI, class Wait>
+__device__ __forceinline__ bool dec_body(const DecArgs& a, int cta, int ncta, unsigned char* dsm,
+                                         const DecArgs* next, Wait&& wait) {
   const int K = a.K, M = a.M, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t kc = packed_chunks(K), kp = kc * kChunkK;
   const int K4 = (K + 3) & ~3;
@@ -92,7 +122,7 @@ __global__ void __launch_bounds__(kDecThreads) dec_kernel(DecArgs a) {
 
   // ---- 1. independent of the predecessor: first-unit weights (bulk copy into shared memory),
   //         L2 prefetch of the other units, norm weights, lower bounds and state
-  const int u0 = blockIdx.x;
+  const int u0 = cta;
   const bool stage = a.stage && u0 < units;
   uint4* wst = reinterpret_cast<uint4*>(red + kDecWarps * NW * MT * 32);  // [NW][kc][32] uint4
   __shared__ __align__(8) uint64_t s_bar;
@@ -109,8 +139,9 @@ __global__ void __launch_bounds__(kDecThreads) dec_kernel(DecArgs a) {
     } else if (u0 < units) {
       for (int j = 0; j < NW; ++j) prefetch_l2(wrow(u0, j) - lane, gbytes);
     }
-    for (int u = u0 + gridDim.x; u < units; u += gridDim.x)
+    for (int u = u0 + ncta; u < units; u += ncta)
       for (int j = 0; j < NW; ++j) prefetch_l2(wrow(u, j) - lane, gbytes);
+    if (next) prefetch_phase(*next, cta, ncta);
   }
   {
     int slot = 0;
@@ -127,19 +158,34 @@ __global__ void __launch_bounds__(kDecThreads) dec_kernel(DecArgs a) {
     if (n < a.N) {
       if (a.lb) lb_pre = __ldg(a.lb + n);
 #pragma unroll
-      for (int t = 0; t < MT; ++t) st_pre[t] = t < M ? a.state[static_cast<int64_t>(t) * a.N + n] : 0.0f;
+      for (int t = 0; t < MT; ++t) st_pre[t] = t < M ? __ldcg(a.state + static_cast<int64_t>(t) * a.N + n) : 0.0f;
     }
   }
 
   // ---- 2. the predecessor's outputs are needed from here on
-  grid_dep_wait();
-  grid_dep_launch();
+  if (!wait()) {
+    if (stage)  // let the staged copy land before the CTA moves on
+      for (uint32_t i = 0; i < kStageSpin && !mbar_test(&s_bar, 0); ++i) {
+      }
+    return false;
+  }
 
-  // ---- 3. prologue: rows into shared memory, exact norms, Q5.10 byte planes
+  // ---- 3. prologue: rows into shared memory (or gathered from the embedding table), exact
+  //         norms, Q5.10 byte planes
   for (int t = 0; t < MT; ++t) {
     const int tr = t < M ? t : M - 1;
     const float* xr = a.x + static_cast<int64_t>(tr) * K;
-    for (int c = tid; c < K; c += kDecThreads) xs[t * K4 + c] = __ldcg(xr + c);
+    if (a.xids) {  // the step's first phase: x = embedding row of the current token
+      const int64_t id = a.xids[tr * a.xstride + *a.xpos];
+      const bool ok = id >= 0 && id < a.V;
+      if (!ok && tid == 0 && a.err) atomicOr(a.err, kErrBadToken);
+      xr = ok ? a.x + id * K : nullptr;
+    }
+    for (int c = tid; c < K; c += kDecThreads) {
+      const float v = xr ? (a.xids ? __ldg(xr + c) : __ldcg(xr + c)) : 0.0f;
+      xs[t * K4 + c] = v;
+      if (a.xcopy && cta == 0 && t < M) a.xcopy[static_cast<int64_t>(t) * K + c] = v;
+    }
   }
   __syncthreads();
   const int myrow = (lane >> 3) < MT ? (lane >> 3) : MT - 1;  // warp 0: 8 lanes per row
@@ -213,7 +259,7 @@ __global__ void __launch_bounds__(kDecThreads) dec_kernel(DecArgs a) {
 #pragma unroll
   for (int t = 0; t < MT; ++t) { best_v[t] = -FLT_MAX; best_i[t] = 0x7fffffff; }
 
-  for (int u = u0; u < units; u += gridDim.x) {
+  for (int u = u0; u < units; u += ncta) {
     int acc_hi[NW][MT][4], acc_lo[NW][MT][4];
 #pragma unroll
     for (int j = 0; j < NW; ++j)
@@ -294,7 +340,7 @@ __global__ void __launch_bounds__(kDecThreads) dec_kernel(DecArgs a) {
             float fv = sigmoid_x(fr, body);
             if (a.lb) fv = lower_bound_x(fv, first ? lb_pre : __ldg(a.lb + n));
             const float sv = swiglu_x(iv, __fadd_rn(1.0f, -fv), body);
-            const float st = hgrn_step_x(fv, first ? st_pre[t] : a.state[e], sv);
+            const float st = hgrn_step_x(fv, first ? st_pre[t] : __ldcg(a.state + e), sv);
             a.state[e] = st;
             a.out[0][e] = st;  // recurrence output
             a.out[1][e] = gv;  // g_proj output (normed by K2)
@@ -339,14 +385,14 @@ __global__ void __launch_bounds__(kDecThreads) dec_kernel(DecArgs a) {
           if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
         }
         if (lane == 0) {
-          a.part_v[static_cast<int64_t>(blockIdx.x) * MT + t] = bv;
-          a.part_i[static_cast<int64_t>(blockIdx.x) * MT + t] = bi;
+          a.part_v[static_cast<int64_t>(cta) * MT + t] = bv;
+          a.part_i[static_cast<int64_t>(cta) * MT + t] = bi;
         }
       }
     }
     __threadfence();
     __syncthreads();
-    if (tid == 0) s_last = atomicAdd(a.done, 1u) == gridDim.x - 1;
+    if (tid == 0) s_last = atomicAdd(a.done, 1u) == static_cast<unsigned>(ncta) - 1;
     __syncthreads();
     if (s_last && warp == 0) {
       __threadfence();
@@ -354,7 +400,7 @@ __global__ void __launch_bounds__(kDecThreads) dec_kernel(DecArgs a) {
       for (int t = 0; t < M && t < MT; ++t) {
         float bv = -FLT_MAX;
         int bi = 0x7fffffff;
-        for (int c = lane; c < static_cast<int>(gridDim.x); c += 32) {
+        for (int c = lane; c < ncta; c += 32) {
           const float ov = __ldcg(a.part_v + static_cast<int64_t>(c) * MT + t);
           const int oi = __ldcg(a.part_i + static_cast<int64_t>(c) * MT + t);
           if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
@@ -377,43 +423,121 @@ __global__ void __launch_bounds__(kDecThreads) dec_kernel(DecArgs a) {
       }
     }
   }
+  return true;
+}
+
+template <int MT, int NP, int NW, int PRO, int EPI>
+__global__ void __launch_bounds__(kDecThreads) dec_kernel(DecArgs a) {
+  extern __shared__ __align__(16) unsigned char dsm[];
+  dec_body<MT, NP, NW, PRO, EPI>(a, blockIdx.x, gridDim.x, dsm, nullptr, [] {
+    grid_dep_wait();
+    grid_dep_launch();
+    return true;
+  });
+}
+
+// The whole decode step in one cooperative launch (phase table in device memory).
+template <int MT>
+__global__ void __launch_bounds__(kDecThreads, 1) dec_persist_kernel(const DecArgs* __restrict__ phases,
+                                                                     int nphases, unsigned* bar,
+                                                                     uint32_t* err) {
+  extern __shared__ __align__(16) unsigned char dsm[];
+  __shared__ unsigned s_ok;
+  const int cta = blockIdx.x, ncta = gridDim.x;
+  for (int ph = 0; ph < nphases; ++ph) {
+    const DecArgs a = phases[ph];
+    const DecArgs* next = ph + 1 < nphases ? &phases[ph + 1] : nullptr;
+    // phase ph may start once every CTA has finished phase ph - 1
+    auto wait = [&]() -> bool {
+      if (ph == 0) return true;  // inputs come from earlier launches
+      if (threadIdx.x == 0) {
+        const unsigned target = static_cast<unsigned>(ncta) * static_cast<unsigned>(ph);
+        unsigned v = 0;
+        for (uint32_t i = 0; i < kBarSpin; ++i) {
+          asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
+          if (v >= target) break;
+        }
+        s_ok = v >= target;
+        if (!s_ok && err) atomicOr(err, kErrTimeout);
+        __threadfence();
+      }
+      __syncthreads();
+      return s_ok != 0;
+    };
+    bool ok;
+    if (a.epi == kDecEpiMixer)
+      ok = dec_body<MT, 3, 3, kDecProNorm2, kDecEpiMixer>(a, cta, ncta, dsm, next, wait);
+    else if (a.epi == kDecEpiSwiglu)
+      ok = dec_body<MT, 1, 2, kDecProNorm2, kDecEpiSwiglu>(a, cta, ncta, dsm, next, wait);
+    else if (a.epi == kDecEpiLogits)
+      ok = dec_body<MT, 1, 1, kDecProNorm2, kDecEpiLogits>(a, cta, ncta, dsm, next, wait);
+    else if (a.pro == kDecProSwish)
+      ok = dec_body<MT, 1, 1, kDecProSwish, kDecEpiResid>(a, cta, ncta, dsm, next, wait);
+    else
+      ok = dec_body<MT, 1, 1, kDecProPlain, kDecEpiResid>(a, cta, ncta, dsm, next, wait);
+    if (!ok) return;  // a barrier timed out (error flag set): every CTA stops
+    // arrive: this CTA's part of phase ph is written
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      atomicAdd(bar, 1u);
+    }
+  }
+}
+
+constexpr size_t kDecSmemMax = 224 * 1024;
+
+// Shared memory of one phase (rows, norm weights, planes, reduction) and of its staged unit.
+struct DecSmem {
+  size_t base, staged;
+};
+static DecSmem dec_smem(int K, int MT, int NP, int NW, int PRO) {
+  const int64_t kp = padded_k(K);
+  const int K4 = (K + 3) & ~3;
+  const int norms = (PRO == kDecProPlain ? 0 : 1) + NP;
+  DecSmem d;
+  d.base = static_cast<size_t>(MT + norms) * K4 * 4 + static_cast<size_t>(NP) * MT * 2 * kp +
+           static_cast<size_t>(kDecWarps) * NW * MT * 32 * 4;
+  d.staged = static_cast<size_t>(NW) * kp / kChunkK * kChunkBytes;
+  return d;
+}
+static void dec_shape(int pro, int epi, int* np, int* nw, int* pr) {
+  if (epi == kDecEpiMixer) { *np = 3; *nw = 3; *pr = kDecProNorm2; }
+  else if (epi == kDecEpiSwiglu) { *np = 1; *nw = 2; *pr = kDecProNorm2; }
+  else if (epi == kDecEpiLogits) { *np = 1; *nw = 1; *pr = kDecProNorm2; }
+  else { *np = 1; *nw = 1; *pr = pro == kDecProSwish ? kDecProSwish : kDecProPlain; }
+}
+static int dec_mt(int M) { return M == 1 ? 1 : (M == 2 ? 2 : 4); }
+
+// raise a kernel's dynamic shared memory limit to `smem` (once per device and size)
+template <class K>
+static cudaError_t dec_smem_attr(K kernel, size_t smem, size_t (&cache)[64]) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (smem > 48 * 1024 && smem > cache[dev & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    cache[dev & 63] = smem;
+  }
+  return cudaSuccess;
 }
 
 template <int MT, int NP, int NW, int PRO, int EPI>
 static cudaError_t launch_dec_t(const DecArgs& a, int grid, cudaStream_t s, bool pdl) {
-  const int64_t kp = padded_k(a.K);
-  const int K4 = (a.K + 3) & ~3;
-  constexpr int kNorms = (PRO == kDecProPlain ? 0 : 1) + NP;
-  size_t smem = static_cast<size_t>(MT + kNorms) * K4 * 4 + static_cast<size_t>(NP) * MT * 2 * kp +
-                static_cast<size_t>(kDecWarps) * NW * MT * 32 * 4;
-  if (smem > 224 * 1024) return cudaErrorInvalidValue;
+  const DecSmem d = dec_smem(a.K, MT, NP, NW, PRO);
+  if (d.base > kDecSmemMax) return cudaErrorInvalidValue;
   // stage the first unit's weights in shared memory when they fit
   DecArgs b = a;
-  const size_t staged = static_cast<size_t>(NW) * padded_k(a.K) / kChunkK * kChunkBytes;
-  b.stage = smem + staged <= 224 * 1024 ? 1 : 0;
-  if (b.stage) smem += staged;
-  // the opt-in limit covers static + dynamic shared memory: raise it to what this launch needs
-  static size_t attr[64] = {0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (smem > 48 * 1024 && smem > attr[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(dec_kernel<MT, NP, NW, PRO, EPI>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
-    attr[dev & 63] = smem;
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(grid));
-  cfg.blockDim = dim3(kDecThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cudaLaunchAttribute attrs[1];
-  attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attrs[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attrs;
-  cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, dec_kernel<MT, NP, NW, PRO, EPI>, b);
+  b.pro = PRO;
+  b.epi = EPI;
+  b.stage = d.base + d.staged <= kDecSmemMax ? 1 : 0;
+  const size_t smem = d.base + (b.stage ? d.staged : 0);
+  static size_t cache[64] = {0};
+  cudaError_t e = dec_smem_attr(dec_kernel<MT, NP, NW, PRO, EPI>, smem, cache);
+  if (e != cudaSuccess) return e;
+  return launch_k(dec_kernel<MT, NP, NW, PRO, EPI>, dim3(static_cast<unsigned>(grid)), dim3(kDecThreads),
+                  smem, s, pdl, b);
 }
 
 // units of work (the launcher uses at most two CTAs per SM)
@@ -438,6 +562,88 @@ cudaError_t launch_dec(const DecArgs& a, int pro, int epi, int grid, cudaStream_
   if (a.M == 2) return launch_dec_mt<2>(a, pro, epi, grid, s, pdl);
   if (a.M <= 4) return launch_dec_mt<4>(a, pro, epi, grid, s, pdl);
   return cudaErrorInvalidValue;
+}
+
+// ---- persistent decode step
+
+size_t dec_persist_plan(DecArgs* phases, int n) {
+  if (n <= 0) return 0;
+  const int MT = dec_mt(phases[0].M);
+  size_t need = 0;
+  for (int i = 0; i < n; ++i) {  // rows, norms, planes of every phase must fit
+    int np, nw, pr;
+    dec_shape(phases[i].pro, phases[i].epi, &np, &nw, &pr);
+    phases[i].pro = pr;
+    const DecSmem d = dec_smem(phases[i].K, MT, np, nw, pr);
+    if (d.base > kDecSmemMax || phases[i].M != phases[0].M) return 0;
+    need = d.base > need ? d.base : need;
+  }
+  size_t smem = need;
+  for (int i = 0; i < n; ++i) {  // stage first units where the largest phase leaves room
+    int np, nw, pr;
+    dec_shape(phases[i].pro, phases[i].epi, &np, &nw, &pr);
+    const DecSmem d = dec_smem(phases[i].K, MT, np, nw, pr);
+    phases[i].stage = d.base + d.staged <= kDecSmemMax ? 1 : 0;
+    if (phases[i].stage && d.base + d.staged > smem) smem = d.base + d.staged;
+  }
+  return smem;
+}
+
+template <int MT>
+static cudaError_t persist_mt(const DecArgs* dev_phases, int n, unsigned* bar, uint32_t* err,
+                              size_t smem, int* grid, bool launch, cudaStream_t s) {
+  static size_t cache[64] = {0};
+  cudaError_t e = dec_smem_attr(dec_persist_kernel<MT>, smem, cache);
+  if (e != cudaSuccess) return e;
+  if (!launch) {  // one CTA per SM, all co-resident (the CTAs wait on one another)
+    int dev = 0, sms = 0, coop = 0, per_sm = 0;
+    cudaGetDevice(&dev);
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev)) != cudaSuccess) return e;
+    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, dec_persist_kernel<MT>, kDecThreads,
+                                                           smem)) != cudaSuccess)
+      return e;
+    *grid = coop && per_sm >= 1 ? sms : 0;
+    return cudaSuccess;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(*grid));
+  cfg.blockDim = dim3(kDecThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeCooperative;
+  at[0].val.cooperative = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, dec_persist_kernel<MT>, dev_phases, n, bar, err);
+}
+
+static cudaError_t persist_dispatch(int M, const DecArgs* dev_phases, int n, unsigned* bar,
+                                    uint32_t* err, size_t smem, int* grid, bool launch, cudaStream_t s) {
+  switch (dec_mt(M)) {
+    case 1: return persist_mt<1>(dev_phases, n, bar, err, smem, grid, launch, s);
+    case 2: return persist_mt<2>(dev_phases, n, bar, err, smem, grid, launch, s);
+    default: return persist_mt<4>(dev_phases, n, bar, err, smem, grid, launch, s);
+  }
+}
+
+int dec_persist_grid(int M, size_t smem) {
+  if (M < 1 || M > kDecMaxRows || smem == 0) return 0;
+  int grid = 0;
+  if (persist_dispatch(M, nullptr, 0, nullptr, nullptr, smem, &grid, false, nullptr) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return grid;
+}
+
+cudaError_t launch_dec_persist(const DecArgs* dev_phases, int nphases, int M, unsigned* bar,
+                               uint32_t* err, size_t smem, int grid, cudaStream_t s) {
+  if (grid <= 0 || nphases <= 0) return cudaErrorInvalidValue;
+  cudaError_t e = cudaMemsetAsync(bar, 0, sizeof(unsigned), s);
+  if (e != cudaSuccess) return e;
+  return persist_dispatch(M, dev_phases, nphases, bar, err, smem, &grid, true, s);
 }
 
 }  // namespace mmfree_cuda

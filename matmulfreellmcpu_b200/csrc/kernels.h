@@ -73,7 +73,7 @@ enum DecEpi : int {
 constexpr int kDecMaxRows = 4;
 
 struct DecArgs {
-  const float* x = nullptr;       // [M, K]
+  const float* x = nullptr;       // [M, K] (or the embedding table [V, K] when xids is set)
   const float* o = nullptr;       // [M, K] recurrence output (kDecProSwish)
   const float* prew = nullptr;    // [K] first norm weight
   const float* normw[3] = {};     // projection norm weights [K]
@@ -92,10 +92,27 @@ struct DecArgs {
   unsigned* done = nullptr;
   float* part_v = nullptr;        // logits: per-CTA partial maxima [grid][kDecMaxRows]
   int* part_i = nullptr;
+  // x gathered from the embedding table: row t is x[xids[t * xstride + *xpos]]; CTA 0 also
+  // writes the rows to xcopy. Ids outside [0, V) set kErrBadToken in *err (zero row).
+  const int64_t* xids = nullptr;
+  int64_t xstride = 0;
+  const int64_t* xpos = nullptr;
+  float* xcopy = nullptr;
+  int V = 0;
+  uint32_t* err = nullptr;
+  int pro = 0, epi = 0;           // phase kind (DecPro, DecEpi)
   int stage = 0;                  // set by the launcher: first unit staged in shared memory
 };
 int dec_units(const DecArgs& a, int epi);
 cudaError_t launch_dec(const DecArgs& a, int pro, int epi, int grid, cudaStream_t s, bool pdl);
+// The persistent decode step: a table of phases (pro/epi set) run by one cooperative launch.
+// dec_persist_plan sets each phase's staging flag and returns the dynamic shared memory
+// (0: some phase does not fit); dec_persist_grid returns the CTA count (one per SM, 0 when a
+// cooperative launch of that size is impossible). The barrier word is zeroed by the launcher.
+size_t dec_persist_plan(DecArgs* phases, int n);
+int dec_persist_grid(int M, size_t smem);
+cudaError_t launch_dec_persist(const DecArgs* dev_phases, int nphases, int M, unsigned* bar,
+                               uint32_t* err, size_t smem, int grid, cudaStream_t s);
 
 // tcgen05 BitLinear matmul (tc_matmul.cu)
 int tc_token_tile(int M);

@@ -57,6 +57,8 @@ Model::Model(const std::string& blob_path, int device, bool fixed, int frac_bits
     fused_ok_ = !(env && env[0] == '0');
     const char* penv = std::getenv("MMFREE_PDL");
     pdl_ = !(penv && penv[0] == '0');
+    const char* cenv = std::getenv("MMFREE_PERSIST");
+    persist_ok_ = cenv && cenv[0] == '1';
   }
   CK(cudaMalloc(&dec_part_v_, sizeof(float) * kDecMaxRows * 2 * 1024));
   CK(cudaMalloc(&dec_part_i_, sizeof(int) * kDecMaxRows * 2 * 1024));
@@ -64,6 +66,7 @@ Model::Model(const std::string& blob_path, int device, bool fixed, int frac_bits
   CK(cudaMemsetAsync(err_, 0, 64, stream_));
   pos_ = reinterpret_cast<int64_t*>(reinterpret_cast<char*>(err_) + 8);
   done_ = reinterpret_cast<unsigned*>(reinterpret_cast<char*>(err_) + 16);
+  persist_bar_ = reinterpret_cast<unsigned*>(reinterpret_cast<char*>(err_) + 24);
 
   // ---- fp32 tensors: one arena
   struct FpItem { std::string name; size_t n; const float** dst; };
@@ -177,6 +180,7 @@ Model::~Model() {
   cudaFree(err_);
   cudaFree(dec_part_v_);
   cudaFree(dec_part_i_);
+  cudaFree(persist_tab_);
   if (pinned_) cudaFreeHost(pinned_);
   if (stream_) cudaStreamDestroy(stream_);
 }
@@ -186,6 +190,8 @@ void Model::drop_graph() {
   graph_ = nullptr;
   graph_b_ = 0;
   graph_stride_ = 0;
+  persist_b_ = 0;  // the persistent phase table holds buffer pointers: rebuild it
+  persist_stride_ = -1;
 }
 
 void Model::ensure_ws(size_t rows) {
@@ -317,7 +323,7 @@ void Model::prep(const PrepArgs& p) {
 
 const char* Model::class_name(int c) {
   static const char* n[kNumClasses] = {"prep", "bitlinear_matmul", "lm_head_matmul", "mixer",
-                                       "swiglu", "embed", "argmax"};
+                                       "swiglu", "embed", "argmax", "decode_step"};
   return (c >= 0 && c < kNumClasses) ? n[c] : "?";
 }
 
@@ -455,6 +461,15 @@ void Model::head(const float* rows, int M) {
 }
 
 void Model::decode_graph_step(int B, int64_t stride) {
+  if (fused_decode(B) && persist_ok_ && persist_b_ == B && persist_stride_ == stride &&
+      persist_grid_ > 0) {
+    // the whole step in one cooperative launch (table prepared by persist_ready)
+    timed(kClsStep, static_cast<double>(packed_bytes_), 0, [&] {
+      CK(launch_dec_persist(persist_tab_, persist_n_, B, persist_bar_, err_, persist_smem_,
+                            persist_grid_, stream_));
+    });
+    return;
+  }
   timed(kClsEmbed, 8.0 * B * H_, 0, [&] {
     CK(launch_embed_at(h_, emb_, loop_ids_, stride, pos_, B, H_, V_, err_, stream_, pdl_));
   });
@@ -473,24 +488,20 @@ bool Model::fused_decode(int B) const {
   return fixed_ && fused_ok_ && B <= kDecMaxRows && I_ % 32 == 0;
 }
 
-// One decode step of B <= 4 streams with the fused kernels of decode.cu: four launches per
-// layer plus the head, each launched as a programmatic dependent of the previous one.
-void Model::fused_step(int B, int64_t stride) {
-  auto dec = [&](DecArgs& a, int pro, int epi, int cls, double wbytes) {
-    const int units = dec_units(a, epi);
-    const int grid = std::max(1, std::min(units, 2 * sms_));
+std::vector<DecArgs> Model::dec_phases(int B, int64_t stride) {
+  std::vector<DecArgs> ph;
+  auto base = [&](DecArgs& a, int pro, int epi) {
     a.M = B;
     a.eps = eps_;
     a.qs = qs_;
-    const double bytes = wbytes + 4.0 * B * a.K * (pro == kDecProSwish ? 2 : 1) + 4.0 * B * a.N;
-    const double ops = 2.0 * B * a.K * a.N * (epi == kDecEpiMixer ? 3 : 1);
-    timed(cls, bytes, ops, [&] { CK(launch_dec(a, pro, epi, grid, stream_, true)); });
+    a.pro = pro;
+    a.epi = epi;
   };
-  auto wb = [](const Proj& p) { return static_cast<double>(packed_bytes(p.out, p.in)); };
   const size_t BH = static_cast<size_t>(B) * H_;
   for (int l = 0; l < L_; ++l) {
     const Layer& ly = layers_[l];
-    DecArgs k1;
+    DecArgs k1;  // i/f/g + mixer: attn rmsnorm, recurrence step (hgrn_model.cpp:95-150)
+    base(k1, kDecProNorm2, kDecEpiMixer);
     k1.x = h_;
     k1.prew = ly.attn_norm;
     for (int j = 0; j < 3; ++j) {
@@ -505,9 +516,10 @@ void Model::fused_step(int B, int64_t stride) {
     k1.state = state_ + static_cast<size_t>(l) * BH;
     k1.lb = ly.lb;
     k1.seg = static_cast<int64_t>(BH);
-    dec(k1, kDecProNorm2, kDecEpiMixer, kClsMatmul, wb(ly.p[kI]) + wb(ly.p[kF]) + wb(ly.p[kG]));
+    ph.push_back(k1);
 
-    DecArgs k2;
+    DecArgs k2;  // o_proj on g_norm(g) * silu(recurrence); resid = h + o (:152-166)
+    base(k2, kDecProSwish, kDecEpiResid);
     k2.x = gb_;
     k2.o = recur_;
     k2.prew = ly.g_norm;
@@ -518,9 +530,10 @@ void Model::fused_step(int B, int64_t stride) {
     k2.N = H_;
     k2.out[0] = resid_;
     k2.resid = h_;
-    dec(k2, kDecProSwish, kDecEpiResid, kClsMatmul, wb(ly.p[kO]));
+    ph.push_back(k2);
 
-    DecArgs k3;
+    DecArgs k3;  // gate_proj on mlp rmsnorm(resid), swiglu (:168-185)
+    base(k3, kDecProNorm2, kDecEpiSwiglu);
     k3.x = resid_;
     k3.prew = ly.mlp_norm;
     k3.normw[0] = ly.p[kGate].normw;
@@ -530,9 +543,10 @@ void Model::fused_step(int B, int64_t stride) {
     k3.N = 2 * I_;
     k3.out[0] = z_;
     k3.seg = static_cast<int64_t>(B) * I_;
-    dec(k3, kDecProNorm2, kDecEpiSwiglu, kClsMatmul, wb(ly.p[kGate]));
+    ph.push_back(k3);
 
-    DecArgs k4;
+    DecArgs k4;  // down_proj; h = resid + down (:187-194)
+    base(k4, kDecProPlain, kDecEpiResid);
     k4.x = z_;
     k4.normw[0] = ly.p[kDown].normw;
     k4.w[0] = ly.p[kDown].w;
@@ -541,9 +555,10 @@ void Model::fused_step(int B, int64_t stride) {
     k4.N = H_;
     k4.out[0] = h_;
     k4.resid = resid_;
-    dec(k4, kDecProPlain, kDecEpiResid, kClsMatmul, wb(ly.p[kDown]));
+    ph.push_back(k4);
   }
-  DecArgs hd;
+  DecArgs hd;  // final norm + lm_head + greedy argmax (:304-310, :269-273)
+  base(hd, kDecProNorm2, kDecEpiLogits);
   hd.x = h_;
   hd.prew = final_norm_;
   hd.normw[0] = lm_head_.normw;
@@ -558,7 +573,52 @@ void Model::fused_step(int B, int64_t stride) {
   hd.done = done_;
   hd.part_v = dec_part_v_;
   hd.part_i = dec_part_i_;
-  dec(hd, kDecProNorm2, kDecEpiLogits, kClsLmHead, wb(lm_head_));
+  ph.push_back(hd);
+  return ph;
+}
+
+bool Model::persist_ready(int B, int64_t stride) {
+  if (!fused_decode(B) || !persist_ok_) return false;
+  if (persist_b_ == B && persist_stride_ == stride) return persist_grid_ > 0;
+  std::vector<DecArgs> ph = dec_phases(B, stride);
+  // the first phase gathers its rows from the embedding table (and writes h for o_proj)
+  ph[0].x = emb_;
+  ph[0].xids = loop_ids_;
+  ph[0].xstride = stride;
+  ph[0].xpos = pos_;
+  ph[0].xcopy = h_;
+  ph[0].V = V_;
+  ph[0].err = err_;
+  const size_t smem = dec_persist_plan(ph.data(), static_cast<int>(ph.size()));
+  const int grid = smem ? dec_persist_grid(B, smem) : 0;
+  if (grid > 2 * 1024) throw std::logic_error("persistent decode: grid above the partials buffer");
+  CK(cudaStreamSynchronize(stream_));
+  cudaFree(persist_tab_);
+  persist_tab_ = nullptr;
+  if (grid > 0) {
+    CK(cudaMalloc(&persist_tab_, ph.size() * sizeof(DecArgs)));
+    CK(cudaMemcpy(persist_tab_, ph.data(), ph.size() * sizeof(DecArgs), cudaMemcpyHostToDevice));
+  }
+  persist_n_ = static_cast<int>(ph.size());
+  persist_smem_ = smem;
+  persist_grid_ = grid;
+  persist_b_ = B;
+  persist_stride_ = stride;
+  return grid > 0;
+}
+
+// One decode step of B <= 4 streams with the fused kernels of decode.cu, one launch per
+// phase, each launched as a programmatic dependent of the previous one.
+void Model::fused_step(int B, int64_t stride) {
+  for (DecArgs& a : dec_phases(B, stride)) {
+    const int units = dec_units(a, a.epi);
+    const int grid = std::max(1, std::min(units, 2 * sms_));
+    const double wbytes = static_cast<double>(packed_bytes(a.N, a.K)) * (a.epi == kDecEpiMixer ? 3 : 1);
+    const double bytes = wbytes + 4.0 * B * a.K * (a.pro == kDecProSwish ? 2 : 1) + 4.0 * B * a.N;
+    const double ops = 2.0 * B * a.K * a.N * (a.epi == kDecEpiMixer ? 3 : 1);
+    timed(a.epi == kDecEpiLogits ? kClsLmHead : kClsMatmul, bytes, ops,
+          [&] { CK(launch_dec(a, a.pro, a.epi, grid, stream_, true)); });
+  }
 }
 
 std::vector<Model::ClassStats> Model::serve_profile(size_t steps) {
@@ -571,6 +631,7 @@ std::vector<Model::ClassStats> Model::serve_profile(size_t steps) {
                        stream_));
   CK(cudaMemcpyAsync(pos_, &zero, 8, cudaMemcpyHostToDevice, stream_));
   marks_.clear();
+  persist_ready(B, stride);
   prof_on_ = true;
   try {
     for (size_t s = 0; s < steps; ++s) decode_graph_step(B, stride);
@@ -683,6 +744,7 @@ std::vector<int64_t> Model::generate(const int64_t* ids, size_t n, size_t new_to
     drop_graph();
     CK(cudaStreamSynchronize(stream_));
     cudaGraph_t g;
+    persist_ready(1, stride);
     CK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
     decode_graph_step(1, stride);
     CK(cudaStreamEndCapture(stream_, &g));
@@ -785,6 +847,7 @@ void Model::serve_step(const int64_t* in_ids, int64_t* out_ids) {
     drop_graph();
     CK(cudaStreamSynchronize(stream_));
     cudaGraph_t g;
+    persist_ready(B, 2);
     CK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
     decode_graph_step(B, 2);
     CK(cudaStreamEndCapture(stream_, &g));
@@ -813,6 +876,7 @@ void Model::serve_run(size_t steps, int64_t* out) {
     drop_graph();
     CK(cudaStreamSynchronize(stream_));
     cudaGraph_t g;
+    persist_ready(B, stride);
     CK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
     decode_graph_step(B, stride);
     CK(cudaStreamEndCapture(stream_, &g));

@@ -66,7 +66,7 @@ class Model {
 
   // Kernel classes of a decode step, for serve_profile.
   enum KernelClass { kClsPrep = 0, kClsMatmul, kClsLmHead, kClsMixer, kClsSwiglu, kClsEmbed,
-                     kClsArgmax, kNumClasses };
+                     kClsArgmax, kClsStep, kNumClasses };  // kClsStep: a persistent whole step
   struct ClassStats {
     double ms = 0;        // summed device time of the class's launches
     int64_t launches = 0;
@@ -109,9 +109,21 @@ class Model {
   void decode_graph_step(int B, int64_t stride);  // embed_at, layers (streams), head, argmax_at
   bool fused_decode(int B) const;                 // use the fused kernels of decode.cu?
   void fused_step(int B, int64_t stride);
+  // The fused step's phases: per layer mixer, o_proj, gate_proj + swiglu, down_proj; then
+  // the head. The first phase gathers its rows from the embedding table at *pos_.
+  std::vector<DecArgs> dec_phases(int B, int64_t stride);
+  // Plans and uploads the persistent step's phase table for (B, stride); false when the
+  // step cannot run as one cooperative launch. Not callable during stream capture.
+  bool persist_ready(int B, int64_t stride);
   int sms_ = 148;
   bool fused_ok_ = true;           // MMFREE_FUSED_DECODE=0 selects the unfused decode step
   bool pdl_ = true;                // MMFREE_PDL=0: plain stream order between kernels
+  bool persist_ok_ = false;        // MMFREE_PERSIST=1: the whole fused step in one launch
+  DecArgs* persist_tab_ = nullptr; // device copy of the persistent step's phase table
+  int persist_n_ = 0, persist_grid_ = 0, persist_b_ = 0;
+  int64_t persist_stride_ = -1;
+  size_t persist_smem_ = 0;
+  unsigned* persist_bar_ = nullptr;  // grid barrier word of the persistent step
   float* dec_part_v_ = nullptr;    // fused head: per-CTA argmax partials
   int* dec_part_i_ = nullptr;
 

@@ -82,6 +82,28 @@ def test_fused_and_unfused_decode_agree(cuda, blob_cache, monkeypatch):
         assert np.array_equal(a, b)
 
 
+@pytest.mark.gpu
+def test_persistent_step_matches_per_launch_step(cuda, monkeypatch, blob_cache, orc):
+    """The persistent decode step (one cooperative launch per token) and the per-phase
+    launches give identical ids, and both match the oracle, at 1, 2 and 3 streams."""
+    path = B.cached_blob("small", 0, blob_cache)
+    om = orc.model(B.Blob.open(path))
+    prompts = [B.seeded_ids(7, 610 + k, 2048) for k in range(3)]
+    out = {}
+    for flag in ("0", "1"):
+        monkeypatch.setenv("MMFREE_PERSIST", flag)  # 1: one cooperative launch per step
+        with api.Model(path, "fixed") as m:
+            out[flag] = (m.generate(prompts[0], 12), m.generate_serve(prompts[:2], 9),
+                         m.generate_serve(prompts, 9))
+    assert np.array_equal(out["0"][0], out["1"][0])
+    assert np.array_equal(out["1"][0], om.generate(prompts[0], 12)[0])
+    for k in (1, 2):
+        ref = om.generate_serve(prompts[:2] if k == 1 else prompts, 9)
+        for a, b, c in zip(out["0"][k], out["1"][k], ref):
+            assert np.array_equal(a, b)
+            assert np.array_equal(b, c)
+
+
 def test_serve_many_streams_matches_oracle(models, orc, blob_cache):
     """20 lockstep streams: decode rows go through the tensor-core matmul (ragged tile)."""
     m = models("small", "fixed")
