@@ -42,8 +42,9 @@ namespace mmfree_cuda {
 
 namespace {
 
-constexpr int kDecThreads = 256;
-constexpr int kDecWarps = kDecThreads / 32;
+// threads per CTA: one stream keeps few registers per thread, so it gets twice the warps for
+// the elementwise prologue and the k-split of the matmul
+__host__ __device__ constexpr int dec_threads(int MT) { return MT == 1 ? 512 : 256; }
 
 __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
@@ -75,6 +76,31 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Copies NA float arrays of K elements (those with a non-null source) from global into
+// shared memory. Each thread issues the loads of a whole batch (kB elements of every array)
+// before its first store, so one memory latency covers the batch. CG: read through L2 only
+// (data written earlier in the same launch); otherwise the read-only path (constants).
+template <int kB, int NA, bool CG, int kThr>
+__device__ __forceinline__ void load_arrays(float* const (&dst)[NA], const float* const (&src)[NA], int K) {
+  for (int c0 = threadIdx.x; c0 < K; c0 += kB * kThr) {
+    float v[NA][kB];
+#pragma unroll
+    for (int s = 0; s < NA; ++s)
+#pragma unroll
+      for (int i = 0; i < kB; ++i) {
+        const int c = c0 + i * kThr;
+        v[s][i] = (src[s] != nullptr && c < K) ? (CG ? __ldcg(src[s] + c) : __ldg(src[s] + c)) : 0.0f;
+      }
+#pragma unroll
+    for (int s = 0; s < NA; ++s)
+#pragma unroll
+      for (int i = 0; i < kB; ++i) {
+        const int c = c0 + i * kThr;
+        if (src[s] != nullptr && c < K) dst[s][c] = v[s][i];
+      }
+  }
+}
+
 }  // namespace
 
 // L2 prefetch of the weights a CTA will read in phase n
@@ -99,12 +125,15 @@ __device__ __forceinline__ void prefetch_phase(const DecArgs& n, int cta, int nc
 template <int MT, int NP, int NW, int PRO, int EPI, class Wait>
 __device__ __forceinline__ bool dec_body(const DecArgs& a, int cta, int ncta, unsigned char* dsm,
                                          const DecArgs* next, Wait&& wait) {
+  constexpr int kDecThreads = dec_threads(MT), kDecWarps = kDecThreads / 32;
   const int K = a.K, M = a.M, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t kc = packed_chunks(K), kp = kc * kChunkK;
   const int K4 = (K + 3) & ~3;
   constexpr int kNorms = (PRO == kDecProPlain ? 0 : 1) + NP;  // prew + projection norms
+  constexpr int kRows = PRO == kDecProSwish ? 2 * MT : MT;    // x rows (+ gate operand rows)
   float* xs = reinterpret_cast<float*>(dsm);                              // [MT][K4]
-  float* nws = xs + static_cast<size_t>(MT) * K4;                         // [kNorms][K4]
+  float* os = xs + static_cast<size_t>(MT) * K4;                          // [MT][K4] (Swish)
+  float* nws = xs + static_cast<size_t>(kRows) * K4;                      // [kNorms][K4]
   int8_t* pl = reinterpret_cast<int8_t*>(nws + static_cast<size_t>(kNorms) * K4);  // [NP][MT][2][kp]
   uint32_t* red = reinterpret_cast<uint32_t*>(pl + static_cast<size_t>(NP) * MT * 2 * kp);
   __shared__ float s_r[MT];
@@ -143,14 +172,18 @@ __device__ __forceinline__ bool dec_body(const DecArgs& a, int cta, int ncta, un
       for (int j = 0; j < NW; ++j) prefetch_l2(wrow(u, j) - lane, gbytes);
     if (next) prefetch_phase(*next, cta, ncta);
   }
-  {
-    int slot = 0;
-    if (PRO != kDecProPlain) {
-      for (int c = tid; c < K; c += kDecThreads) nws[c] = __ldg(a.prew + c);
-      slot = 1;
+  {  // norm weights (one batch of loads)
+    constexpr int s0 = PRO == kDecProPlain ? 0 : 1;
+    float* const dst[4] = {nws, nws + s0 * K4, nws + (s0 + 1) * K4, nws + (s0 + 2) * K4};
+    const float* const src[4] = {PRO == kDecProPlain ? nullptr : a.prew, a.normw[0],
+                                 NP > 1 ? a.normw[1] : nullptr, NP > 2 ? a.normw[2] : nullptr};
+    if (PRO == kDecProPlain) {
+      float* const d1[4] = {dst[1], nullptr, nullptr, nullptr};
+      const float* const s1[4] = {a.normw[0], nullptr, nullptr, nullptr};
+      load_arrays<8, 4, false, kDecThreads>(d1, s1, K);
+    } else {
+      load_arrays<8, 4, false, kDecThreads>(dst, src, K);
     }
-    for (int j = 0; j < NP; ++j)
-      for (int c = tid; c < K; c += kDecThreads) nws[(slot + j) * K4 + c] = __ldg(a.normw[j] + c);
   }
   float lb_pre = 0.0f, st_pre[MT];
   if (EPI == kDecEpiMixer && warp == 0 && u0 < units) {
@@ -172,22 +205,34 @@ __device__ __forceinline__ bool dec_body(const DecArgs& a, int cta, int ncta, un
 
   // ---- 3. prologue: rows into shared memory (or gathered from the embedding table), exact
   //         norms, Q5.10 byte planes
-  for (int t = 0; t < MT; ++t) {
-    const int tr = t < M ? t : M - 1;
-    const float* xr = a.x + static_cast<int64_t>(tr) * K;
-    if (a.xids) {  // the step's first phase: x = embedding row of the current token
-      const int64_t id = a.xids[tr * a.xstride + *a.xpos];
-      const bool ok = id >= 0 && id < a.V;
-      if (!ok && tid == 0 && a.err) atomicOr(a.err, kErrBadToken);
-      xr = ok ? a.x + id * K : nullptr;
+  {
+    float* dst[2 * MT];
+    const float* src[2 * MT];
+#pragma unroll
+    for (int t = 0; t < MT; ++t) {
+      const int tr = t < M ? t : M - 1;
+      const float* xr = a.x + static_cast<int64_t>(tr) * K;
+      if (a.xids) {  // the step's first phase: x = embedding row of the current token
+        const int64_t id = a.xids[tr * a.xstride + *a.xpos];
+        const bool ok = id >= 0 && id < a.V;
+        if (!ok && tid == 0 && a.err) atomicOr(a.err, kErrBadToken);
+        xr = ok ? a.x + id * K : nullptr;
+      }
+      dst[t] = xs + t * K4;
+      src[t] = xr;
+      dst[MT + t] = os + t * K4;
+      src[MT + t] = PRO == kDecProSwish ? a.o + static_cast<int64_t>(tr) * K : nullptr;
     }
-    for (int c = tid; c < K; c += kDecThreads) {
-      const float v = xr ? (a.xids ? __ldg(xr + c) : __ldcg(xr + c)) : 0.0f;
-      xs[t * K4 + c] = v;
-      if (a.xcopy && cta == 0 && t < M) a.xcopy[static_cast<int64_t>(t) * K + c] = v;
-    }
+    load_arrays<MT == 1 ? 16 : 8, 2 * MT, true, kDecThreads>(dst, src, K);
+#pragma unroll
+    for (int t = 0; t < MT; ++t)  // a bad id gives a zero row
+      if (src[t] == nullptr)
+        for (int c = tid; c < K; c += kDecThreads) xs[t * K4 + c] = 0.0f;
   }
   __syncthreads();
+  if (a.xcopy && cta == 0)
+    for (int t = 0; t < M && t < MT; ++t)
+      for (int c = tid; c < K; c += kDecThreads) a.xcopy[static_cast<int64_t>(t) * K + c] = xs[t * K4 + c];
   const int myrow = (lane >> 3) < MT ? (lane >> 3) : MT - 1;  // warp 0: 8 lanes per row
   const float* nproj = nws + (PRO == kDecProPlain ? 0 : K4);    // projection norm weights
   if (PRO != kDecProPlain) {
@@ -198,11 +243,9 @@ __device__ __forceinline__ bool dec_body(const DecArgs& a, int cta, int ncta, un
     __syncthreads();
     for (int t = 0; t < MT; ++t) {
       const float r1 = s_r[t];
-      const int tr = t < M ? t : M - 1;
       for (int c = tid; c < K; c += kDecThreads) {
         float v = norm_x(xs[t * K4 + c], r1, nws[c]);
-        if (PRO == kDecProSwish)
-          v = __fmul_rn(v, silu_x(__ldcg(a.o + static_cast<int64_t>(tr) * K + c), in_body(c, K)));
+        if (PRO == kDecProSwish) v = __fmul_rn(v, silu_x(os[t * K4 + c], in_body(c, K)));
         xs[t * K4 + c] = v;
       }
     }
@@ -219,19 +262,29 @@ __device__ __forceinline__ bool dec_body(const DecArgs& a, int cta, int ncta, un
     for (int j = 0; j < NP; ++j)
 #pragma unroll
       for (int t = 0; t < MT; ++t) local[j][t] = 0;
-    for (int c = tid; c < kp; c += kDecThreads) {
+    // 4 consecutive k per step: vector loads, one 4-byte store per plane
+    for (int c4 = tid * 4; c4 < kp; c4 += kDecThreads * 4) {
 #pragma unroll
       for (int t = 0; t < MT; ++t) {
-        const float xv = c < K ? xs[t * K4 + c] : 0.0f;
+        const float4 xv4 = c4 < K ? *reinterpret_cast<const float4*>(xs + t * K4 + c4) : make_float4(0, 0, 0, 0);
+        const float xv[4] = {xv4.x, xv4.y, xv4.z, xv4.w};
         const float r2 = s_r[t];
 #pragma unroll
         for (int j = 0; j < NP; ++j) {
-          int32_t q = 0;
-          if (c < K) q = quant_x(norm_x(xv, r2, nproj[j * K4 + c]), a.qs, in_body(c, K));
-          local[j][t] += q;
+          const float4 w4 = c4 < K ? *reinterpret_cast<const float4*>(nproj + j * K4 + c4) : make_float4(0, 0, 0, 0);
+          const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+          uint32_t hw = 0, lw = 0;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int c = c4 + e;
+            const int32_t q = c < K ? quant_x(norm_x(xv[e], r2, wv[e]), a.qs, in_body(c, K)) : 0;
+            local[j][t] += q;
+            hw |= static_cast<uint32_t>((q >> 8) & 0xff) << (8 * e);
+            lw |= static_cast<uint32_t>(q & 0xff) << (8 * e);
+          }
           int8_t* hi = pl + (static_cast<int64_t>(j) * MT + t) * 2 * kp;
-          hi[c] = static_cast<int8_t>(q >> 8);
-          hi[kp + c] = static_cast<int8_t>(q & 0xff);
+          *reinterpret_cast<uint32_t*>(hi + c4) = hw;
+          *reinterpret_cast<uint32_t*>(hi + kp + c4) = lw;
         }
       }
     }
@@ -427,7 +480,7 @@ __device__ __forceinline__ bool dec_body(const DecArgs& a, int cta, int ncta, un
 }
 
 template <int MT, int NP, int NW, int PRO, int EPI>
-__global__ void __launch_bounds__(kDecThreads) dec_kernel(DecArgs a) {
+__global__ void __launch_bounds__(dec_threads(MT)) dec_kernel(DecArgs a) {
   extern __shared__ __align__(16) unsigned char dsm[];
   dec_body<MT, NP, NW, PRO, EPI>(a, blockIdx.x, gridDim.x, dsm, nullptr, [] {
     grid_dep_wait();
@@ -438,14 +491,28 @@ __global__ void __launch_bounds__(kDecThreads) dec_kernel(DecArgs a) {
 
 // The whole decode step in one cooperative launch (phase table in device memory).
 template <int MT>
-__global__ void __launch_bounds__(kDecThreads, 1) dec_persist_kernel(const DecArgs* __restrict__ phases,
+__global__ void __launch_bounds__(dec_threads(MT), 1) dec_persist_kernel(const DecArgs* __restrict__ phases,
                                                                      int nphases, unsigned* bar,
                                                                      uint32_t* err) {
   extern __shared__ __align__(16) unsigned char dsm[];
   __shared__ unsigned s_ok;
+  __shared__ DecArgs s_args[2];  // this phase's descriptor and the next one (copied ahead)
+  constexpr int kWords = sizeof(DecArgs) / 16;
   const int cta = blockIdx.x, ncta = gridDim.x;
+  auto fetch = [&](int ph) {  // asynchronous 16-byte copies, completed before the next phase
+    if (threadIdx.x < kWords)
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(
+                       reinterpret_cast<const char*>(&s_args[ph & 1]) + 16 * threadIdx.x)),
+                   "l"(reinterpret_cast<const char*>(phases + ph) + 16 * threadIdx.x)
+                   : "memory");
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  fetch(0);
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncthreads();
   for (int ph = 0; ph < nphases; ++ph) {
-    const DecArgs a = phases[ph];
+    if (ph + 1 < nphases) fetch(ph + 1);
+    const DecArgs& a = s_args[ph & 1];
     const DecArgs* next = ph + 1 < nphases ? &phases[ph + 1] : nullptr;
     // phase ph may start once every CTA has finished phase ph - 1
     auto wait = [&]() -> bool {
@@ -475,6 +542,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) dec_persist_kernel(const DecAr
       ok = dec_body<MT, 1, 1, kDecProSwish, kDecEpiResid>(a, cta, ncta, dsm, next, wait);
     else
       ok = dec_body<MT, 1, 1, kDecProPlain, kDecEpiResid>(a, cta, ncta, dsm, next, wait);
+    asm volatile("cp.async.wait_all;" ::: "memory");  // the next descriptor has landed
     if (!ok) return;  // a barrier timed out (error flag set): every CTA stops
     // arrive: this CTA's part of phase ph is written
     __syncthreads();
@@ -495,9 +563,10 @@ static DecSmem dec_smem(int K, int MT, int NP, int NW, int PRO) {
   const int64_t kp = padded_k(K);
   const int K4 = (K + 3) & ~3;
   const int norms = (PRO == kDecProPlain ? 0 : 1) + NP;
+  const int rows = PRO == kDecProSwish ? 2 * MT : MT;
   DecSmem d;
-  d.base = static_cast<size_t>(MT + norms) * K4 * 4 + static_cast<size_t>(NP) * MT * 2 * kp +
-           static_cast<size_t>(kDecWarps) * NW * MT * 32 * 4;
+  d.base = static_cast<size_t>(rows + norms) * K4 * 4 + static_cast<size_t>(NP) * MT * 2 * kp +
+           static_cast<size_t>(dec_threads(MT) / 32) * NW * MT * 32 * 4;
   d.staged = static_cast<size_t>(NW) * kp / kChunkK * kChunkBytes;
   return d;
 }
@@ -536,7 +605,7 @@ static cudaError_t launch_dec_t(const DecArgs& a, int grid, cudaStream_t s, bool
   static size_t cache[64] = {0};
   cudaError_t e = dec_smem_attr(dec_kernel<MT, NP, NW, PRO, EPI>, smem, cache);
   if (e != cudaSuccess) return e;
-  return launch_k(dec_kernel<MT, NP, NW, PRO, EPI>, dim3(static_cast<unsigned>(grid)), dim3(kDecThreads),
+  return launch_k(dec_kernel<MT, NP, NW, PRO, EPI>, dim3(static_cast<unsigned>(grid)), dim3(dec_threads(MT)),
                   smem, s, pdl, b);
 }
 
@@ -600,7 +669,7 @@ static cudaError_t persist_mt(const DecArgs* dev_phases, int n, unsigned* bar, u
     cudaGetDevice(&dev);
     if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
     if ((e = cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev)) != cudaSuccess) return e;
-    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, dec_persist_kernel<MT>, kDecThreads,
+    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, dec_persist_kernel<MT>, dec_threads(MT),
                                                            smem)) != cudaSuccess)
       return e;
     *grid = coop && per_sm >= 1 ? sms : 0;
@@ -608,7 +677,7 @@ static cudaError_t persist_mt(const DecArgs* dev_phases, int n, unsigned* bar, u
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(*grid));
-  cfg.blockDim = dim3(kDecThreads);
+  cfg.blockDim = dim3(dec_threads(MT));
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute at[1];

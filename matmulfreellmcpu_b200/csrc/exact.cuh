@@ -100,19 +100,17 @@ __device__ __forceinline__ float norm_x(float x, float rstd, float w) {
 
 // simd::quant_q510 (simd.hpp:162-187), one element. In the SIMD body the float->int
 // conversion is cvtps2dq (round half to even, NaN / out-of-range -> INT32_MIN) followed by
-// an integer clamp; in the scalar tail the clamp is in float and the cast truncates.
+// an integer clamp; in the scalar tail the clamp is in float and the cast truncates (NaN ->
+// INT32_MIN). Both forms are evaluated with selects (no branches in unrolled loops).
 __device__ __forceinline__ int32_t quant_x(float y, float qs, bool body) {
-  float q = __fmul_rn(y, qs);
-  if (body) {
-    int32_t v;
-    if (isnan(q) || q >= 2147483648.0f || q < -2147483648.0f) v = INT32_MIN;
-    else v = __float2int_rn(q);
-    return v < -32768 ? -32768 : (v > 32767 ? 32767 : v);
-  }
+  const float q = __fmul_rn(y, qs);
+  const int32_t cv = __float2int_rn(q);
+  const int32_t vb = fabsf(q) < 2147483648.0f ? cv : INT32_MIN;  // false for NaN too
+  const int32_t bq = vb < -32768 ? -32768 : (vb > 32767 ? 32767 : vb);
   float r = rintf(q);
-  if (r > 32767.0f) r = 32767.0f;
-  else if (r < -32768.0f) r = -32768.0f;
-  return isnan(r) ? INT32_MIN : static_cast<int32_t>(r);
+  r = r > 32767.0f ? 32767.0f : (r < -32768.0f ? -32768.0f : r);
+  const int32_t tq = isnan(q) ? INT32_MIN : static_cast<int32_t>(r);
+  return body ? bq : tq;
 }
 
 // Lower-bounded forget gate of layers > 0 (hgrn_model.cpp:116-124), as fused by the build.
@@ -142,28 +140,32 @@ __device__ __forceinline__ float hsum8_lanes(float v, unsigned mask = 0xffffffff
 
 // Lane j (= threadIdx.x & 7) of an 8-lane group runs chain j of the AVX2 sum of squares
 // (simd.hpp:69-89) over s[0..K): acc_j = fma(s[8i+j], s[8i+j], acc_j) for i < K/8, in order.
-// The loads are issued in batches of 8 one batch ahead of the FMAs, so the serial chain
-// waits only on the FMA latency. Returns this lane's partial (combine with hsum8_lanes).
+// Whole batches of 8 are loaded unconditionally one batch ahead of their FMAs, so the serial
+// chain waits only on the FMA latency; a remainder of K/8 mod 8 steps follows.
 __device__ __forceinline__ float sumsq_chain_lane(const float* s, int K) {
-  const int j = threadIdx.x & 7;
-  const int n8 = K >> 3;
+  const float* p = s + (threadIdx.x & 7);
+  const int n8 = K >> 3, nb = n8 >> 3;
   float acc = 0.0f;
-  float cur[8], nxt[8];
-  int i = 0;
+  if (nb > 0) {
+    float cur[8];
 #pragma unroll
-  for (int u = 0; u < 8; ++u) cur[u] = (u < n8) ? s[8 * u + j] : 0.0f;
-  for (; i + 8 <= n8; i += 8) {
-    const bool more = i + 8 < n8;
+    for (int u = 0; u < 8; ++u) cur[u] = p[8 * u];
+    for (int b = 1; b < nb; ++b) {
+      float nxt[8];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) nxt[u] = (more && i + 8 + u < n8) ? s[8 * (i + 8 + u) + j] : 0.0f;
+      for (int u = 0; u < 8; ++u) nxt[u] = p[64 * b + 8 * u];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc = __fmaf_rn(cur[u], cur[u], acc);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) cur[u] = nxt[u];
+    }
 #pragma unroll
     for (int u = 0; u < 8; ++u) acc = __fmaf_rn(cur[u], cur[u], acc);
-#pragma unroll
-    for (int u = 0; u < 8; ++u) cur[u] = nxt[u];
   }
-#pragma unroll
-  for (int u = 0; u < 8; ++u)
-    if (i + u < n8) acc = __fmaf_rn(cur[u], cur[u], acc);
+  for (int i = nb * 8; i < n8; ++i) {
+    const float v = p[8 * i];
+    acc = __fmaf_rn(v, v, acc);
+  }
   return acc;
 }
 

@@ -72,7 +72,7 @@ enum DecEpi : int {
 };
 constexpr int kDecMaxRows = 4;
 
-struct DecArgs {
+struct alignas(16) DecArgs {
   const float* x = nullptr;       // [M, K] (or the embedding table [V, K] when xids is set)
   const float* o = nullptr;       // [M, K] recurrence output (kDecProSwish)
   const float* prew = nullptr;    // [K] first norm weight
