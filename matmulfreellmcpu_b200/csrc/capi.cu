@@ -150,6 +150,8 @@ void run_bitlinear(int k, float* const* outs, const float* x, const float* const
   p.eps = eps;
   p.qs = static_cast<float>(1u << frac_bits);
   p.fixed = fixed;
+  // the tensor-core matmul (taken for >= kTcMinRows fixed rows) reads the low plane as lo - 128
+  p.lo_signed = fixed && static_cast<int>(rows) >= kTcMinRows;
   for (int j = 0; j < k; ++j) {
     char* b = base + 256 + j * per;
     p.normw[j] = nws[j];
@@ -176,6 +178,7 @@ void run_bitlinear(int k, float* const* outs, const float* x, const float* const
     a.acc_out = (acc_out && fixed) ? acc_out + static_cast<size_t>(j) * rows * out_dim : nullptr;
     a.fixed = fixed;
     a.allow_tc = true;
+    a.lo_signed = p.lo_signed;
     a.tc_accum = tc_accum;
     a.tc_accum_words = accum_words;
     a.tc_tiles = tc_tiles;

@@ -175,7 +175,8 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepArgs a, int mode
         const int32_t q = c < K ? quant_x(y, a.qs, in_body(c, K)) : 0;
         local[j] += q;
         a.planes[j][static_cast<int64_t>(m) * Kp + c] = static_cast<int8_t>(q >> 8);
-        a.planes[j][(static_cast<int64_t>(a.M) + m) * Kp + c] = static_cast<int8_t>(q & 0xff);
+        a.planes[j][(static_cast<int64_t>(a.M) + m) * Kp + c] =
+            static_cast<int8_t>((q & 0xff) ^ (a.lo_signed ? 0x80 : 0));
       } else {
         a.yf[j][static_cast<int64_t>(m) * Kp + c] = y;
       }
@@ -404,7 +405,8 @@ static int sm_count() {
 
 cudaError_t launch_matmul(const MatmulArgs& a, cudaStream_t s) {
   if (a.M <= 0 || a.N <= 0) return cudaSuccess;
-  if (a.fixed && a.allow_tc && a.M >= kTcMinRows) {
+  if (matmul_uses_tc(a)) {
+    if (!a.lo_signed) return cudaErrorInvalidValue;  // planes in the wrong form
     int splits = tc_splits(a, sm_count());
     if (splits > 1 && (!a.tc_accum || a.tc_accum_words < static_cast<size_t>(a.M) * a.N ||
                        !a.tc_tiles || a.tc_tiles_words < static_cast<size_t>(tc_tile_count(a.M, a.N))))

@@ -23,6 +23,8 @@ struct PrepArgs {
   const float* normw[3] = {};    // per projection BitLinear norm weight [K]
   float* norm_out = nullptr;     // optional [M, K]: normalized input of projection 0
   int8_t* planes[3] = {};        // fixed: [2][M][Kp] high bytes then low bytes of Q5.10 codes
+  bool lo_signed = false;        // fixed: low plane stored as (lo ^ 0x80) = lo - 128 (s8), the
+                                 // form the tensor-core matmul reads (matmul_uses_tc)
   int32_t* rowsum[3] = {};       // fixed: [M] sum of codes
   float* yf[3] = {};             // float: [M][Kp] normalized activations (zero padded)
   int M = 0, K = 0;
@@ -54,9 +56,12 @@ struct MatmulArgs {
   size_t tc_tiles_words = 0;
   uint32_t* err = nullptr;
   bool pdl = false;               // launch as a programmatic dependent of the previous kernel
+  bool lo_signed = false;         // planes hold lo - 128 (required by the tensor-core path)
 };
 
 constexpr int kTcMinRows = 16;
+// Does launch_matmul take the tensor-core path (whose planes must be lo_signed)?
+inline bool matmul_uses_tc(const MatmulArgs& a) { return a.fixed && a.allow_tc && a.M >= kTcMinRows; }
 
 // ---- fused few-row decode kernels (decode.cu)
 enum DecPro : int {
@@ -116,9 +121,15 @@ cudaError_t launch_dec_persist(const DecArgs* dev_phases, int nphases, int M, un
 
 // tcgen05 BitLinear matmul (tc_matmul.cu)
 int tc_token_tile(int M);
-int tc_splits(const MatmulArgs& a, int sm_count);
+int tc_splits(const MatmulArgs& a, int sm_count, int nproj = 1);
 cudaError_t launch_matmul_tc(const MatmulArgs& a, uint32_t* accum, uint32_t* tiles, int splits,
                              uint32_t* err, cudaStream_t s);
+// Several tensor-core BitLinears in one launch: nproj (1..3) projections of one shape (the
+// i/f/g cluster; a[0] carries the shared workspace, error word and launch mode), or with
+// swiglu_I > 0 (I % 64 == 0, nproj 1) a gate_proj of N = 2I whose epilogue writes
+// a[0].out = z [M, I] = silu(y[:, :I]) * y[:, I:] with SIMD tails per seg elements.
+cudaError_t launch_matmul_tc_group(const MatmulArgs* a, int nproj, int swiglu_I, int64_t seg,
+                                   int sm_count, cudaStream_t s);
 // output tiles of the tcgen05 path (split-K counters needed)
 inline int64_t tc_tile_count(int M, int N) {
   return ((N + 127) / 128) * static_cast<int64_t>((M + tc_token_tile(M) - 1) / tc_token_tile(M));

@@ -318,6 +318,7 @@ void Model::prep(const PrepArgs& p) {
                        rows * out_row * p.nproj;
   PrepArgs q = p;
   q.pdl = pdl_;
+  q.lo_signed = tc_rows(q.M);  // the BitLinear of these rows runs on the tensor cores
   timed(kClsPrep, bytes, 0, [&] { CK(launch_prep(q, stream_)); });
 }
 
@@ -327,7 +328,7 @@ const char* Model::class_name(int c) {
   return (c >= 0 && c < kNumClasses) ? n[c] : "?";
 }
 
-void Model::bitlinear(const Proj& p, int plane, float* out, int M, const float* resid) {
+MatmulArgs Model::mm_args(const Proj& p, int plane, float* out, int M, const float* resid) const {
   MatmulArgs a;
   a.w = p.w;
   a.planes = planes_[plane];
@@ -349,11 +350,50 @@ void Model::bitlinear(const Proj& p, int plane, float* out, int M, const float* 
   a.tc_tiles_words = tc_tiles_words_;
   a.err = err_;
   a.pdl = pdl_;
+  a.lo_signed = tc_rows(M);
+  return a;
+}
+
+void Model::bitlinear(const Proj& p, int plane, float* out, int M, const float* resid) {
+  const MatmulArgs a = mm_args(p, plane, out, M, resid);
   // algorithmic bytes (2-bit weights, activations in, outputs out) and 2*M*K*N ops
   const double K = p.in, N = p.out;
   const double bytes = K * N / 4 + 4.0 * M * K + 4.0 * M * N * (resid ? 2 : 1);
   timed(&p == &lm_head_ ? kClsLmHead : kClsMatmul, bytes, 2.0 * M * K * N,
         [&] { CK(launch_matmul(a, stream_)); });
+}
+
+bool Model::tc_rows(int M) const { return fixed_ && M >= kTcMinRows; }
+
+void Model::bitlinear_ifg(const Layer& ly, int M) {
+  if (!tc_rows(M)) {
+    bitlinear(ly.p[kI], 0, ib_, M, nullptr);
+    bitlinear(ly.p[kF], 1, fb_, M, nullptr);
+    bitlinear(ly.p[kG], 2, gb_, M, nullptr);
+    return;
+  }
+  const MatmulArgs a[3] = {mm_args(ly.p[kI], 0, ib_, M, nullptr), mm_args(ly.p[kF], 1, fb_, M, nullptr),
+                           mm_args(ly.p[kG], 2, gb_, M, nullptr)};
+  const double K = H_, N = H_;
+  const double bytes = 3 * (K * N / 4 + 4.0 * M * K + 4.0 * M * N);
+  timed(kClsMatmul, bytes, 6.0 * M * K * N,
+        [&] { CK(launch_matmul_tc_group(a, 3, 0, 0, sms_, stream_)); });
+}
+
+void Model::bitlinear_gate_swiglu(const Layer& ly, int M, int seg_rows) {
+  if (!tc_rows(M) || I_ % 64 != 0) {
+    bitlinear(ly.p[kGate], 0, y_, M, nullptr);
+    timed(kClsSwiglu, 12.0 * M * I_, 0,
+          [&] { CK(launch_swiglu_split(z_, y_, M, I_, seg_rows, stream_, pdl_)); });
+    return;
+  }
+  MatmulArgs a = mm_args(ly.p[kGate], 0, z_, M, nullptr);
+  a.ldo = I_;
+  const double K = H_, N = 2.0 * I_;
+  const double bytes = K * N / 4 + 4.0 * M * K + 4.0 * M * I_;
+  timed(kClsMatmul, bytes, 2.0 * M * K * N, [&] {
+    CK(launch_matmul_tc_group(&a, 1, I_, static_cast<int64_t>(seg_rows) * I_, sms_, stream_));
+  });
 }
 
 template <class StateFn>
@@ -380,9 +420,7 @@ void Model::layers(int nseq, int len, int seg_rows, StateFn state) {
     p.normw[1] = ly.p[kF].normw;
     p.normw[2] = ly.p[kG].normw;
     prep(p);
-    bitlinear(ly.p[kI], 0, ib_, rows, nullptr);
-    bitlinear(ly.p[kF], 1, fb_, rows, nullptr);
-    bitlinear(ly.p[kG], 2, gb_, rows, nullptr);
+    bitlinear_ifg(ly, rows);
     timed(kClsMixer, 4.0 * rows * H_ * 5 + 8.0 * nseq * H_, 0, [&] {
       CK(launch_mixer(ib_, fb_, recur_, state(l), ly.lb, nseq, len, H_, seg_rows, stream_, pdl_));
     });
@@ -400,9 +438,7 @@ void Model::layers(int nseq, int len, int seg_rows, StateFn state) {
     p.prew = ly.mlp_norm;
     p.normw[0] = ly.p[kGate].normw;
     prep(p);
-    bitlinear(ly.p[kGate], 0, y_, rows, nullptr);
-    timed(kClsSwiglu, 12.0 * rows * I_, 0,
-          [&] { CK(launch_swiglu_split(z_, y_, rows, I_, seg_rows, stream_, pdl_)); });
+    bitlinear_gate_swiglu(ly, rows, seg_rows);
     p.x = z_;
     p.prew = nullptr;
     p.K = I_;

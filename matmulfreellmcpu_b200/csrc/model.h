@@ -99,7 +99,11 @@ class Model {
   void prep(const PrepArgs& p);
   template <class F>
   void timed(int cls, double bytes, double ops, F&& launch);
+  MatmulArgs mm_args(const Proj& p, int plane, float* out, int M, const float* resid) const;
   void bitlinear(const Proj& p, int plane, float* out, int M, const float* resid);
+  bool tc_rows(int M) const;                          // tensor-core BitLinear for M rows?
+  void bitlinear_ifg(const Layer& ly, int M);         // i/f/g (one launch on tensor cores)
+  void bitlinear_gate_swiglu(const Layer& ly, int M, int seg_rows);  // z = swiglu(gate_proj)
   // All layers over `rows` = nseq * len rows of h_ ([nseq][len][H]); state(l) gives the
   // layer's state base ([nseq][H]) or nullptr; seg_rows = rows of one reference block call.
   template <class StateFn>

@@ -11,24 +11,27 @@
 //                              weights depend on no earlier kernel, so this runs ahead of
 //                              griddepcontrol.wait and overlaps the predecessor kernel
 //   warp 5  activation producer after griddepcontrol.wait, TMA (cp.async.bulk.tensor.2d)
-//                              loads of the high-byte (s8) and low-byte (u8) planes of the
-//                              Q5.10 codes, BN rows x 128 B per plane and k-block, written
-//                              with the 128-byte swizzle the MMA descriptor names
+//                              loads of the high-byte planes and the low-byte planes stored
+//                              as lo - 128 (both s8) of the Q5.10 codes, BN rows x 128 B each
+//                              per k-block, back to back: one 2*BN-row operand written with
+//                              the 128-byte swizzle the MMA descriptor names
 //   warps 0-3 expanders        warp w expands group w's 2-bit codes u = w + 1 to u8 and
 //                              writes them to TENSOR MEMORY (lane = weight row, 4 codes per
-//                              32-bit column) with tcgen05.st; a 4-stage TMEM ring
-//   warp 6  MMA issuer         tcgen05.mma.cta_group::1.kind::i8 with A from TMEM:
-//                              D_hi += u x hi (u8 x s8), D_lo += u x lo (u8 x u8), M=128,
-//                              N=BN, K=32 per instruction, int32 accumulators in TMEM;
-//                              tcgen05.commit releases the ring stages
-//   epilogue (warps 0-3)       tcgen05.ld of D_hi/D_lo; acc = 256*D_hi + D_lo - sum_k q[t, k]
-//                              (exact in int32); split-K partials are combined with integer
-//                              atomics (exact, order free) and the last CTA of a tile
-//                              applies dequant (+ residual).
+//                              32-bit column) with tcgen05.st (a 4-stage TMEM ring), and
+//                              sums its row's codes (popcount) for the low-plane offset
+//   warp 6  MMA issuer         tcgen05.mma.cta_group::1.kind::i8 with A from TMEM, one
+//                              instruction per 32 k for both planes: D[:, 0:BN] += u x hi,
+//                              D[:, BN:2BN] += u x (lo - 128) (u8 x s8, M=128, N=2*BN),
+//                              int32 accumulators in TMEM; tcgen05.commit releases the rings
+//   epilogue (warps 0-3)       tcgen05.ld of D; acc = 256*D_hi + D_lo' + 128*sum_k u - sum_k q
+//                              (exact modulo 2^32, hence in int32); split-K partials are
+//                              combined with integer atomics (exact, order free) and the last
+//                              CTA of a tile applies dequant (+ residual, or the SwiGLU pair).
 // Every wait on an mbarrier is bounded; on timeout the CTA sets an error flag, the other roles
 // stop, producers wait (bounded) for their copies in flight, the MMA issuer's final commit
 // covers its MMAs, and the tensor memory is freed.
 #include "common.cuh"
+#include "exact.cuh"
 #include "kernels.h"
 
 #include <cuda.h>
@@ -181,12 +184,28 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 
 }  // namespace
 
+// One projection of a launch (i/f/g share a launch; they differ only in these).
+struct TcProj {
+  const void* w;           // packed weights
+  const int32_t* rowsum;   // [M] code sums of the projection's activation rows
+  float* out;              // [M, ldo]
+  float scale;             // 1 / (2^f * scale_w)
+  uint32_t* accum;         // split-K: [M, N] int32 partial sums (zero on entry and exit)
+  uint32_t* tiles;         // split-K: one arrival counter per output tile (zero on entry, exit)
+};
+
 struct TcArgs {
-  MatmulArgs m;
-  uint32_t* accum;    // split-K: [M, N] int32 partial sums (zero on entry, left zero on exit)
-  uint32_t* tiles;    // split-K: one arrival counter per (weight tile, token tile), left zero
+  MatmulArgs m;       // shape, residual and raw-accumulator output (single projection)
+  TcProj pj[3];
+  int nproj;          // grid.z = nproj * splits
+  int pair;           // SwiGLU gate_proj: I/32, the first group of the up rows; 0 otherwise
+  int64_t seg;        // SwiGLU: elements of one reference vector call (SIMD tails)
   uint32_t* err;      // bit kErrTimeout on a timed-out wait
-  int splits;         // k-block ranges per tile (grid.z)
+  int splits;         // k-block ranges per tile
+};
+
+struct TcMaps {
+  CUtensorMap m[3];   // activation planes of each projection
 };
 
 namespace {
@@ -221,7 +240,7 @@ __device__ __forceinline__ bool role_wait(uint64_t* bar, uint32_t parity, uint32
 
 template <int BN>
 __global__ void __launch_bounds__(kTcThreads, 1)
-    tc_matmul_kernel(const __grid_constant__ CUtensorMap bmap, TcArgs p) {
+    tc_matmul_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcArgs p) {
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 64, "BN must be 16..64, a multiple of 16");
   constexpr int kCols = kAStages * 32 + 2 * BN;  // A stages + D_hi + D_lo
   constexpr int kAllocCols = kCols <= 128 ? 128 : (kCols <= 256 ? 256 : 512);
@@ -243,10 +262,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const MatmulArgs& a = p.m;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n0 = blockIdx.x * 128, t0 = blockIdx.y * BN;
+  const int proj = blockIdx.z / p.splits, split = blockIdx.z % p.splits;
+  const TcProj& P = p.pj[proj];
+  const CUtensorMap* bmap = &maps.m[proj];
+  // weight row group of row block g (0..3): 4 consecutive groups, or for a SwiGLU pair the
+  // gate groups 2x, 2x+1 and the up groups pair + 2x, pair + 2x + 1
+  auto tile_group = [&](int g) -> int64_t {
+    return p.pair ? (g < 2 ? 2 * blockIdx.x + g : p.pair + 2 * blockIdx.x + g - 2) : (n0 >> 5) + g;
+  };
   const int64_t kc = packed_chunks(a.K);
   const int nkb = static_cast<int>((kc + 1) / 2);
-  const int kb0 = static_cast<int>(static_cast<int64_t>(nkb) * blockIdx.z / p.splits);
-  const int kb1 = static_cast<int>(static_cast<int64_t>(nkb) * (blockIdx.z + 1) / p.splits);
+  const int kb0 = static_cast<int>(static_cast<int64_t>(nkb) * split / p.splits);
+  const int kb1 = static_cast<int>(static_cast<int64_t>(nkb) * (split + 1) / p.splits);
   const int nk = kb1 - kb0;
 
   if (tid == 0) {
@@ -268,7 +295,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   if (warp == kBWarp && lane == 0)
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&bmap)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(bmap)) : "memory");
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -281,7 +308,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // ---- weight producer: 4 groups x (1 or 2) chunks per k-block, contiguous per group
     if (lane == 0) {
       const int64_t ngroups = packed_groups(a.N);
-      const unsigned char* wbase = static_cast<const unsigned char*>(a.w);
+      const unsigned char* wbase = static_cast<const unsigned char*>(P.w);
       const uint64_t pol = l2_evict_first();
       int i = 0;
       for (; i < nk; ++i) {
@@ -294,10 +321,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const uint32_t bytes = c0 + 1 < kc ? 2 * kChunkBytes : kChunkBytes;
         uint32_t total = 0;
         for (int g = 0; g < 4; ++g)
-          if ((n0 >> 5) + g < ngroups) total += bytes;
+          if (tile_group(g) < ngroups) total += bytes;
         mbar_arrive_tx(&wfull[s], total);
         for (int g = 0; g < 4; ++g) {
-          const int64_t gg = (n0 >> 5) + g;
+          const int64_t gg = tile_group(g);
           if (gg < ngroups)
             bulk_g2s(wst + s * kWBlock + g * 2 * kChunkBytes, wbase + (gg * kc + c0) * kChunkBytes,
                      bytes, &wfull[s], pol);
@@ -321,8 +348,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int x = (kb0 + i) * kKBlock;
         unsigned char* dst = bst + s * L::kBStage;
         mbar_arrive_tx(&bfull[s], static_cast<uint32_t>(L::kBStage));
-        tma_load_2d(dst, &bmap, x, t0, &bfull[s]);                  // high plane rows
-        tma_load_2d(dst + L::kBPlane, &bmap, x, a.M + t0, &bfull[s]);  // low plane rows
+        tma_load_2d(dst, bmap, x, t0, &bfull[s]);                  // high plane rows
+        tma_load_2d(dst + L::kBPlane, bmap, x, a.M + t0, &bfull[s]);  // low plane rows
       }
       if (i < nk) {
         atomicOr(&s_fail, 1u);
@@ -343,13 +370,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         tc_fence_after();
         const uint32_t hi_base = smem_u32(bst + sb * L::kBStage);
-        const uint32_t lo_base = hi_base + L::kBPlane;
+        // both planes in one instruction: B rows [0, BN) are the high bytes, [BN, 2BN) the
+        // low bytes - 128 (both s8, one 128-byte-swizzled tile), D columns likewise
 #pragma unroll
         for (int j = 0; j < kKBlock / 32; ++j) {
           const uint32_t acc = (i > 0 || j > 0) ? 1u : 0u;
           const uint32_t a_addr = tmem_a + static_cast<uint32_t>(sa * 32 + j * 8);
-          mma_i8_ts(tmem_dhi, a_addr, smem_desc_sw128(hi_base + j * 32), idesc_i8(true, BN), acc);
-          mma_i8_ts(tmem_dlo, a_addr, smem_desc_sw128(lo_base + j * 32), idesc_i8(false, BN), acc);
+          mma_i8_ts(tmem_dhi, a_addr, smem_desc_sw128(hi_base + j * 32), idesc_i8(true, 2 * BN), acc);
         }
         mma_commit(&aempty[sa]);
         mma_commit(&bempty[sb]);
@@ -363,11 +390,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     //      u8 TMEM columns, then the epilogue
     const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
     bool ok = true;
+    uint32_t su = 0;  // sum of this row's codes u over the k-blocks of this CTA (k < Kp)
     for (int i = 0; i < nk; ++i) {
       const int sw = i % kWStages, sa = i % kAStages;
       if (!role_wait(&wfull[sw], (i / kWStages) & 1, &s_fail)) { ok = false; break; }
       const uint4* src = reinterpret_cast<const uint4*>(wst + sw * kWBlock + warp * 2 * kChunkBytes) + lane;
       const uint4 wv[2] = {src[0], src[kChunkBytes / 16]};
+      const int nch = 2 * static_cast<int64_t>(kb0 + i) + 1 < kc ? 2 : 1;  // chunks below Kp
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        if (h >= nch) break;
+        const uint32_t wd[4] = {wv[h].x, wv[h].y, wv[h].z, wv[h].w};
+#pragma unroll
+        for (int w4 = 0; w4 < 4; ++w4)
+          su += __popc(wd[w4] & 0x55555555u) + 2u * __popc(wd[w4] & 0xAAAAAAAAu);
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive(&wempty[sw]);
       if (i == kAStages) grid_dep_wait();  // later stages wait on MMAs that need activations
@@ -395,11 +432,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // stores (a store may alias them) and the next group's residuals are fetched while the
     // current group is written.
     grid_dep_wait();
-    const int n = n0 + tid;  // thread = weight row n, columns = tokens
+    // thread = weight row n (TMEM lane tid), columns = tokens
+    const int n = p.pair ? (tid < 64 ? 64 * blockIdx.x + tid : p.pair * 32 + 64 * blockIdx.x + tid - 64)
+                         : n0 + tid;
     const bool n_ok = n < a.N;
-    if (tid < BN) s_rowsum[tid] = t0 + tid < a.M ? a.rowsum[t0 + tid] : 0;
+    if (tid < BN) s_rowsum[tid] = t0 + tid < a.M ? P.rowsum[t0 + tid] : 0;
     const bool direct = p.splits == 1;
-    const bool add_resid = a.resid && a.out;
+    const bool add_resid = a.resid && P.out;
     auto load16 = [&](int c0, float (&r)[16]) {
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
@@ -414,18 +453,41 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (!done) atomicOr(&s_fail, 1u);
     named_sync(1, 128);  // row sums staged; the decision below is uniform over the 4 warps
     const bool fail = s_fail != 0;
-    // dequant (+ residual) of 16 finished int32 accumulators of tokens t0 + c0 + [0, 16)
+    // dequant (+ residual) of 16 finished int32 accumulators of tokens t0 + c0 + [0, 16);
+    // a SwiGLU pair then combines gate row c (thread c) with up row I + c (thread 64 + c).
+    // Called by all 128 epilogue threads alike (the pair exchange synchronises them).
     auto emit16 = [&](int c0, const uint32_t (&v)[16], const float (&r)[16]) {
+      float o[16];
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int t = t0 + c0 + j;
-        if (!n_ok || t >= a.M) continue;
         const int32_t acc = static_cast<int32_t>(v[j] - static_cast<uint32_t>(s_rowsum[c0 + j]));
-        if (a.acc_out) a.acc_out[static_cast<int64_t>(t) * a.N + n] = acc;
-        if (a.out) {
-          float o = __fmul_rn(__int2float_rn(acc), a.scale);
-          if (a.resid) o = __fadd_rn(r[j], o);
-          a.out[static_cast<int64_t>(t) * a.ldo + n] = o;
+        if (a.acc_out && n_ok && t < a.M) a.acc_out[static_cast<int64_t>(t) * a.N + n] = acc;
+        o[j] = __fmul_rn(__int2float_rn(acc), P.scale);
+        if (a.resid) o[j] = __fadd_rn(r[j], o[j]);
+      }
+      if (!p.pair) {
+        if (P.out)
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (n_ok && t0 + c0 + j < a.M) P.out[static_cast<int64_t>(t0 + c0 + j) * a.ldo + n] = o[j];
+        return;
+      }
+      float* xch = reinterpret_cast<float*>(bst);  // [16][64]: the B ring is idle after the MMAs
+      named_sync(1, 128);                          // the previous group has been read
+      if (tid >= 64)
+#pragma unroll
+        for (int j = 0; j < 16; ++j) xch[j * 64 + tid - 64] = o[j];
+      named_sync(1, 128);
+      if (tid < 64) {
+        const int I = p.pair * 32;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int t = t0 + c0 + j;
+          if (t >= a.M) continue;
+          const int64_t e = static_cast<int64_t>(t) * I + n;
+          P.out[static_cast<int64_t>(t) * a.ldo + n] =
+              swiglu_x(o[j], xch[j * 64 + tid], in_body(e % p.seg, p.seg));
         }
       }
     };
@@ -438,7 +500,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tmem_ld16(tmem_dhi + lane_base + c0, dh);
         tmem_ld16(tmem_dlo + lane_base + c0, dl);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) part[j] = (dh[j] << 8) + dl[j];  // 256*D_hi + D_lo (mod 2^32)
+        // 256*D_hi + D_lo, with D_lo = D_lo' + 128*sum(u) for the low plane stored as lo - 128
+        for (int j = 0; j < 16; ++j) part[j] = (dh[j] << 8) + dl[j] + (su << 7);  // mod 2^32
         if (direct) {
           float rn[16];
           if (c0 + 16 < BN) load16(c0 + 16, rn);
@@ -448,7 +511,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         } else {
 #pragma unroll
           for (int j = 0; j < 16; ++j)
-            if (n_ok && t0 + c0 + j < a.M) atomicAdd(p.accum + static_cast<int64_t>(t0 + c0 + j) * a.N + n, part[j]);
+            if (n_ok && t0 + c0 + j < a.M) atomicAdd(P.accum + static_cast<int64_t>(t0 + c0 + j) * a.N + n, part[j]);
         }
       }
       if (!direct) {
@@ -456,8 +519,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         named_sync(1, 128);
         if (tid == 0) {
           const uint32_t tile = blockIdx.y * gridDim.x + blockIdx.x;
-          s_last = atomicAdd(p.tiles + tile, 1u) == static_cast<uint32_t>(p.splits - 1);
-          if (s_last) p.tiles[tile] = 0;
+          s_last = atomicAdd(P.tiles + tile, 1u) == static_cast<uint32_t>(p.splits - 1);
+          if (s_last) P.tiles[tile] = 0;
         }
         named_sync(1, 128);
         if (s_last) {
@@ -469,12 +532,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
               const int t = t0 + c0 + j;
-              sum[j] = (n_ok && t < a.M) ? __ldcg(p.accum + static_cast<int64_t>(t) * a.N + n) : 0u;
+              sum[j] = (n_ok && t < a.M) ? __ldcg(P.accum + static_cast<int64_t>(t) * a.N + n) : 0u;
             }
             load16(c0, r16);
 #pragma unroll
             for (int j = 0; j < 16; ++j)  // leave the workspace zeroed for the next launch
-              if (n_ok && t0 + c0 + j < a.M) p.accum[static_cast<int64_t>(t0 + c0 + j) * a.N + n] = 0;
+              if (n_ok && t0 + c0 + j < a.M) P.accum[static_cast<int64_t>(t0 + c0 + j) * a.N + n] = 0;
             emit16(c0, sum, r16);
           }
         }
@@ -532,55 +595,87 @@ cudaError_t planes_map(CUtensorMap* map, const int8_t* planes, int M, int64_t kp
 }  // namespace
 
 template <int BN>
-static cudaError_t launch_tc_bn(const TcArgs& p, bool pdl, cudaStream_t s) {
+static cudaError_t launch_tc_bn(const TcArgs& p, const MatmulArgs* a, bool pdl, cudaStream_t s) {
   using L = TcLayout<BN>;
-  CUtensorMap map;
-  cudaError_t e = planes_map(&map, p.m.planes, p.m.M, padded_k(p.m.K), BN);
-  if (e != cudaSuccess) return e;
+  TcMaps maps;
+  for (int j = 0; j < p.nproj; ++j) {
+    cudaError_t e = planes_map(&maps.m[j], a[j].planes, a[j].M, padded_k(a[j].K), BN);
+    if (e != cudaSuccess) return e;
+  }
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_set[dev & 63]) {
-    e = cudaFuncSetAttribute(tc_matmul_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kDyn);
+    cudaError_t e = cudaFuncSetAttribute(tc_matmul_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kDyn);
     if (e != cudaSuccess) return e;
     attr_set[dev & 63] = true;
   }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(ceil_div(p.m.N, 128)), static_cast<unsigned>(ceil_div(p.m.M, BN)),
-                     static_cast<unsigned>(p.splits));
-  cfg.blockDim = dim3(kTcThreads);
-  cfg.dynamicSmemBytes = L::kDyn;
-  cfg.stream = s;
-  cudaLaunchAttribute attrs[1];
-  attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attrs[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attrs;
-  cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, tc_matmul_kernel<BN>, map, p);
+  const dim3 grid(static_cast<unsigned>(ceil_div(p.m.N, 128)), static_cast<unsigned>(ceil_div(p.m.M, BN)),
+                  static_cast<unsigned>(p.nproj * p.splits));
+  return launch_k(tc_matmul_kernel<BN>, grid, dim3(kTcThreads), L::kDyn, s, pdl, maps, p);
 }
 
 int tc_token_tile(int M) { return M <= 16 ? 16 : (M <= 32 ? 32 : 64); }
 
-int tc_splits(const MatmulArgs& a, int sm_count) {
+int tc_splits(const MatmulArgs& a, int sm_count, int nproj) {
   // enough CTAs to cover the SMs; every split keeps >= 2 k-blocks
-  const int64_t tiles = ceil_div(a.N, 128) * ceil_div(a.M, tc_token_tile(a.M));
+  const int64_t tiles = ceil_div(a.N, 128) * ceil_div(a.M, tc_token_tile(a.M)) * nproj;
   const int nkb = static_cast<int>((packed_chunks(a.K) + 1) / 2);
   int splits = 1;
   while (tiles * splits * 2 <= sm_count && nkb / (splits * 2) >= 2) splits *= 2;
   return splits;
 }
 
+// nproj projections of one shape in one launch (workspace slices j * M * N and j * tiles);
+// pair > 0: a SwiGLU gate_proj (N = 2I, pair = I / 32, out = z [M, I], tails per seg)
+static cudaError_t launch_tc(const MatmulArgs* a, int nproj, int pair, int64_t seg, int splits,
+                             cudaStream_t s) {
+  const MatmulArgs& m = a[0];
+  if (m.M <= 0 || m.N <= 0) return cudaSuccess;
+  const int nkb = static_cast<int>((packed_chunks(m.K) + 1) / 2);
+  if (nproj < 1 || nproj > 3 || splits < 1 || splits > nkb) return cudaErrorInvalidValue;
+  if (pair && (nproj != 1 || m.N != 64 * pair || pair % 2 != 0)) return cudaErrorInvalidValue;
+  for (int j = 0; j < nproj; ++j)
+    if (a[j].M != m.M || a[j].N != m.N || a[j].K != m.K || !a[j].lo_signed) return cudaErrorInvalidValue;
+  const size_t mn = static_cast<size_t>(m.M) * m.N;
+  const size_t tiles = static_cast<size_t>(tc_tile_count(m.M, m.N));
+  if (splits > 1 && (!m.tc_accum || m.tc_accum_words < nproj * mn || !m.tc_tiles ||
+                     m.tc_tiles_words < nproj * tiles))
+    return cudaErrorInvalidValue;
+  TcArgs p{};
+  p.m = m;
+  p.nproj = nproj;
+  p.pair = pair;
+  p.seg = seg > 0 ? seg : 1;
+  p.err = m.err;
+  p.splits = splits;
+  for (int j = 0; j < nproj; ++j)
+    p.pj[j] = TcProj{a[j].w, a[j].rowsum, a[j].out, a[j].scale,
+                     splits > 1 ? m.tc_accum + j * mn : nullptr, splits > 1 ? m.tc_tiles + j * tiles : nullptr};
+  switch (tc_token_tile(m.M)) {
+    case 16: return launch_tc_bn<16>(p, a, m.pdl, s);
+    case 32: return launch_tc_bn<32>(p, a, m.pdl, s);
+    default: return launch_tc_bn<64>(p, a, m.pdl, s);
+  }
+}
+
 cudaError_t launch_matmul_tc(const MatmulArgs& a, uint32_t* accum, uint32_t* tiles, int splits,
                              uint32_t* err, cudaStream_t s) {
-  if (a.M <= 0 || a.N <= 0) return cudaSuccess;
-  const int nkb = static_cast<int>((packed_chunks(a.K) + 1) / 2);
-  if (splits < 1 || splits > nkb) return cudaErrorInvalidValue;  // every split owns a k-block
-  TcArgs p{a, accum, tiles, err, splits};
-  switch (tc_token_tile(a.M)) {
-    case 16: return launch_tc_bn<16>(p, a.pdl, s);
-    case 32: return launch_tc_bn<32>(p, a.pdl, s);
-    default: return launch_tc_bn<64>(p, a.pdl, s);
-  }
+  MatmulArgs b = a;
+  b.tc_accum = accum;
+  b.tc_tiles = tiles;
+  b.err = err;
+  return launch_tc(&b, 1, 0, 1, splits, s);
+}
+
+cudaError_t launch_matmul_tc_group(const MatmulArgs* a, int nproj, int swiglu_I, int64_t seg,
+                                   int sm_count, cudaStream_t s) {
+  int splits = tc_splits(a[0], sm_count, nproj);
+  const size_t mn = static_cast<size_t>(a[0].M) * a[0].N;
+  if (splits > 1 && (!a[0].tc_accum || a[0].tc_accum_words < nproj * mn || !a[0].tc_tiles ||
+                     a[0].tc_tiles_words < nproj * static_cast<size_t>(tc_tile_count(a[0].M, a[0].N))))
+    splits = 1;
+  return launch_tc(a, nproj, swiglu_I > 0 ? swiglu_I / 32 : 0, seg, splits, s);
 }
 
 }  // namespace mmfree_cuda
