@@ -169,6 +169,16 @@ def cpu_reference(steps: int, warmup: int, threads: int | None = None):
             "ms_per_step": 1e3 * dec_s / max(steps, 1)}
 
 
+def load_traffic():
+    """DRAM bytes per launch by kernel class, summarised from ncu captures in profiles/."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return {}
+
+
 def run_reference_arm(a, rank, world):
     if rank != 0:
         return
@@ -235,7 +245,7 @@ def run_ours(a, rank, world, local):
 
     # e2e through the public per-step API: pinned host ids in, next ids out, every step
     first = model.serve_begin(shard)
-    K_e2e = min(K, 128)
+    K_e2e = max(1, min(K, a.e2e_steps))
     hin = torch.empty(S, dtype=torch.int64).pin_memory()
     hout = torch.empty(S, dtype=torch.int64).pin_memory()
     hin.copy_(torch.from_numpy(first))
@@ -302,6 +312,17 @@ def run_ours(a, rank, world, local):
         roof = {"bound": "hbm", "achieved": gbs, "peak": float(peaks["hbm_gbs"]), "unit": "GB/s",
                 "frac": gbs / float(peaks["hbm_gbs"]), "traffic": None,
                 "peak_source": f"hbm_gbs of {src} peaks"}
+    # DRAM traffic per launch of the same kernel class from an ncu capture (profiles/)
+    tr = load_traffic().get("bitlinear_matmul")
+    if tr:
+        # the class's packed weight bytes per launch (every projection of every layer once
+        # per step) times the DRAM bytes per weight byte the capture measured
+        H, I, L = 2048, 5632, 24
+        pk = lambda n, k: -(-n // 32) * -(-k // 64) * 512
+        wstep = L * (4 * pk(H, H) + pk(2 * I, H) + pk(H, I))
+        per_launch = wstep / (mm["launches"] / prof_steps)
+        roof["traffic"] = tr["dram_bytes_per_weight_byte"] * per_launch
+        roof["traffic_source"] = tr["source"]
     roof.update({"kernel": "bitlinear_matmul (all per-layer BitLinear projections)",
                  "launches_per_step": mm["launches"] / prof_steps,
                  "avg_launch_us": 1e3 * mm["ms"] / mm["launches"],
@@ -396,6 +417,8 @@ def main():
     ap.add_argument("--op", default=None,
                     help="configuration 1 instead: 'sweep' or 'M,K,N' (isolated BitLinear)")
     ap.add_argument("--op-reps", type=int, default=50)
+    ap.add_argument("--e2e-steps", type=int, default=128,
+                    help="decode steps of the end-to-end (host ids in/out) measurement")
     ap.add_argument("--steps", type=int, default=500)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
