@@ -134,14 +134,14 @@ def allmax(v: float, world: int) -> float:
     return float(t.item())
 
 
-def blob_path(rank, world):
+def blob_path(rank, world, name="1.3B"):
     from matmulfreellmcpu_b200 import blob as B
     cache = os.environ.get("MMFREE_BLOB_CACHE", "/tmp/mmfree_blobs")
     if rank == 0:
-        p = B.cached_blob("1.3B", 0, cache)
+        p = B.cached_blob(name, 0, cache)
     barrier(world)
     if rank != 0:
-        p = B.cached_blob("1.3B", 0, cache)  # written by rank 0 already
+        p = B.cached_blob(name, 0, cache)  # written by rank 0 already
     return p
 
 
@@ -182,6 +182,20 @@ def load_traffic():
 
 def run_reference_arm(a, rank, world):
     if rank != 0:
+        return
+    if getattr(a, "workload", "decode") == "prefill":
+        cb = cpu_prefill()
+        line = {"impl": "reference", "metric": "HGRN-Bit 2.7B prefill tok/s (8 x 2048 tokens)",
+                "value": cb["value"], "unit": "tok/s", "n_gpus": world, "steps": 1, "warmup": 1,
+                "ms_per_step": cb["ms_per_step"], "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": DTYPE, "data": "synthetic (seeded random-init blob)",
+                "config": {"workload": "config4: 2.7B prefill (CPU sample: one prompt)",
+                           "model": "HGRN-Bit 2.7B random-init seed 0", "mode": "fixed",
+                           "engine": "reference CPU (AVX2 + OpenMP)"},
+                "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
         return
     steps = max(1, min(a.steps, 4))
     cb = cpu_reference(steps, min(a.warmup, 1))
@@ -358,6 +372,111 @@ def run_ours(a, rank, world, local):
     model.close()
 
 
+# ------------------------------------------------------------------ configuration 4: prefill
+P4_SEQS, P4_LEN = 8, 2048   # 2.7B, 8 x 2048 seeded tokens, prefill only
+P4_CPU_LEN = 64             # CPU reference sample: one prompt of this length
+
+
+def p4_prompts():
+    from matmulfreellmcpu_b200.blob import seeded_ids
+    return [seeded_ids(P4_LEN, 4000 + b) for b in range(P4_SEQS)]
+
+
+def p4_ops_per_token():
+    """Algorithmic int ops per prefill token: 2 x the per-layer BitLinear weights (the head
+    runs on one row per sequence and is left out)."""
+    H, I, L = 2560, 6912, 32
+    return 2.0 * L * (4 * H * H + 2 * I * H + I * H)
+
+
+def cpu_prefill(threads=0):
+    """The reference engine's Model::forward on one P4_CPU_LEN-token prompt of the 2.7B blob,
+    timed on this host; tok/s = prompt tokens / seconds."""
+    import oracle
+    from matmulfreellmcpu_b200.blob import seeded_ids
+    R = oracle.Reference()
+    if threads:
+        R.set_threads(threads)
+    m = R.model(blob_path(0, 1, "2.7B"), 1)
+    ids = seeded_ids(P4_CPU_LEN, 4000)
+    m.forward(ids[:8])  # warm-up (page the weights in)
+    t0 = time.perf_counter()
+    m.forward(ids)
+    dt = time.perf_counter() - t0
+    m.close()
+    return {"value": P4_CPU_LEN / dt, "unit": "tok/s", "cores": R.threads(), "kind": "reference",
+            "sample": f"Model::forward of one {P4_CPU_LEN}-token prompt (2.7B, fixed) in {dt:.2f} s",
+            "ms_per_step": 1e3 * dt}
+
+
+def run_prefill(a, rank, world, local):
+    """Configuration 4: batched prefill of 8 x 2048 tokens on the 2.7B model (the last
+    position's logits and argmax plus the final recurrent states of every sequence).
+    Sequences are sharded over ranks (sequence-parallel, no data-path collective)."""
+    import torch
+
+    from matmulfreellmcpu_b200 import api
+    from matmulfreellmcpu_b200.dp import shard_bounds
+
+    torch.cuda.set_device(local)
+    model = api.Model(blob_path(rank, world, "2.7B"), a.mode, 10, device=local)
+    stream = torch.cuda.ExternalStream(model.stream_ptr, device=torch.device("cuda", local))
+    b0, b1 = shard_bounds(P4_SEQS, rank, world)
+    shard = p4_prompts()[b0:b1]
+    K, W = max(1, min(a.steps, 20)), a.warmup
+    for _ in range(max(W, 1)):
+        if shard:
+            model.serve_begin(shard)
+            model.serve_end()
+    barrier(world)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        ev0.record(stream)
+        for _ in range(K):
+            if shard:
+                model.serve_begin(shard)  # host ids in, first ids out: the public API call
+                model.serve_end()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = allmax(ev0.elapsed_time(ev1), world)
+    tokens = P4_SEQS * P4_LEN * K
+    value = tokens / (ms / 1e3)
+    if rank != 0:
+        model.close()
+        return
+    peaks, src = load_peaks()
+    int8_peak = 2.0 * float(peaks["bf16_tflops"])
+    tops = p4_ops_per_token() * tokens / (ms / 1e3) / 1e12
+    cpu = None
+    if world == 1 and not a.no_cpu:
+        try:
+            cb = cpu_prefill()
+            cpu = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        except Exception as ex:
+            cpu = {"value": None, "unit": "tok/s", "cores": None, "kind": "reference",
+                   "sample": f"unavailable: {ex}"}
+    line = {"metric": "HGRN-Bit 2.7B prefill tok/s (8 x 2048 tokens)", "value": value,
+            "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms / K,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": DTYPE,
+            "data": "synthetic (seeded random-init 2.7B blob, seeded prompt ids)",
+            "config": {"workload": "config4: 2.7B prefill, 8 sequences x 2048 tokens",
+                       "model": "HGRN-Bit 2.7B random-init seed 0 (L32 H2560 I6912 V32000)",
+                       "mode": a.mode, "parallelism": f"sp{world} (sequences sharded, no collective)",
+                       "l2": "no flush: 655 MB packed weights > 126 MB L2 per forward"},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 8 * P4_SEQS * P4_LEN,
+                    "d2h_bytes_per_step": 8 * P4_SEQS,
+                    "note": "each step is the public serve_begin call: host ids in, first ids out"},
+            "roofline": {"bound": "tensor", "achieved": tops, "peak": int8_peak, "unit": "TOP/s",
+                         "frac": tops / int8_peak, "traffic": None,
+                         "kernel": "whole prefill forward (algorithmic 2*T*weights int ops)",
+                         "peak_source": f"int8 dense = 2 x bf16_tflops of {src} peaks (no int8 entry)"},
+            "cpu_baseline": cpu, "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+    model.close()
+
+
 SWEEP_M = (1, 16, 64, 512, 4096)
 SWEEP_KN = ((1024, 1024), (1024, 5632), (2048, 2048), (2048, 11264), (5632, 2048),
             (2560, 13824), (6912, 2560))
@@ -423,6 +542,8 @@ def main():
     ap.add_argument("--steps", type=int, default=500)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode",
+                    help="decode: configuration 3 (default); prefill: configuration 4")
     ap.add_argument("--mode", choices=["fixed", "float"], default="fixed")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--b1-steps", type=int, default=B1_GEN - 1,
@@ -438,7 +559,10 @@ def main():
         return
     rank, world, local = dist_setup()
     try:
-        run_ours(a, rank, world, local)
+        if a.workload == "prefill":
+            run_prefill(a, rank, world, local)
+        else:
+            run_ours(a, rank, world, local)
     finally:
         if world > 1:
             import torch.distributed as dist
