@@ -1,13 +1,15 @@
 """Benchmark: HGRN-Bit 1.3B lockstep decode tok/s (configuration 3) on N B200s.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--workload decode|prefill] [--op sweep|M,K,N]
   (N > 1: launched by torch.distributed.run, one rank per GPU)
 
 Workload: the seeded random-init 1.3B blob (seed 0), 64
-independent streams with 256-id seeded prompts (seed 1000 + b), FixedQ510 greedy decode.
-The 64 streams are sharded over the N ranks (64/N each, no inter-GPU communication; total
-work fixed, so scaling is "strong"). One step = one lockstep decode step of every stream
-(64 new tokens in total); value = 64 * K / (max over ranks of the device time of K steps).
+independent streams with 256-id seeded prompts, FixedQ510 greedy decode. Every GPU serves its
+own 64 streams (rank r: seeds 1000 + 64 r + b; no inter-GPU communication, the streams share
+nothing but the weights), so the per-GPU batch stays b=64 and scaling is "weak". One step =
+one lockstep decode step of every stream (64 N new tokens); value = 64 N K / (max over ranks
+of the device time of K steps).
 The prefill of the prompts happens before the timed region (untimed), so the timed steps
 start from resident state. Weights (325 MB packed) exceed the 126 MB L2, so consecutive
 steps stream them from HBM without an explicit flush.
@@ -37,7 +39,7 @@ N_STREAMS = 64
 PROMPT_LEN = 256
 GEN_TOKENS = 512          # configuration 3: 512 generated tokens per stream
 B1_PROMPT, B1_GEN = 128, 256
-METRIC = "HGRN-Bit 1.3B decode tok/s (b=64 lockstep, 64 streams / N GPUs)"
+METRIC = "HGRN-Bit 1.3B decode tok/s (b=64 lockstep, 64 streams per GPU)"
 DTYPE = "q5.10-int16 x ternary(2-bit) -> int32"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 
@@ -51,9 +53,20 @@ def load_peaks():
     return PEAKS_FALLBACK, "fallback"
 
 
-def prompts_all():
+def prompts_for(rank: int):
+    """The 64 independent streams of one GPU (weak scaling: every rank serves its own 64;
+    rank 0's are the configuration's streams, seeds 1000 + b)."""
     from matmulfreellmcpu_b200.blob import seeded_ids
-    return [seeded_ids(PROMPT_LEN, 1000 + b) for b in range(N_STREAMS)]
+    return [seeded_ids(PROMPT_LEN, 1000 + N_STREAMS * rank + b) for b in range(N_STREAMS)]
+
+
+def host_threads() -> int:
+    """Host cores this process may use (torchrun sets OMP_NUM_THREADS=1 per worker, so the
+    CPU reference sets its thread count explicitly)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
 
 
 class Clocks:
@@ -154,8 +167,7 @@ def cpu_reference(steps: int, warmup: int, threads: int | None = None):
     import oracle
     from matmulfreellmcpu_b200.blob import seeded_ids
     R = oracle.Reference()
-    if threads:
-        R.set_threads(threads)
+    R.set_threads(threads or host_threads())
     path = blob_path(0, 1)
     m = R.model(path, 1)
     prompts = [seeded_ids(4, 1000 + b) for b in range(N_STREAMS)]
@@ -201,7 +213,7 @@ def run_reference_arm(a, rank, world):
     cb = cpu_reference(steps, min(a.warmup, 1))
     line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "tok/s",
             "n_gpus": world, "steps": steps, "warmup": min(a.warmup, 1),
-            "ms_per_step": cb["ms_per_step"], "higher_is_better": True, "scaling": "strong",
+            "ms_per_step": cb["ms_per_step"], "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": DTYPE, "data": "synthetic (seeded random-init blob)",
             "config": {"workload": "config3: 1.3B lockstep decode, 64 streams",
                        "model": "HGRN-Bit 1.3B random-init seed 0", "streams": N_STREAMS,
@@ -217,14 +229,12 @@ def run_ours(a, rank, world, local):
     import torch
 
     from matmulfreellmcpu_b200 import api
-    from matmulfreellmcpu_b200.dp import shard_bounds
 
     torch.cuda.set_device(local)
     path = blob_path(rank, world)
     model = api.Model(path, a.mode, 10, device=local)
     stream = torch.cuda.ExternalStream(model.stream_ptr, device=torch.device("cuda", local))
-    b0, b1 = shard_bounds(N_STREAMS, rank, world)
-    shard = prompts_all()[b0:b1]
+    shard = prompts_for(rank)  # weak scaling: 64 independent streams on every GPU
     S = len(shard)
     budget = GEN_TOKENS - 1  # decode steps available after the prefill token
     K = min(a.steps, budget)
@@ -247,7 +257,7 @@ def run_ours(a, rank, world, local):
         torch.cuda.nvtx.range_pop()
     barrier(world)
     ms = allmax(ev0.elapsed_time(ev1), world)
-    value = N_STREAMS * K / (ms / 1e3)
+    value = N_STREAMS * world * K / (ms / 1e3)  # all ranks' tokens / the slowest rank's time
 
     # per-kernel-class breakdown of the same decode steps (event pairs, not graph-captured)
     prof_steps = min(16, max(1, budget - K)) if budget - K > 0 else 8
@@ -277,7 +287,7 @@ def run_ours(a, rank, world, local):
     torch.cuda.synchronize()
     ms_e2e = allmax(e0.elapsed_time(e1), world)
     model.serve_end()
-    e2e = N_STREAMS * K_e2e / (ms_e2e / 1e3)
+    e2e = N_STREAMS * world * K_e2e / (ms_e2e / 1e3)
 
     # b = 1 decode (configuration 2 shape: 128-id prompt, 255 decode steps), rank 0
     b1 = None
@@ -354,13 +364,14 @@ def run_ours(a, rank, world, local):
                    "sample": f"unavailable: {ex}"}
 
     line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K,
-            "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong",
+            "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": DTYPE,
             "data": "synthetic (seeded random-init 1.3B blob, seeded prompt ids)",
             "config": {"workload": "config3: 1.3B lockstep decode, 64 streams, 256-id prompts",
                        "model": "HGRN-Bit 1.3B random-init seed 0 (L24 H2048 I5632 V32000)",
-                       "streams": N_STREAMS, "streams_per_gpu": S, "prompt_len": PROMPT_LEN,
-                       "mode": a.mode, "parallelism": f"dp{world} (independent streams)",
+                       "streams": N_STREAMS * world, "streams_per_gpu": S, "prompt_len": PROMPT_LEN,
+                       "mode": a.mode,
+                       "parallelism": f"dp{world} (64 independent streams per GPU, no collective)",
                        "l2": "no flush: 325 MB packed weights > 126 MB L2 per step"},
             "e2e": {"value": e2e, "unit": "tok/s", "steps": K_e2e,
                     "h2d_bytes_per_step": 8 * S + 16, "d2h_bytes_per_step": 8 * S},
@@ -395,8 +406,7 @@ def cpu_prefill(threads=0):
     import oracle
     from matmulfreellmcpu_b200.blob import seeded_ids
     R = oracle.Reference()
-    if threads:
-        R.set_threads(threads)
+    R.set_threads(threads or host_threads())
     m = R.model(blob_path(0, 1, "2.7B"), 1)
     ids = seeded_ids(P4_CPU_LEN, 4000)
     m.forward(ids[:8])  # warm-up (page the weights in)
