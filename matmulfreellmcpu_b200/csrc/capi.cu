@@ -130,17 +130,7 @@ void run_bitlinear(int k, float* const* outs, const float* x, const float* const
   if (rows == 0) return;
   const size_t kp = static_cast<size_t>(padded_k(static_cast<int64_t>(in_dim)));
   const size_t per = fixed ? a256(2 * rows * kp) + a256(rows * 4) : a256(rows * kp * 4);
-  // split-K workspace of the tensor-core path (small row counts only)
-  const size_t accum_words = (fixed && rows <= 512) ? rows * out_dim : 0;
-  const size_t tiles_words = fixed ? static_cast<size_t>(tc_tile_count(static_cast<int>(rows),
-                                                                        static_cast<int>(out_dim)))
-                                   : 0;
-  const size_t ws_bytes = a256(accum_words * 4) + a256(tiles_words * 4);
-  char* base = scratch(static_cast<size_t>(k) * per + ws_bytes);
-  uint32_t* tc_accum = reinterpret_cast<uint32_t*>(base + 256 + static_cast<size_t>(k) * per);
-  uint32_t* tc_tiles = reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(tc_accum) +
-                                                   a256(accum_words * 4));
-  if (ws_bytes) ck(cudaMemsetAsync(tc_accum, 0, ws_bytes, st), "cudaMemsetAsync(workspace)");
+  char* base = scratch(static_cast<size_t>(k) * per);
   PrepArgs p;
   p.x = x;
   p.nproj = k;
@@ -179,10 +169,6 @@ void run_bitlinear(int k, float* const* outs, const float* x, const float* const
     a.fixed = fixed;
     a.allow_tc = true;
     a.lo_signed = p.lo_signed;
-    a.tc_accum = tc_accum;
-    a.tc_accum_words = accum_words;
-    a.tc_tiles = tc_tiles;
-    a.tc_tiles_words = tiles_words;
     a.err = reinterpret_cast<uint32_t*>(base);
     ck(launch_matmul(a, st), "matmul kernel");
   }

@@ -407,11 +407,7 @@ cudaError_t launch_matmul(const MatmulArgs& a, cudaStream_t s) {
   if (a.M <= 0 || a.N <= 0) return cudaSuccess;
   if (matmul_uses_tc(a)) {
     if (!a.lo_signed) return cudaErrorInvalidValue;  // planes in the wrong form
-    int splits = tc_splits(a, sm_count());
-    if (splits > 1 && (!a.tc_accum || a.tc_accum_words < static_cast<size_t>(a.M) * a.N ||
-                       !a.tc_tiles || a.tc_tiles_words < static_cast<size_t>(tc_tile_count(a.M, a.N))))
-      splits = 1;
-    return launch_matmul_tc(a, a.tc_accum, a.tc_tiles, splits, a.err, s);
+    return launch_matmul_tc(a, tc_splits(a, sm_count()), s);
   }
   if (a.M == 1) return launch_matmul_mt<1>(a, s);
   if (a.M == 2) return launch_matmul_mt<2>(a, s);

@@ -47,13 +47,9 @@ struct MatmulArgs {
   int ldr = 0;
   int32_t* acc_out = nullptr;     // optional [M, N] raw int32 accumulators (fixed)
   bool fixed = true;
-  // tensor-core path (FixedQ510, M >= kTcMinRows): opt-in, plus an optional split-K
-  // workspace (zeroed once; every launch leaves it zeroed) and a device error word
+  // tensor-core path (FixedQ510, M >= kTcMinRows): opt-in, plus a device error word
+  // (split-K partials are reduced inside a thread-block cluster: no workspace)
   bool allow_tc = false;
-  uint32_t* tc_accum = nullptr;   // >= M*N words for split-K
-  size_t tc_accum_words = 0;
-  uint32_t* tc_tiles = nullptr;   // one counter per output tile
-  size_t tc_tiles_words = 0;
   uint32_t* err = nullptr;
   bool pdl = false;               // launch as a programmatic dependent of the previous kernel
   bool lo_signed = false;         // planes hold lo - 128 (required by the tensor-core path)
@@ -122,18 +118,13 @@ cudaError_t launch_dec_persist(const DecArgs* dev_phases, int nphases, int M, un
 // tcgen05 BitLinear matmul (tc_matmul.cu)
 int tc_token_tile(int M);
 int tc_splits(const MatmulArgs& a, int sm_count, int nproj = 1);
-cudaError_t launch_matmul_tc(const MatmulArgs& a, uint32_t* accum, uint32_t* tiles, int splits,
-                             uint32_t* err, cudaStream_t s);
+cudaError_t launch_matmul_tc(const MatmulArgs& a, int splits, cudaStream_t s);
 // Several tensor-core BitLinears in one launch: nproj (1..3) projections of one shape (the
-// i/f/g cluster; a[0] carries the shared workspace, error word and launch mode), or with
+// i/f/g cluster; a[0] carries the error word and the launch mode), or with
 // swiglu_I > 0 (I % 64 == 0, nproj 1) a gate_proj of N = 2I whose epilogue writes
 // a[0].out = z [M, I] = silu(y[:, :I]) * y[:, I:] with SIMD tails per seg elements.
 cudaError_t launch_matmul_tc_group(const MatmulArgs* a, int nproj, int swiglu_I, int64_t seg,
                                    int sm_count, cudaStream_t s);
-// output tiles of the tcgen05 path (split-K counters needed)
-inline int64_t tc_tile_count(int M, int N) {
-  return ((N + 127) / 128) * static_cast<int64_t>((M + tc_token_tile(M) - 1) / tc_token_tile(M));
-}
 
 // int8 ternary [n, k] (nn.Linear layout) -> tiled 2-bit format; entries outside {-1,0,1}
 // set bit 2 (kErrNotTernary) of *err (nullable) and are packed by sign.

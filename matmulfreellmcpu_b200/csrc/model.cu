@@ -208,12 +208,6 @@ void Model::ensure_ws(size_t rows) {
          o_fb = carve(rows * H * 4), o_gb = carve(rows * H * 4), o_recur = carve(rows * H * 4),
          o_y = carve(rows * 2 * I * 4), o_z = carve(rows * I * 4), o_lg = carve(rows * V * 4),
          o_hl = carve(rows * H * 4), o_ids = carve(rows * 8);
-  // split-K workspace of the tensor-core matmul (decode-sized row counts)
-  const size_t maxn = std::max({V, 2 * I, H});
-  const size_t acc_rows = std::min<size_t>(rows, 512);
-  tc_accum_words_ = fixed_ ? acc_rows * maxn : 0;
-  tc_tiles_words_ = fixed_ ? static_cast<size_t>(tc_tile_count(static_cast<int>(rows), static_cast<int>(maxn))) : 0;
-  const size_t o_acc = carve(tc_accum_words_ * 4), o_tiles = carve(tc_tiles_words_ * 4);
   size_t o_pl[3], o_rs[3], o_yf[3];
   for (int j = 0; j < 3; ++j) {
     o_pl[j] = fixed_ ? carve(2 * rows * Kp) : 0;
@@ -233,9 +227,6 @@ void Model::ensure_ws(size_t rows) {
   logits_ = reinterpret_cast<float*>(b + o_lg);
   hl_ = reinterpret_cast<float*>(b + o_hl);
   ids_ = reinterpret_cast<int64_t*>(b + o_ids);
-  tc_accum_ = reinterpret_cast<uint32_t*>(b + o_acc);
-  tc_tiles_ = reinterpret_cast<uint32_t*>(b + o_tiles);
-  CK(cudaMemsetAsync(b + o_acc, 0, o_tiles + tc_tiles_words_ * 4 - o_acc, stream_));
   for (int j = 0; j < 3; ++j) {
     planes_[j] = fixed_ ? reinterpret_cast<int8_t*>(b + o_pl[j]) : nullptr;
     rowsum_[j] = reinterpret_cast<int32_t*>(b + o_rs[j]);
@@ -344,10 +335,6 @@ MatmulArgs Model::mm_args(const Proj& p, int plane, float* out, int M, const flo
   a.ldr = p.out;
   a.fixed = fixed_;
   a.allow_tc = true;
-  a.tc_accum = tc_accum_;
-  a.tc_accum_words = tc_accum_words_;
-  a.tc_tiles = tc_tiles_;
-  a.tc_tiles_words = tc_tiles_words_;
   a.err = err_;
   a.pdl = pdl_;
   a.lo_signed = tc_rows(M);

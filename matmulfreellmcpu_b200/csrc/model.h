@@ -157,9 +157,6 @@ class Model {
   int32_t* rowsum_[3] = {};
   float* yf_[3] = {};
   int64_t* ids_ = nullptr;
-  uint32_t* tc_accum_ = nullptr;   // split-K partial sums (kept zero between launches)
-  uint32_t* tc_tiles_ = nullptr;
-  size_t tc_accum_words_ = 0, tc_tiles_words_ = 0;
 
   // state and decode loop
   float* state_ = nullptr;

@@ -113,6 +113,21 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
 __device__ __forceinline__ void named_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
+// all threads of all CTAs of the cluster (release / acquire of shared memory)
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// address of the same shared-memory location in CTA `rank` of this cluster
+__device__ __forceinline__ uint32_t cluster_map(uint32_t saddr, int rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ uint32_t ld_cluster_u32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
 
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -190,8 +205,6 @@ struct TcProj {
   const int32_t* rowsum;   // [M] code sums of the projection's activation rows
   float* out;              // [M, ldo]
   float scale;             // 1 / (2^f * scale_w)
-  uint32_t* accum;         // split-K: [M, N] int32 partial sums (zero on entry and exit)
-  uint32_t* tiles;         // split-K: one arrival counter per output tile (zero on entry, exit)
 };
 
 struct TcArgs {
@@ -201,7 +214,7 @@ struct TcArgs {
   int pair;           // SwiGLU gate_proj: I/32, the first group of the up rows; 0 otherwise
   int64_t seg;        // SwiGLU: elements of one reference vector call (SIMD tails)
   uint32_t* err;      // bit kErrTimeout on a timed-out wait
-  int splits;         // k-block ranges per tile
+  int splits;         // k-block ranges per tile = cluster size along z (1, 2, 4 or 8)
 };
 
 struct TcMaps {
@@ -239,7 +252,7 @@ __device__ __forceinline__ bool role_wait(uint64_t* bar, uint32_t parity, uint32
 }  // namespace
 
 template <int BN>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(kTcThreads, 2)
     tc_matmul_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcArgs p) {
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 64, "BN must be 16..64, a multiple of 16");
   constexpr int kCols = kAStages * 32 + 2 * BN;  // A stages + D_hi + D_lo
@@ -256,7 +269,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __shared__ uint64_t afull[kAStages], aempty[kAStages], dfull;
   __shared__ uint32_t tmem_base_sh;
   __shared__ uint32_t s_fail;
-  __shared__ uint32_t s_last;
   __shared__ int s_rowsum[BN];
 
   const MatmulArgs& a = p.m;
@@ -303,6 +315,57 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t tmem_a = tmem;                   // columns [0, 32*kAStages)
   const uint32_t tmem_dhi = tmem + kAStages * 32; // BN columns
   const uint32_t tmem_dlo = tmem_dhi + BN;        // BN columns
+
+  // ---- epilogue helpers (epilogue warps 0-3; thread = TMEM lane = weight row n)
+  const int n = p.pair ? (tid < 64 ? 64 * blockIdx.x + tid : p.pair * 32 + 64 * blockIdx.x + tid - 64)
+                       : n0 + tid;
+  const bool n_ok = tid < 128 && n < a.N;
+  uint32_t* xtile = reinterpret_cast<uint32_t*>(bst);                 // [BN][128] split-K partials
+  float* xch = reinterpret_cast<float*>(bst + BN * 128 * 4);          // [16][64] SwiGLU exchange
+  const bool add_resid = a.resid && P.out;
+  auto load16 = [&](int c0, float (&r)[16]) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int t = t0 + c0 + j;
+      r[j] = (add_resid && n_ok && t < a.M) ? a.resid[static_cast<int64_t>(t) * a.ldr + n] : 0.0f;
+    }
+  };
+  // dequant (+ residual) of 16 finished int32 accumulators of tokens t0 + c0 + [0, 16);
+  // a SwiGLU pair then combines gate row c (thread c) with up row I + c (thread 64 + c).
+  // Called by all 128 epilogue threads alike (the pair exchange synchronises them).
+  auto emit16 = [&](int c0, const uint32_t (&v)[16], const float (&r)[16]) {
+    float o[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int t = t0 + c0 + j;
+      const int32_t acc = static_cast<int32_t>(v[j] - static_cast<uint32_t>(s_rowsum[c0 + j]));
+      if (a.acc_out && n_ok && t < a.M) a.acc_out[static_cast<int64_t>(t) * a.N + n] = acc;
+      o[j] = __fmul_rn(__int2float_rn(acc), P.scale);
+      if (a.resid) o[j] = __fadd_rn(r[j], o[j]);
+    }
+    if (!p.pair) {
+      if (P.out)
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (n_ok && t0 + c0 + j < a.M) P.out[static_cast<int64_t>(t0 + c0 + j) * a.ldo + n] = o[j];
+      return;
+    }
+    named_sync(1, 128);  // the previous group has been read
+    if (tid >= 64)
+#pragma unroll
+      for (int j = 0; j < 16; ++j) xch[j * 64 + tid - 64] = o[j];
+    named_sync(1, 128);
+    if (tid < 64) {
+      const int I = p.pair * 32;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int t = t0 + c0 + j;
+        if (t >= a.M) continue;
+        const int64_t e = static_cast<int64_t>(t) * I + n;
+        P.out[static_cast<int64_t>(t) * a.ldo + n] = swiglu_x(o[j], xch[j * 64 + tid], in_body(e % p.seg, p.seg));
+      }
+    }
+  };
 
   if (warp == kWWarp) {
     // ---- weight producer: 4 groups x (1 or 2) chunks per k-block, contiguous per group
@@ -426,123 +489,82 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (lane == 0) mbar_arrive(&afull[sa]);
     }
     if (!ok) atomicOr(&s_fail, 1u);
-    // epilogue: row sums, residuals and the split-K workspace belong to earlier kernels.
-    // The code runs once per CTA, so every instruction is a cold instruction-cache miss:
-    // the loops over 16-token groups stay rolled. Loads of a group are issued before its
-    // stores (a store may alias them) and the next group's residuals are fetched while the
-    // current group is written.
+    // epilogue: row sums and residuals belong to earlier kernels. The code runs once per
+    // CTA, so every instruction is a cold instruction-cache miss: the loops over 16-token
+    // groups stay rolled. Loads of a group are issued before its stores (a store may alias
+    // them) and the next group's residuals are fetched while the current group is written.
     grid_dep_wait();
-    // thread = weight row n (TMEM lane tid), columns = tokens
-    const int n = p.pair ? (tid < 64 ? 64 * blockIdx.x + tid : p.pair * 32 + 64 * blockIdx.x + tid - 64)
-                         : n0 + tid;
-    const bool n_ok = n < a.N;
     if (tid < BN) s_rowsum[tid] = t0 + tid < a.M ? P.rowsum[t0 + tid] : 0;
-    const bool direct = p.splits == 1;
-    const bool add_resid = a.resid && P.out;
-    auto load16 = [&](int c0, float (&r)[16]) {
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int t = t0 + c0 + j;
-        r[j] = (add_resid && n_ok && t < a.M) ? a.resid[static_cast<int64_t>(t) * a.ldr + n] : 0.0f;
-      }
-    };
-    float rv[16];
-    if (direct) load16(0, rv);
     const bool done = mbar_wait(&dfull, 0);
     tc_fence_after();
     if (!done) atomicOr(&s_fail, 1u);
     named_sync(1, 128);  // row sums staged; the decision below is uniform over the 4 warps
-    const bool fail = s_fail != 0;
-    // dequant (+ residual) of 16 finished int32 accumulators of tokens t0 + c0 + [0, 16);
-    // a SwiGLU pair then combines gate row c (thread c) with up row I + c (thread 64 + c).
-    // Called by all 128 epilogue threads alike (the pair exchange synchronises them).
-    auto emit16 = [&](int c0, const uint32_t (&v)[16], const float (&r)[16]) {
-      float o[16];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int t = t0 + c0 + j;
-        const int32_t acc = static_cast<int32_t>(v[j] - static_cast<uint32_t>(s_rowsum[c0 + j]));
-        if (a.acc_out && n_ok && t < a.M) a.acc_out[static_cast<int64_t>(t) * a.N + n] = acc;
-        o[j] = __fmul_rn(__int2float_rn(acc), P.scale);
-        if (a.resid) o[j] = __fadd_rn(r[j], o[j]);
-      }
-      if (!p.pair) {
-        if (P.out)
-#pragma unroll
-          for (int j = 0; j < 16; ++j)
-            if (n_ok && t0 + c0 + j < a.M) P.out[static_cast<int64_t>(t0 + c0 + j) * a.ldo + n] = o[j];
-        return;
-      }
-      float* xch = reinterpret_cast<float*>(bst);  // [16][64]: the B ring is idle after the MMAs
-      named_sync(1, 128);                          // the previous group has been read
-      if (tid >= 64)
-#pragma unroll
-        for (int j = 0; j < 16; ++j) xch[j * 64 + tid - 64] = o[j];
-      named_sync(1, 128);
-      if (tid < 64) {
-        const int I = p.pair * 32;
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int t = t0 + c0 + j;
-          if (t >= a.M) continue;
-          const int64_t e = static_cast<int64_t>(t) * I + n;
-          P.out[static_cast<int64_t>(t) * a.ldo + n] =
-              swiglu_x(o[j], xch[j * 64 + tid], in_body(e % p.seg, p.seg));
-        }
-      }
-    };
-    if (fail) {
+    if (s_fail != 0) {
       if (tid == 0 && p.err) atomicOr(p.err, kErrTimeout);
     } else if (nk > 0) {
-#pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        uint32_t dh[16], dl[16], part[16];
+      // 256*D_hi + D_lo, with D_lo = D_lo' + 128*sum(u) for the low plane stored as lo - 128
+      auto part16 = [&](int c0, uint32_t (&v)[16]) {
+        uint32_t dh[16], dl[16];
         tmem_ld16(tmem_dhi + lane_base + c0, dh);
         tmem_ld16(tmem_dlo + lane_base + c0, dl);
 #pragma unroll
-        // 256*D_hi + D_lo, with D_lo = D_lo' + 128*sum(u) for the low plane stored as lo - 128
-        for (int j = 0; j < 16; ++j) part[j] = (dh[j] << 8) + dl[j] + (su << 7);  // mod 2^32
-        if (direct) {
+        for (int j = 0; j < 16; ++j) v[j] = (dh[j] << 8) + dl[j] + (su << 7);  // mod 2^32
+      };
+      if (p.splits == 1) {
+        float rv[16];
+        load16(0, rv);
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          uint32_t v[16];
+          part16(c0, v);
           float rn[16];
           if (c0 + 16 < BN) load16(c0 + 16, rn);
-          emit16(c0, part, rv);
+          emit16(c0, v, rv);
 #pragma unroll
           for (int j = 0; j < 16; ++j) rv[j] = rn[j];
-        } else {
-#pragma unroll
-          for (int j = 0; j < 16; ++j)
-            if (n_ok && t0 + c0 + j < a.M) atomicAdd(P.accum + static_cast<int64_t>(t0 + c0 + j) * a.N + n, part[j]);
         }
-      }
-      if (!direct) {
-        __threadfence();
-        named_sync(1, 128);
-        if (tid == 0) {
-          const uint32_t tile = blockIdx.y * gridDim.x + blockIdx.x;
-          s_last = atomicAdd(P.tiles + tile, 1u) == static_cast<uint32_t>(p.splits - 1);
-          if (s_last) P.tiles[tile] = 0;
-        }
-        named_sync(1, 128);
-        if (s_last) {
-          __threadfence();
+      } else {
+        // split-K: leave this CTA's partial tile in shared memory for the cluster leader
 #pragma unroll 1
-          for (int c0 = 0; c0 < BN; c0 += 16) {
-            uint32_t sum[16];
-            float r16[16];
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          uint32_t v[16];
+          part16(c0, v);
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int t = t0 + c0 + j;
-              sum[j] = (n_ok && t < a.M) ? __ldcg(P.accum + static_cast<int64_t>(t) * a.N + n) : 0u;
-            }
-            load16(c0, r16);
-#pragma unroll
-            for (int j = 0; j < 16; ++j)  // leave the workspace zeroed for the next launch
-              if (n_ok && t0 + c0 + j < a.M) P.accum[static_cast<int64_t>(t0 + c0 + j) * a.N + n] = 0;
-            emit16(c0, sum, r16);
-          }
+          for (int j = 0; j < 16; ++j) xtile[(c0 + j) * 128 + tid] = v[j];
         }
       }
     }
+  }
+
+  __syncwarp();
+  if (p.splits > 1) {
+    // split-K over the cluster (the CTAs of one output tile): after the first barrier every
+    // partial tile is in its CTA's shared memory; split 0 sums them over distributed shared
+    // memory and writes the tile; the second barrier keeps the others' shared memory alive
+    // until it has read them. Every CTA reaches both barriers, on the error paths too.
+    cluster_sync();
+    if (split == 0 && warp < 4 && s_fail == 0 && nk > 0) {
+      const uint32_t local = smem_u32(xtile) + 4u * static_cast<uint32_t>(tid);
+      float rv[16];
+      load16(0, rv);
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        uint32_t v[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = xtile[(c0 + j) * 128 + tid];
+        for (int r = 1; r < p.splits; ++r) {
+          const uint32_t peer = cluster_map(local + 4u * 128u * c0, r);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] += ld_cluster_u32(peer + 4u * 128u * j);
+        }
+        float rn[16];
+        if (c0 + 16 < BN) load16(c0 + 16, rn);
+        emit16(c0, v, rv);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) rv[j] = rn[j];
+      }
+    }
+    cluster_sync();
   }
   tc_fence_before();
   __syncthreads();
@@ -610,38 +632,54 @@ static cudaError_t launch_tc_bn(const TcArgs& p, const MatmulArgs* a, bool pdl, 
     if (e != cudaSuccess) return e;
     attr_set[dev & 63] = true;
   }
-  const dim3 grid(static_cast<unsigned>(ceil_div(p.m.N, 128)), static_cast<unsigned>(ceil_div(p.m.M, BN)),
-                  static_cast<unsigned>(p.nproj * p.splits));
-  return launch_k(tc_matmul_kernel<BN>, grid, dim3(kTcThreads), L::kDyn, s, pdl, maps, p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(ceil_div(p.m.N, 128)), static_cast<unsigned>(ceil_div(p.m.M, BN)),
+                     static_cast<unsigned>(p.nproj * p.splits));
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = L::kDyn;
+  cfg.stream = s;
+  cudaLaunchAttribute at[2];
+  int na = 0;
+  if (p.splits > 1) {  // the k-splits of one output tile form a cluster (reduced over DSMEM)
+    at[na].id = cudaLaunchAttributeClusterDimension;
+    at[na].val.clusterDim.x = 1;
+    at[na].val.clusterDim.y = 1;
+    at[na].val.clusterDim.z = static_cast<unsigned>(p.splits);
+    ++na;
+  }
+  if (pdl) {
+    at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = at;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, tc_matmul_kernel<BN>, maps, p);
 }
 
 int tc_token_tile(int M) { return M <= 16 ? 16 : (M <= 32 ? 32 : 64); }
 
 int tc_splits(const MatmulArgs& a, int sm_count, int nproj) {
-  // enough CTAs to cover the SMs; every split keeps >= 2 k-blocks
+  // enough CTAs to cover the SMs; every split keeps >= 2 k-blocks; a cluster holds <= 8 CTAs
   const int64_t tiles = ceil_div(a.N, 128) * ceil_div(a.M, tc_token_tile(a.M)) * nproj;
   const int nkb = static_cast<int>((packed_chunks(a.K) + 1) / 2);
   int splits = 1;
-  while (tiles * splits * 2 <= sm_count && nkb / (splits * 2) >= 2) splits *= 2;
+  while (splits < 8 && tiles * splits * 2 <= sm_count && nkb / (splits * 2) >= 2) splits *= 2;
   return splits;
 }
 
-// nproj projections of one shape in one launch (workspace slices j * M * N and j * tiles);
-// pair > 0: a SwiGLU gate_proj (N = 2I, pair = I / 32, out = z [M, I], tails per seg)
+// nproj projections of one shape in one launch; pair > 0: a SwiGLU gate_proj (N = 2I,
+// pair = I / 32, out = z [M, I], tails per seg)
 static cudaError_t launch_tc(const MatmulArgs* a, int nproj, int pair, int64_t seg, int splits,
                              cudaStream_t s) {
   const MatmulArgs& m = a[0];
   if (m.M <= 0 || m.N <= 0) return cudaSuccess;
   const int nkb = static_cast<int>((packed_chunks(m.K) + 1) / 2);
-  if (nproj < 1 || nproj > 3 || splits < 1 || splits > nkb) return cudaErrorInvalidValue;
+  if (nproj < 1 || nproj > 3 || splits < 1 || splits > 8 || (splits & (splits - 1)) || splits > nkb)
+    return cudaErrorInvalidValue;
   if (pair && (nproj != 1 || m.N != 64 * pair || pair % 2 != 0)) return cudaErrorInvalidValue;
   for (int j = 0; j < nproj; ++j)
     if (a[j].M != m.M || a[j].N != m.N || a[j].K != m.K || !a[j].lo_signed) return cudaErrorInvalidValue;
-  const size_t mn = static_cast<size_t>(m.M) * m.N;
-  const size_t tiles = static_cast<size_t>(tc_tile_count(m.M, m.N));
-  if (splits > 1 && (!m.tc_accum || m.tc_accum_words < nproj * mn || !m.tc_tiles ||
-                     m.tc_tiles_words < nproj * tiles))
-    return cudaErrorInvalidValue;
   TcArgs p{};
   p.m = m;
   p.nproj = nproj;
@@ -649,9 +687,7 @@ static cudaError_t launch_tc(const MatmulArgs* a, int nproj, int pair, int64_t s
   p.seg = seg > 0 ? seg : 1;
   p.err = m.err;
   p.splits = splits;
-  for (int j = 0; j < nproj; ++j)
-    p.pj[j] = TcProj{a[j].w, a[j].rowsum, a[j].out, a[j].scale,
-                     splits > 1 ? m.tc_accum + j * mn : nullptr, splits > 1 ? m.tc_tiles + j * tiles : nullptr};
+  for (int j = 0; j < nproj; ++j) p.pj[j] = TcProj{a[j].w, a[j].rowsum, a[j].out, a[j].scale};
   switch (tc_token_tile(m.M)) {
     case 16: return launch_tc_bn<16>(p, a, m.pdl, s);
     case 32: return launch_tc_bn<32>(p, a, m.pdl, s);
@@ -659,23 +695,13 @@ static cudaError_t launch_tc(const MatmulArgs* a, int nproj, int pair, int64_t s
   }
 }
 
-cudaError_t launch_matmul_tc(const MatmulArgs& a, uint32_t* accum, uint32_t* tiles, int splits,
-                             uint32_t* err, cudaStream_t s) {
-  MatmulArgs b = a;
-  b.tc_accum = accum;
-  b.tc_tiles = tiles;
-  b.err = err;
-  return launch_tc(&b, 1, 0, 1, splits, s);
+cudaError_t launch_matmul_tc(const MatmulArgs& a, int splits, cudaStream_t s) {
+  return launch_tc(&a, 1, 0, 1, splits, s);
 }
 
 cudaError_t launch_matmul_tc_group(const MatmulArgs* a, int nproj, int swiglu_I, int64_t seg,
                                    int sm_count, cudaStream_t s) {
-  int splits = tc_splits(a[0], sm_count, nproj);
-  const size_t mn = static_cast<size_t>(a[0].M) * a[0].N;
-  if (splits > 1 && (!a[0].tc_accum || a[0].tc_accum_words < nproj * mn || !a[0].tc_tiles ||
-                     a[0].tc_tiles_words < nproj * static_cast<size_t>(tc_tile_count(a[0].M, a[0].N))))
-    splits = 1;
-  return launch_tc(a, nproj, swiglu_I > 0 ? swiglu_I / 32 : 0, seg, splits, s);
+  return launch_tc(a, nproj, swiglu_I > 0 ? swiglu_I / 32 : 0, seg, tc_splits(a[0], sm_count, nproj), s);
 }
 
 }  // namespace mmfree_cuda
