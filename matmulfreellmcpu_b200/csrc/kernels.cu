@@ -15,12 +15,13 @@
 #include "kernels.h"
 
 #include <cfloat>
+#include <cstdlib>
 #include <mutex>
 
 namespace mmfree_cuda {
 
 namespace {
-constexpr int kPrepThreads = 256;
+constexpr int kPrepThreads = 512;  // prep: 16 warps share a row's elementwise passes
 constexpr int kMatmulThreads = 128;
 constexpr int kMaxDynSmem = 224 * 1024;  // below the 227 KB opt-in, leaving room for static smem
 }  // namespace
@@ -194,7 +195,7 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepArgs a, int mode
     __syncthreads();
     if (tid < a.nproj) {
       int total = 0;
-      for (int w = 0; w < kPrepThreads / 32; ++w) total += s_red[tid][w];
+      for (int w = 0; w < static_cast<int>(blockDim.x / 32); ++w) total += s_red[tid][w];
       a.rowsum[tid][m] = total;
     }
   }

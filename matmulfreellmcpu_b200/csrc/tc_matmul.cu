@@ -36,6 +36,7 @@
 
 #include <cuda.h>
 #include <cstdint>
+#include <cstdlib>
 
 namespace mmfree_cuda {
 
@@ -660,7 +661,8 @@ static cudaError_t launch_tc_bn(const TcArgs& p, const MatmulArgs* a, bool pdl, 
 int tc_token_tile(int M) { return M <= 16 ? 16 : (M <= 32 ? 32 : 64); }
 
 int tc_splits(const MatmulArgs& a, int sm_count, int nproj) {
-  // enough CTAs to cover the SMs; every split keeps >= 2 k-blocks; a cluster holds <= 8 CTAs
+  // about one CTA per SM (two per SM measured slower: the cluster reduction grows with the
+  // split count); every split keeps >= 2 k-blocks; a cluster holds <= 8 CTAs
   const int64_t tiles = ceil_div(a.N, 128) * ceil_div(a.M, tc_token_tile(a.M)) * nproj;
   const int nkb = static_cast<int>((packed_chunks(a.K) + 1) / 2);
   int splits = 1;
