@@ -8,7 +8,7 @@
 //           fp32 FMA (float), dequant and optional residual add in the epilogue.
 //           Restates ternary_backend.hpp:96-103 + simd.hpp:191-206 (+ hgrn_model.cpp:161-166,
 //           :189-194 for the residual).
-// gate/scan the HGRN token mixer (hgrn_model.cpp:109-150).
+// mixer    the HGRN token mixer (hgrn_model.cpp:109-150): gate + scan in one pass.
 // others    swiglu split (hgrn_model.cpp:171-185), embedding gather, greedy argmax.
 #include "common.cuh"
 #include "exact.cuh"
@@ -419,20 +419,6 @@ cudaError_t launch_matmul(const MatmulArgs& a, cudaStream_t s) {
 // ------------------------------------------------------------------------------ mixer
 // In place: f <- lower-bounded sigmoid(f); i <- silu(i) * (1 - f). The SIMD body/tail split
 // of element e is taken within its segment of seg elements (one reference block() call).
-__global__ void gate_kernel(float* __restrict__ i, float* __restrict__ f,
-                            const float* __restrict__ lb, int64_t n, int64_t seg, int H) {
-  grid_dep_launch();
-  grid_dep_wait();
-  const int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-  if (e >= n) return;
-  const bool body = in_body(e % seg, seg);
-  float fv = sigmoid_x(f[e], body);
-  if (lb) fv = lower_bound_x(fv, lb[e % H]);
-  const float onemf = __fadd_rn(1.0f, -fv);
-  i[e] = swiglu_x(i[e], onemf, body);
-  f[e] = fv;
-}
-
 // state = fma(f, state, s) along t for each of nseq x H lanes; x layout [nseq][T][H],
 // state [nseq][H] (nullable: zero start, not written back).
 __global__ void scan_kernel(float* __restrict__ out, const float* __restrict__ s,
@@ -454,16 +440,57 @@ __global__ void scan_kernel(float* __restrict__ out, const float* __restrict__ s
   if (state) state[lane] = st;
 }
 
+// The whole token mixer in one pass, one thread per (sequence, channel) lane: per step the
+// forget gate (sigmoid, lower bound), the SwiGLU scan input and the recurrence step, i.e.
+// the reference's gate loop (hgrn_model.cpp:109-134) followed by its scan (hgrn_scan.cpp:11-19)
+// without the intermediate arrays. Loads run kMixAhead steps ahead of the serial recurrence.
+constexpr int kMixAhead = 16;
+__global__ void __launch_bounds__(128) mixer_kernel(float* __restrict__ out, const float* __restrict__ iv,
+                                                    const float* __restrict__ fv, float* __restrict__ state,
+                                                    const float* __restrict__ lb, int nseq, int T, int H,
+                                                    int64_t seg) {
+  grid_dep_launch();
+  grid_dep_wait();
+  const int64_t lane = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (lane >= static_cast<int64_t>(nseq) * H) return;
+  const int64_t q = lane / H, c = lane % H;
+  const int64_t base = q * T * H + c;
+  const float lbc = lb ? __ldg(lb + c) : 0.0f;
+  const int64_t body_n = seg & ~int64_t(7);
+  int64_t es = base % seg;  // element index within its reference vector call (seg >= H)
+  float st = state ? state[lane] : 0.0f;
+  for (int t0 = 0; t0 < T; t0 += kMixAhead) {
+    float a[kMixAhead], b[kMixAhead];
+#pragma unroll
+    for (int u = 0; u < kMixAhead; ++u) {
+      const int64_t e = base + static_cast<int64_t>(t0 + u) * H;
+      a[u] = t0 + u < T ? __ldcs(iv + e) : 0.0f;
+      b[u] = t0 + u < T ? __ldcs(fv + e) : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < kMixAhead; ++u) {
+      if (t0 + u >= T) break;
+      const int64_t e = base + static_cast<int64_t>(t0 + u) * H;
+      const bool body = es < body_n;
+      es += H;
+      if (es >= seg) es -= seg;
+      float f = sigmoid_x(b[u], body);
+      if (lb) f = lower_bound_x(f, lbc);
+      const float sv = swiglu_x(a[u], __fadd_rn(1.0f, -f), body);
+      st = hgrn_step_x(f, st, sv);
+      out[e] = st;
+    }
+  }
+  if (state) state[lane] = st;
+}
+
 cudaError_t launch_mixer(float* i, float* f, float* recur, float* state, const float* lb,
                          int nseq, int len, int H, int seg_rows, cudaStream_t s, bool pdl) {
-  const int64_t n = static_cast<int64_t>(nseq) * len * H;
-  if (n == 0) return cudaSuccess;
-  cudaError_t e = launch_k(gate_kernel, dim3(static_cast<unsigned>(ceil_div(n, 256))), dim3(256), 0, s,
-                           pdl, i, f, lb, n, static_cast<int64_t>(seg_rows) * H, H);
-  if (e != cudaSuccess) return e;
   const int64_t lanes = static_cast<int64_t>(nseq) * H;
-  return launch_k(scan_kernel, dim3(static_cast<unsigned>(ceil_div(lanes, 128))), dim3(128), 0, s, pdl,
-                  recur, static_cast<const float*>(i), static_cast<const float*>(f), state, nseq, len, H);
+  if (lanes == 0 || len == 0) return cudaSuccess;
+  return launch_k(mixer_kernel, dim3(static_cast<unsigned>(ceil_div(lanes, 128))), dim3(128), 0, s, pdl,
+                  recur, static_cast<const float*>(i), static_cast<const float*>(f), state, lb, nseq, len,
+                  H, static_cast<int64_t>(seg_rows) * H);
 }
 
 cudaError_t launch_scan(float* out, const float* i, const float* f, int T, int D, float* state,

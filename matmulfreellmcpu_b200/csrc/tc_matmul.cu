@@ -45,7 +45,7 @@ namespace {
 constexpr int kTcThreads = 224;      // 7 warps (roles above)
 constexpr int kWWarp = 4, kBWarp = 5, kMmaWarp = 6;
 constexpr int kWStages = 8;          // weight k-blocks in shared memory
-constexpr int kBStages = 4;          // activation k-blocks in shared memory
+constexpr int kBStages1 = 4;         // activation k-blocks in shared memory (one token tile)
 constexpr int kAStages = 4;          // expanded weight k-blocks in tensor memory (32 columns)
 constexpr int kKBlock = 128;         // k per pipeline stage (2 packed chunks)
 constexpr int kWBlock = 4 * 2 * kChunkBytes;  // bytes of one weight k-block (4 groups)
@@ -226,15 +226,21 @@ namespace {
 
 // Smem layout of one CTA (offsets from a 1024-byte aligned base): the activation ring first
 // (1024-aligned stages, as the 128-byte swizzle wants), then the weight ring.
-template <int BN>
+// TT token tiles of BN rows share each expanded weight k-block (TT > 1: large M, one CTA
+// per SM, all 512 TMEM columns).
+template <int BN, int TT>
 struct TcLayout {
-  static constexpr int kBPlane = BN * 128;               // one plane of one k-block
-  static constexpr int kBStage = 2 * kBPlane;            // high + low plane
+  static constexpr int kBStages = TT == 1 ? kBStages1 : 3;
+  static constexpr int kBPlane = BN * 128;               // one plane of one token tile
+  static constexpr int kBTile = 2 * kBPlane;             // high + low plane of one token tile
+  static constexpr int kBStage = TT * kBTile;            // one k-block of every token tile
   static constexpr int kWOff = kBStages * kBStage;
   static constexpr int kBytes = kWOff + kWStages * kWBlock;
-  // at least 80 KB, so that no more than two CTAs (2 x 256 TMEM columns) share an SM and
-  // tcgen05.alloc never waits for a CTA of this kernel
+  // TT == 1: at least 80 KB, so that no more than two CTAs (2 x 256 TMEM columns) share an
+  // SM and tcgen05.alloc never waits for a CTA of this kernel; TT > 1 needs more than half
+  // of the SM's shared memory anyway (one CTA per SM, 512 columns)
   static constexpr int kDyn = (kBytes + 1024) < 80 * 1024 ? 80 * 1024 : (kBytes + 1024);
+  static_assert(TT == 1 || kDyn > 114 * 1024, "TT > 1 must keep one CTA per SM");
 };
 
 __device__ __forceinline__ bool cta_failed(const uint32_t* f) {
@@ -252,14 +258,16 @@ __device__ __forceinline__ bool role_wait(uint64_t* bar, uint32_t parity, uint32
 
 }  // namespace
 
-template <int BN>
+template <int BN, int TT>
 __global__ void __launch_bounds__(kTcThreads, 2)
     tc_matmul_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcArgs p) {
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 64, "BN must be 16..64, a multiple of 16");
-  constexpr int kCols = kAStages * 32 + 2 * BN;  // A stages + D_hi + D_lo
+  constexpr int kCols = kAStages * 32 + TT * 2 * BN;  // A stages + TT x (D_hi, D_lo)
   constexpr int kAllocCols = kCols <= 128 ? 128 : (kCols <= 256 ? 256 : 512);
-  static_assert(kAllocCols <= 256, "two CTAs per SM must fit in the 512 TMEM columns");
-  using L = TcLayout<BN>;
+  static_assert(kCols <= 512 && (TT > 1 || kAllocCols <= 256),
+                "two CTAs per SM must fit in the 512 TMEM columns");
+  using L = TcLayout<BN, TT>;
+  constexpr int kBStages = L::kBStages;
 
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
@@ -274,7 +282,8 @@ __global__ void __launch_bounds__(kTcThreads, 2)
 
   const MatmulArgs& a = p.m;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int n0 = blockIdx.x * 128, t0 = blockIdx.y * BN;
+  const int n0 = blockIdx.x * 128, tb = blockIdx.y * BN * TT;  // first token of the CTA
+  int t0 = tb;  // first token of the tile the epilogue works on
   const int proj = blockIdx.z / p.splits, split = blockIdx.z % p.splits;
   const TcProj& P = p.pj[proj];
   const CUtensorMap* bmap = &maps.m[proj];
@@ -412,8 +421,12 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         const int x = (kb0 + i) * kKBlock;
         unsigned char* dst = bst + s * L::kBStage;
         mbar_arrive_tx(&bfull[s], static_cast<uint32_t>(L::kBStage));
-        tma_load_2d(dst, bmap, x, t0, &bfull[s]);                  // high plane rows
-        tma_load_2d(dst + L::kBPlane, bmap, x, a.M + t0, &bfull[s]);  // low plane rows
+#pragma unroll
+        for (int tt = 0; tt < TT; ++tt) {
+          const int tr = tb + tt * BN;
+          tma_load_2d(dst + tt * L::kBTile, bmap, x, tr, &bfull[s]);                   // high rows
+          tma_load_2d(dst + tt * L::kBTile + L::kBPlane, bmap, x, a.M + tr, &bfull[s]);  // low rows
+        }
       }
       if (i < nk) {
         atomicOr(&s_fail, 1u);
@@ -433,15 +446,19 @@ __global__ void __launch_bounds__(kTcThreads, 2)
           break;
         }
         tc_fence_after();
-        const uint32_t hi_base = smem_u32(bst + sb * L::kBStage);
+        const uint32_t b_base = smem_u32(bst + sb * L::kBStage);
         // both planes in one instruction: B rows [0, BN) are the high bytes, [BN, 2BN) the
-        // low bytes - 128 (both s8, one 128-byte-swizzled tile), D columns likewise
+        // low bytes - 128 (both s8, one 128-byte-swizzled tile), D columns likewise; the
+        // same A (weight) columns serve every token tile
 #pragma unroll
-        for (int j = 0; j < kKBlock / 32; ++j) {
-          const uint32_t acc = (i > 0 || j > 0) ? 1u : 0u;
-          const uint32_t a_addr = tmem_a + static_cast<uint32_t>(sa * 32 + j * 8);
-          mma_i8_ts(tmem_dhi, a_addr, smem_desc_sw128(hi_base + j * 32), idesc_i8(true, 2 * BN), acc);
-        }
+        for (int tt = 0; tt < TT; ++tt)
+#pragma unroll
+          for (int j = 0; j < kKBlock / 32; ++j) {
+            const uint32_t acc = (i > 0 || j > 0) ? 1u : 0u;
+            const uint32_t a_addr = tmem_a + static_cast<uint32_t>(sa * 32 + j * 8);
+            mma_i8_ts(tmem_dhi + tt * 2 * BN, a_addr,
+                      smem_desc_sw128(b_base + tt * L::kBTile + j * 32), idesc_i8(true, 2 * BN), acc);
+          }
         mma_commit(&aempty[sa]);
         mma_commit(&bempty[sb]);
       }
@@ -504,32 +521,42 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       if (tid == 0 && p.err) atomicOr(p.err, kErrTimeout);
     } else if (nk > 0) {
       // 256*D_hi + D_lo, with D_lo = D_lo' + 128*sum(u) for the low plane stored as lo - 128
-      auto part16 = [&](int c0, uint32_t (&v)[16]) {
+      auto part16 = [&](int tt, int c0, uint32_t (&v)[16]) {
         uint32_t dh[16], dl[16];
-        tmem_ld16(tmem_dhi + lane_base + c0, dh);
-        tmem_ld16(tmem_dlo + lane_base + c0, dl);
+        tmem_ld16(tmem_dhi + tt * 2 * BN + lane_base + c0, dh);
+        tmem_ld16(tmem_dlo + tt * 2 * BN + lane_base + c0, dl);
 #pragma unroll
         for (int j = 0; j < 16; ++j) v[j] = (dh[j] << 8) + dl[j] + (su << 7);  // mod 2^32
       };
       if (p.splits == 1) {
-        float rv[16];
-        load16(0, rv);
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 16) {
-          uint32_t v[16];
-          part16(c0, v);
-          float rn[16];
-          if (c0 + 16 < BN) load16(c0 + 16, rn);
-          emit16(c0, v, rv);
+        for (int tt = 0; tt < TT; ++tt) {
+          if (tt > 0) {  // next token tile: its row sums (uniform over the 128 threads)
+            t0 = tb + tt * BN;
+            if (t0 >= a.M) break;
+            named_sync(1, 128);
+            if (tid < BN) s_rowsum[tid] = t0 + tid < a.M ? P.rowsum[t0 + tid] : 0;
+            named_sync(1, 128);
+          }
+          float rv[16];
+          load16(0, rv);
+#pragma unroll 1
+          for (int c0 = 0; c0 < BN; c0 += 16) {
+            uint32_t v[16];
+            part16(tt, c0, v);
+            float rn[16];
+            if (c0 + 16 < BN) load16(c0 + 16, rn);
+            emit16(c0, v, rv);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) rv[j] = rn[j];
+            for (int j = 0; j < 16; ++j) rv[j] = rn[j];
+          }
         }
       } else {
         // split-K: leave this CTA's partial tile in shared memory for the cluster leader
 #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += 16) {
           uint32_t v[16];
-          part16(c0, v);
+          part16(0, c0, v);
 #pragma unroll
           for (int j = 0; j < 16; ++j) xtile[(c0 + j) * 128 + tid] = v[j];
         }
@@ -617,9 +644,9 @@ cudaError_t planes_map(CUtensorMap* map, const int8_t* planes, int M, int64_t kp
 
 }  // namespace
 
-template <int BN>
+template <int BN, int TT>
 static cudaError_t launch_tc_bn(const TcArgs& p, const MatmulArgs* a, bool pdl, cudaStream_t s) {
-  using L = TcLayout<BN>;
+  using L = TcLayout<BN, TT>;
   TcMaps maps;
   for (int j = 0; j < p.nproj; ++j) {
     cudaError_t e = planes_map(&maps.m[j], a[j].planes, a[j].M, padded_k(a[j].K), BN);
@@ -629,12 +656,12 @@ static cudaError_t launch_tc_bn(const TcArgs& p, const MatmulArgs* a, bool pdl, 
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_set[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(tc_matmul_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kDyn);
+    cudaError_t e = cudaFuncSetAttribute(tc_matmul_kernel<BN, TT>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kDyn);
     if (e != cudaSuccess) return e;
     attr_set[dev & 63] = true;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(ceil_div(p.m.N, 128)), static_cast<unsigned>(ceil_div(p.m.M, BN)),
+  cfg.gridDim = dim3(static_cast<unsigned>(ceil_div(p.m.N, 128)), static_cast<unsigned>(ceil_div(p.m.M, BN * TT)),
                      static_cast<unsigned>(p.nproj * p.splits));
   cfg.blockDim = dim3(kTcThreads);
   cfg.dynamicSmemBytes = L::kDyn;
@@ -655,7 +682,7 @@ static cudaError_t launch_tc_bn(const TcArgs& p, const MatmulArgs* a, bool pdl, 
   }
   cfg.attrs = at;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, tc_matmul_kernel<BN>, maps, p);
+  return cudaLaunchKernelEx(&cfg, tc_matmul_kernel<BN, TT>, maps, p);
 }
 
 int tc_token_tile(int M) { return M <= 16 ? 16 : (M <= 32 ? 32 : 64); }
@@ -691,9 +718,11 @@ static cudaError_t launch_tc(const MatmulArgs* a, int nproj, int pair, int64_t s
   p.splits = splits;
   for (int j = 0; j < nproj; ++j) p.pj[j] = TcProj{a[j].w, a[j].rowsum, a[j].out, a[j].scale};
   switch (tc_token_tile(m.M)) {
-    case 16: return launch_tc_bn<16>(p, a, m.pdl, s);
-    case 32: return launch_tc_bn<32>(p, a, m.pdl, s);
-    default: return launch_tc_bn<64>(p, a, m.pdl, s);
+    case 16: return launch_tc_bn<16, 1>(p, a, m.pdl, s);
+    case 32: return launch_tc_bn<32, 1>(p, a, m.pdl, s);
+    // (three 64-row token tiles per CTA sharing each expanded weight k-block, TT = 3, were
+    // measured 1.3x slower on the 2.7B prefill than two one-tile CTAs per SM)
+    default: return launch_tc_bn<64, 1>(p, a, m.pdl, s);
   }
 }
 

@@ -107,6 +107,17 @@ def test_bitlinear_large_m_rows(cuda, orc, M):
     assert bits_equal(out[rows], r_out)
 
 
+def test_bitlinear_many_rows_all_match(cuda, orc):
+    """M >= 1024 without a k-split (many token tiles); ragged M, K and N, every row checked
+    bit for bit."""
+    M, K, N = 1100, 1000, 700
+    x, nw, wq = sweep_inputs(M, K, N, seed=11)
+    out, acc, _ = run_gpu(cuda, x, nw, wq, 20.0, "fixed")
+    r_out, r_acc, _ = orc.bitlinear(x, nw, wq, 20.0, act_quant=1)
+    assert np.array_equal(acc, r_acc)
+    assert bits_equal(out, r_out)
+
+
 def test_bitlinear_saturation_and_ragged(cuda, orc):
     """Q5.10 saturation (|y*1024| > 32767), K%8 tails, K%64 and N%32 padding, frac_bits."""
     rng = np.random.default_rng(11)

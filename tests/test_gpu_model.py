@@ -67,6 +67,15 @@ def test_layer_trace_matches_oracle(models, orc, blob_cache, name):
     assert bits_equal(lg, olg)
 
 
+def test_long_prefill_matches_oracle(models, orc, blob_cache):
+    """A 1100-token forward through the grouped i/f/g and paired SwiGLU tensor-core launches
+    without k-splits, and the fused mixer over 1100 steps; logits bit-identical to the oracle."""
+    m = models("small", "fixed")
+    om = orc.model(B.Blob.open(B.cached_blob("small", 0, blob_cache)))
+    ids = B.seeded_ids(1100, 31, 2048)
+    assert bits_equal(m.forward(ids), om.forward(ids))
+
+
 def test_fused_and_unfused_decode_agree(cuda, blob_cache, monkeypatch):
     """The fused few-row decode kernels (<= 4 streams) and the general per-op path give
     identical ids (both are bit-exact restatements)."""
