@@ -567,29 +567,28 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   __syncwarp();
   if (p.splits > 1) {
     // split-K over the cluster (the CTAs of one output tile): after the first barrier every
-    // partial tile is in its CTA's shared memory; split 0 sums them over distributed shared
-    // memory and writes the tile; the second barrier keeps the others' shared memory alive
-    // until it has read them. Every CTA reaches both barriers, on the error paths too.
+    // partial tile is in its CTA's shared memory; CTA r then sums token group g (16 tokens)
+    // for g = r, r + S, ... from every peer over distributed shared memory and writes it;
+    // the second barrier keeps each CTA's shared memory alive until its peers have read it.
+    // Every CTA reaches both barriers, on the error paths too.
     cluster_sync();
-    if (split == 0 && warp < 4 && s_fail == 0 && nk > 0) {
+    if (warp < 4 && s_fail == 0 && nk > 0) {
       const uint32_t local = smem_u32(xtile) + 4u * static_cast<uint32_t>(tid);
-      float rv[16];
-      load16(0, rv);
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
+      for (int c0 = 16 * split; c0 < BN; c0 += 16 * p.splits) {
+        float rv[16];
+        load16(c0, rv);
         uint32_t v[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = xtile[(c0 + j) * 128 + tid];
-        for (int r = 1; r < p.splits; ++r) {
-          const uint32_t peer = cluster_map(local + 4u * 128u * c0, r);
+        for (int j = 0; j < 16; ++j) v[j] = 0;
 #pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] += ld_cluster_u32(peer + 4u * 128u * j);
+        for (int r = 0; r < 8; ++r) {  // every split's partial (this CTA's through its own map)
+          if (r >= p.splits) break;
+          const uint32_t src = cluster_map(local + 4u * 128u * c0, r);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] += ld_cluster_u32(src + 4u * 128u * j);
         }
-        float rn[16];
-        if (c0 + 16 < BN) load16(c0 + 16, rn);
         emit16(c0, v, rv);
-#pragma unroll
-        for (int j = 0; j < 16; ++j) rv[j] = rn[j];
       }
     }
     cluster_sync();
