@@ -22,6 +22,8 @@ namespace mmfree_cuda {
 
 namespace {
 constexpr int kPrepThreads = 512;  // prep: 16 warps share a row's elementwise passes
+constexpr int kPrepThreadsMany = 128;  // prep of many rows: several row CTAs per SM
+constexpr int kPrepManyRows = 1024;
 constexpr int kMatmulThreads = 128;
 constexpr int kMaxDynSmem = 224 * 1024;  // below the 227 KB opt-in, leaving room for static smem
 }  // namespace
@@ -223,7 +225,10 @@ cudaError_t launch_prep(const PrepArgs& a, cudaStream_t s) {
   }
   if (smem > kMaxDynSmem) return cudaErrorInvalidValue;
   if (smem > 48 * 1024) raise_smem_limit(reinterpret_cast<const void*>(prep_kernel));
-  return launch_k(prep_kernel, dim3(a.M), dim3(kPrepThreads), smem, s, a.pdl, a, mode, staged);
+  // few rows: latency-bound, 512 threads per row; many rows: throughput-bound, 128 threads
+  // per row so that registers allow several row CTAs per SM
+  const int threads = a.M >= kPrepManyRows ? kPrepThreadsMany : kPrepThreads;
+  return launch_k(prep_kernel, dim3(a.M), dim3(threads), smem, s, a.pdl, a, mode, staged);
 }
 
 __device__ __forceinline__ int block_sum_int(int v, int* red) {

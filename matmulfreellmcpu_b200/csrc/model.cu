@@ -893,7 +893,10 @@ void Model::serve_step(const int64_t* in_ids, int64_t* out_ids) {
 void Model::serve_run(size_t steps, int64_t* out) {
   if (serve_b_ == 0) throw std::logic_error("serve_run without serve_begin");
   const int B = serve_b_;
-  const int64_t stride = static_cast<int64_t>(steps) + 1;
+  int64_t stride = static_cast<int64_t>(steps) + 1;
+  // the stride is only the row pitch of the id buffer: a graph captured for a longer run
+  // serves a shorter one too (no re-capture)
+  if (graph_ && graph_b_ == B && graph_stride_ >= stride) stride = graph_stride_;
   loop_ids(static_cast<size_t>(stride) * B);
   if (!graph_ || graph_b_ != B || graph_stride_ != stride) {
     drop_graph();
