@@ -140,43 +140,29 @@ __device__ __forceinline__ float hsum8_lanes(float v, unsigned mask = 0xffffffff
 
 // Lane j (= threadIdx.x & 7) of an 8-lane group runs chain j of the AVX2 sum of squares
 // (simd.hpp:69-89) over s[0..K): acc_j = fma(s[8i+j], s[8i+j], acc_j) for i < K/8, in order.
-// Batches of 8 are loaded unconditionally two batches (16 FMAs) ahead of their FMAs, so the
-// serial chain waits only on the FMA latency; a remainder of K/8 mod 16 steps follows.
+// Whole batches of 8 are loaded unconditionally one batch ahead of their FMAs, so the serial
+// chain waits only on the FMA latency; a remainder of K/8 mod 8 steps follows.
 __device__ __forceinline__ float sumsq_chain_lane(const float* s, int K) {
   const float* p = s + (threadIdx.x & 7);
-  const int n8 = K >> 3, nb = n8 >> 3;  // whole batches of 8 steps
+  const int n8 = K >> 3, nb = n8 >> 3;
   float acc = 0.0f;
-  int b = 0;
-  if (nb >= 2) {
-    float c0[8], c1[8];
+  if (nb > 0) {
+    float cur[8];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      c0[u] = p[8 * u];
-      c1[u] = p[64 + 8 * u];
-    }
-    for (b = 2; b + 1 < nb; b += 2) {
-      float n0[8], n1[8];
+    for (int u = 0; u < 8; ++u) cur[u] = p[8 * u];
+    for (int b = 1; b < nb; ++b) {
+      float nxt[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        n0[u] = p[64 * b + 8 * u];
-        n1[u] = p[64 * (b + 1) + 8 * u];
-      }
+      for (int u = 0; u < 8; ++u) nxt[u] = p[64 * b + 8 * u];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) acc = __fmaf_rn(c0[u], c0[u], acc);
+      for (int u = 0; u < 8; ++u) acc = __fmaf_rn(cur[u], cur[u], acc);
 #pragma unroll
-      for (int u = 0; u < 8; ++u) acc = __fmaf_rn(c1[u], c1[u], acc);
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        c0[u] = n0[u];
-        c1[u] = n1[u];
-      }
+      for (int u = 0; u < 8; ++u) cur[u] = nxt[u];
     }
 #pragma unroll
-    for (int u = 0; u < 8; ++u) acc = __fmaf_rn(c0[u], c0[u], acc);
-#pragma unroll
-    for (int u = 0; u < 8; ++u) acc = __fmaf_rn(c1[u], c1[u], acc);
+    for (int u = 0; u < 8; ++u) acc = __fmaf_rn(cur[u], cur[u], acc);
   }
-  for (int i = 8 * b; i < n8; ++i) {  // the batches left over (fewer than 2) and the tail
+  for (int i = nb * 8; i < n8; ++i) {
     const float v = p[8 * i];
     acc = __fmaf_rn(v, v, acc);
   }
