@@ -32,6 +32,7 @@ from dataclasses import dataclass, field
 import numpy as np
 
 MAGIC = b"MMFREE1\n"
+MAGIC2 = b"MMFREE2\n"  # the load cache: ternary weights as dtype "t2" (tiled 2-bit)
 ALIGN = 64
 PROJS = ("i_proj", "f_proj", "g_proj", "o_proj", "gate_proj", "down_proj")
 
@@ -164,6 +165,64 @@ def cached_blob(name: str, seed: int = 0, cache_dir: str | None = None) -> str:
     return path
 
 
+def packed_nbytes(out: int, k: int) -> int:
+    """Bytes of the tiled 2-bit format of an [out, k] ternary matrix."""
+    return -(-out // 32) * -(-k // 64) * 512
+
+
+def pack_ternary(wq: np.ndarray) -> np.ndarray:
+    """int8 ternary [out, k] -> the engine's tiled 2-bit format (csrc/common.cuh): 32-row
+    groups x 64-column chunks of 512 bytes, row r of a group at bytes 16r..16r+15, 32-bit
+    word w holding the codes u = w + 1 of columns 16w + 4g + j at bit 8j + 2g; padding rows
+    and columns hold u = 1 (weight 0). Entries outside {-1, 0, 1} are rejected."""
+    wq = np.asarray(wq)
+    if wq.ndim != 2 or ((wq < -1) | (wq > 1)).any():
+        raise ValueError("pack_ternary: expected a 2-D array of -1/0/+1")
+    out, k = wq.shape
+    ng, kc = -(-out // 32), -(-k // 64)
+    u = np.ones((ng * 32, kc * 64), np.uint8)
+    u[:out, :k] = (wq.astype(np.int16) + 1).astype(np.uint8)
+    u6 = u.reshape(ng, 32, kc, 4, 4, 4)  # [group, row, chunk, word, g, j]
+    b = u6[:, :, :, :, 0, :] | (u6[:, :, :, :, 1, :] << 2) | (u6[:, :, :, :, 2, :] << 4) | \
+        (u6[:, :, :, :, 3, :] << 6)      # [group, row, chunk, word, byte j]
+    return np.ascontiguousarray(b.transpose(0, 2, 1, 3, 4)).reshape(-1)
+
+
+def write_packed_blob(src: str, dst: str) -> str:
+    """model.mmfree -> model.mmfree2: the same header and tensors, every ternary *.wq
+    stored packed (dtype "t2", shape kept as [out, in]); returns ``dst``."""
+    with open(src, "rb") as f:
+        if f.read(8) != MAGIC:
+            raise ValueError(f"bad magic in {src}")
+        (hl,) = struct.unpack("<Q", f.read(8))
+        header = json.loads(f.read(hl))
+    data_start = _align(16 + hl)
+    mm = np.memmap(src, dtype=np.uint8, mode="r")
+    meta, off, parts = {}, 0, []
+    for name, m in header["tensors"].items():
+        raw = mm[data_start + m["offset"]:data_start + m["offset"] + m["nbytes"]]
+        if m["dtype"] == "i8" and name.endswith(".wq"):
+            body = pack_ternary(raw.view(np.int8).reshape(m["shape"]))
+            meta[name] = {"dtype": "t2", "shape": m["shape"], "offset": off, "nbytes": body.size}
+        else:
+            body = raw
+            meta[name] = dict(m, offset=off)
+        parts.append((off, body))
+        off = _align(off + body.size)
+    hb = json.dumps({"config": header["config"], "tensors": meta}).encode()
+    start = _align(len(MAGIC2) + 8 + len(hb))
+    tmp = dst + ".tmp"
+    with open(tmp, "wb") as f:
+        f.write(MAGIC2)
+        f.write(struct.pack("<Q", len(hb)))
+        f.write(hb)
+        for o, body in parts:
+            f.write(b"\0" * (start + o - f.tell()))
+            f.write(np.ascontiguousarray(body).tobytes())
+    os.replace(tmp, dst)
+    return dst
+
+
 @dataclass
 class Blob:
     """Read-only view of a ``model.mmfree`` file (numpy memmap, zero copy)."""
@@ -174,7 +233,8 @@ class Blob:
     @classmethod
     def open(cls, path: str) -> "Blob":
         with open(path, "rb") as f:
-            if f.read(8) != MAGIC:
+            magic = f.read(8)
+            if magic not in (MAGIC, MAGIC2):
                 raise ValueError(f"bad magic in {path}")
             (hl,) = struct.unpack("<Q", f.read(8))
             header = json.loads(f.read(hl))
@@ -182,9 +242,12 @@ class Blob:
         mm = np.memmap(path, dtype=np.uint8, mode="r")
         tensors = {}
         for name, m in header["tensors"].items():
+            start = data_start + m["offset"]
+            if m["dtype"] == "t2":  # packed ternary (model.mmfree2): the raw tiled bytes
+                tensors[name] = mm[start:start + packed_nbytes(*m["shape"])]
+                continue
             dt = np.int8 if m["dtype"] == "i8" else np.float32
             n = int(np.prod(m["shape"]))
-            start = data_start + m["offset"]
             tensors[name] = mm[start:start + n * dt().itemsize].view(dt).reshape(m["shape"])
         return cls(path, header["config"], tensors)
 
@@ -195,3 +258,18 @@ class Blob:
 def seeded_ids(n: int, seed: int, vocab: int = 32000, low: int = 3) -> np.ndarray:
     """Prompt ids: uniform integers in [low, vocab) from ``default_rng(seed)``."""
     return np.random.default_rng(seed).integers(low, vocab, size=n, dtype=np.int64)
+
+
+def main(argv=None) -> int:
+    """python -m matmulfreellmcpu_b200.blob pack SRC.mmfree DST.mmfree2"""
+    import sys
+    args = sys.argv[1:] if argv is None else argv
+    if len(args) != 3 or args[0] != "pack":
+        print(main.__doc__, file=sys.stderr)
+        return 2
+    write_packed_blob(args[1], args[2])
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -179,7 +179,8 @@ Blob::Blob(const std::string& path) {
   }
   try {
     const char* bytes = static_cast<const char*>(base_);
-    if (std::strncmp(bytes, "MMFREE1\n", 8) != 0)
+    const bool v2 = std::strncmp(bytes, "MMFREE2\n", 8) == 0;
+    if (!v2 && std::strncmp(bytes, "MMFREE1\n", 8) != 0)
       throw std::runtime_error("weights: bad magic in " + path);
     uint64_t hl = 0;
     std::memcpy(&hl, bytes + 8, 8);
@@ -214,12 +215,19 @@ Blob::Blob(const std::string& path) {
       BlobTensor t;
       const JValue* dt = m.member("dtype");
       t.is_int8 = dt && dt->kind == JValue::String && dt->str == "i8";
+      t.is_packed = v2 && dt && dt->kind == JValue::String && dt->str == "t2";
       if (const JValue* sh = m.member("shape"))
         for (const auto& d : sh->items) t.shape.push_back(static_cast<size_t>(d.num));
       const JValue* off = m.member("offset");
       if (!off) throw std::runtime_error("weights: tensor without offset: " + kv.first);
       t.offset = data_start + static_cast<size_t>(off->num);
-      t.nbytes = t.numel() * (t.is_int8 ? 1 : 4);
+      if (t.is_packed) {
+        if (t.shape.size() != 2) throw std::runtime_error("weights: t2 tensor must be 2-D: " + kv.first);
+        // tiled 2-bit: 32-row groups x 64-column chunks of 512 bytes (common.cuh)
+        t.nbytes = (t.shape[0] + 31) / 32 * ((t.shape[1] + 63) / 64) * 512;
+      } else {
+        t.nbytes = t.numel() * (t.is_int8 ? 1 : 4);
+      }
       if (t.offset + t.nbytes > size_)
         throw std::runtime_error("weights: tensor past end of file: " + kv.first);
       tensors_.emplace(kv.first, std::move(t));

@@ -5,6 +5,10 @@
 // nbytes}}}, zero padding to 64 bytes, then the data section with 64-byte aligned tensors
 // (offsets relative to the data-section start). Errors throw std::runtime_error with the
 // same wording as the reference loader (weights.cpp:193-242, weights.hpp:49).
+//
+// model.mmfree2 ("MMFREE2\n", this engine's load cache) is the same container with every
+// ternary weight stored as dtype "t2": the tiled 2-bit format of common.cuh for the logical
+// shape [out, in] (packed_bytes(out, in) bytes), so loading uploads it without a repack.
 #pragma once
 
 #include <cstddef>
@@ -29,6 +33,7 @@ struct BlobConfig {
 
 struct BlobTensor {
   bool is_int8 = false;
+  bool is_packed = false;  // dtype "t2" (model.mmfree2): tiled 2-bit ternary
   std::vector<size_t> shape;
   size_t offset = 0;  // absolute file offset
   size_t nbytes = 0;

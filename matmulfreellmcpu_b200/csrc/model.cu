@@ -136,21 +136,25 @@ Model::Model(const std::string& blob_path, int device, bool fixed, int frac_bits
   packed_bytes_ = 0;
   for (auto& w : ws) {
     const BlobTensor& t = blob.get(w.tag + ".wq");
-    if (!t.is_int8 || t.shape.size() != 2 || t.shape[0] != w.out || t.shape[1] != w.in)
+    if (!(t.is_int8 || t.is_packed) || t.shape.size() != 2 || t.shape[0] != w.out || t.shape[1] != w.in)
       throw std::runtime_error("weights: unexpected dtype/shape for " + w.tag + ".wq");
     expect(w.tag + ".scale_w", {1}, false);
-    max_i8 = std::max(max_i8, w.out * w.in);
+    if (!t.is_packed) max_i8 = std::max(max_i8, w.out * w.in);
     packed_bytes_ += static_cast<size_t>(packed_bytes(w.out, w.in));
   }
   CK(cudaMalloc(&arena_, packed_bytes_));
-  int8_t* staging = nullptr;
-  CK(cudaMalloc(&staging, max_i8));
+  int8_t* staging = nullptr;  // int8 upload buffer of the repack (none for model.mmfree2)
+  if (max_i8) CK(cudaMalloc(&staging, max_i8));
   {
     char* cur = static_cast<char*>(arena_);
     for (auto& w : ws) {
       const BlobTensor& t = blob.get(w.tag + ".wq");
-      CK(cudaMemcpyAsync(staging, blob.data(t), w.out * w.in, cudaMemcpyHostToDevice, stream_));
-      CK(launch_repack(cur, staging, w.out, w.in, err_, stream_));
+      if (t.is_packed) {  // model.mmfree2: already in the device format
+        CK(cudaMemcpyAsync(cur, blob.data(t), packed_bytes(w.out, w.in), cudaMemcpyHostToDevice, stream_));
+      } else {
+        CK(cudaMemcpyAsync(staging, blob.data(t), w.out * w.in, cudaMemcpyHostToDevice, stream_));
+        CK(launch_repack(cur, staging, w.out, w.in, err_, stream_));
+      }
       float s;
       std::memcpy(&s, blob.data(blob.get(w.tag + ".scale_w")), 4);
       w.p->w = cur;

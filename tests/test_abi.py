@@ -126,3 +126,35 @@ def test_seeded_blob_is_deterministic(tmp_path):
     wq = blob["model.layers.1.gate_proj.wq"]
     assert wq.shape == (104, 36) and set(np.unique(wq)) <= {-1, 0, 1}
     assert np.allclose(blob["lower_bounds"][:, 0], np.arange(2) / 2)
+
+
+# ---- model.mmfree2 (packed load cache)
+
+@pytest.mark.parametrize("n,k", [(37, 100), (64, 128), (96, 1003), (1, 1), (300, 64)])
+def test_numpy_packer_matches_c_abi_packer(n, k):
+    """blob.pack_ternary (the converter's packer) writes exactly the library's format."""
+    from matmulfreellmcpu_b200 import blob as B
+    w = np.random.default_rng(n * 7 + k).integers(-1, 2, size=(n, k)).astype(np.int8)
+    ref = np.zeros(B.packed_nbytes(n, k), np.uint8)
+    assert _lib.lib().mmfree_cuda_pack_ternary_host(ref.ctypes.data, w.ctypes.data, n, k) == 0
+    assert np.array_equal(B.pack_ternary(w), ref)
+
+
+def test_packed_blob_roundtrip(tmp_path, blob_cache):
+    """model.mmfree -> model.mmfree2 keeps every tensor; ternary weights become the tiled
+    2-bit bytes of the same matrix."""
+    from matmulfreellmcpu_b200 import blob as B
+    src = B.cached_blob("ragged", 0, blob_cache)
+    dst = B.write_packed_blob(src, str(tmp_path / "ragged.mmfree2"))
+    a, b = B.Blob.open(src), B.Blob.open(dst)
+    assert a.config == b.config and set(a.tensors) == set(b.tensors)
+    npacked = 0
+    for name, t in a.tensors.items():
+        if name.endswith(".wq"):
+            assert np.array_equal(b[name], B.pack_ternary(t))
+            npacked += 1
+        else:
+            assert np.array_equal(b[name], t)
+    assert npacked == 1 + 6 * a.config["num_hidden_layers"]
+    with pytest.raises(ValueError):
+        B.pack_ternary(np.full((2, 2), 2, np.int8))

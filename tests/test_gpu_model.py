@@ -67,6 +67,22 @@ def test_layer_trace_matches_oracle(models, orc, blob_cache, name):
     assert bits_equal(lg, olg)
 
 
+def test_packed_blob_loads_identically(cuda, tmp_path, blob_cache):
+    """A model loaded from model.mmfree2 (weights uploaded packed, no repack) gives the same
+    logits and ids as one loaded from model.mmfree."""
+    src = B.cached_blob("small", 0, blob_cache)
+    dst = B.write_packed_blob(src, str(tmp_path / "small.mmfree2"))
+    ids = B.seeded_ids(40, 7, 2048)
+    out = []
+    for path in (src, dst):
+        with api.Model(path, "fixed") as m:
+            out.append((m.forward(ids), m.generate(ids[:9], 12), m.generate_serve([ids[:5], ids[5:12]], 6)))
+    assert bits_equal(out[0][0], out[1][0])
+    assert np.array_equal(out[0][1], out[1][1])
+    for a, b in zip(out[0][2], out[1][2]):
+        assert np.array_equal(a, b)
+
+
 def test_long_prefill_matches_oracle(models, orc, blob_cache):
     """A 1100-token forward through the grouped i/f/g and paired SwiGLU tensor-core launches
     without k-splits, and the fused mixer over 1100 steps; logits bit-identical to the oracle."""
