@@ -122,7 +122,7 @@ __device__ __forceinline__ void prefetch_phase(const DecArgs& n, int cta, int nc
 // One phase for CTA `cta` of `ncta`: units cta, cta + ncta, ... `wait` is called by every
 // thread once the phase's constants are staged; it returns false when the step must stop.
 // Returns false when it stopped.
-template <int MT, int NP, int NW, int PRO, int EPI, class Wait>
+template <int MT, int NP, int NW, int PRO, int EPI, bool FL, class Wait>
 __device__ __forceinline__ bool dec_body(const DecArgs& a, int cta, int ncta, unsigned char* dsm,
                                          const DecArgs* next, Wait&& wait) {
   constexpr int kDecThreads = dec_threads(MT), kDecWarps = kDecThreads / 32;
@@ -134,8 +134,10 @@ __device__ __forceinline__ bool dec_body(const DecArgs& a, int cta, int ncta, un
   float* xs = reinterpret_cast<float*>(dsm);                              // [MT][K4]
   float* os = xs + static_cast<size_t>(MT) * K4;                          // [MT][K4] (Swish)
   float* nws = xs + static_cast<size_t>(kRows) * K4;                      // [kNorms][K4]
-  int8_t* pl = reinterpret_cast<int8_t*>(nws + static_cast<size_t>(kNorms) * K4);  // [NP][MT][2][kp]
-  uint32_t* red = reinterpret_cast<uint32_t*>(pl + static_cast<size_t>(NP) * MT * 2 * kp);
+  // FixedQ510: Q5.10 byte planes [NP][MT][2][kp]; Float: normalised activations [NP][MT][kp]
+  int8_t* pl = reinterpret_cast<int8_t*>(nws + static_cast<size_t>(kNorms) * K4);
+  float* yf = reinterpret_cast<float*>(pl);
+  uint32_t* red = reinterpret_cast<uint32_t*>(pl + static_cast<size_t>(NP) * MT * (FL ? 4 : 2) * kp);
   __shared__ float s_r[MT];
   __shared__ int s_rowsum[NP][MT];
 
@@ -263,7 +265,25 @@ __device__ __forceinline__ bool dec_body(const DecArgs& a, int cta, int ncta, un
 #pragma unroll
       for (int t = 0; t < MT; ++t) local[j][t] = 0;
     // 4 consecutive k per step: vector loads, one 4-byte store per plane
-    for (int c4 = tid * 4; c4 < kp; c4 += kDecThreads * 4) {
+    for (int c4 = tid * 4; FL && c4 < kp; c4 += kDecThreads * 4) {  // Float: y in fp32 (bitlinear.cpp:95-105)
+#pragma unroll
+      for (int t = 0; t < MT; ++t) {
+        const float4 xv4 = c4 < K ? *reinterpret_cast<const float4*>(xs + t * K4 + c4) : make_float4(0, 0, 0, 0);
+        const float xv[4] = {xv4.x, xv4.y, xv4.z, xv4.w};
+        const float r2 = s_r[t];
+#pragma unroll
+        for (int j = 0; j < NP; ++j) {
+          const float4 w4 = c4 < K ? *reinterpret_cast<const float4*>(nproj + j * K4 + c4) : make_float4(0, 0, 0, 0);
+          const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+          float y[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) y[e] = c4 + e < K ? norm_x(xv[e], r2, wv[e]) : 0.0f;
+          *reinterpret_cast<float4*>(yf + (static_cast<int64_t>(j) * MT + t) * kp + c4) =
+              make_float4(y[0], y[1], y[2], y[3]);
+        }
+      }
+    }
+    for (int c4 = tid * 4; !FL && c4 < kp; c4 += kDecThreads * 4) {
 #pragma unroll
       for (int t = 0; t < MT; ++t) {
         const float4 xv4 = c4 < K ? *reinterpret_cast<const float4*>(xs + t * K4 + c4) : make_float4(0, 0, 0, 0);
@@ -314,15 +334,40 @@ __device__ __forceinline__ bool dec_body(const DecArgs& a, int cta, int ncta, un
 
   for (int u = u0; u < units; u += ncta) {
     int acc_hi[NW][MT][4], acc_lo[NW][MT][4];
+    float accf[NW][MT];  // Float: sum of y * w (order free within the mode's tolerance)
 #pragma unroll
     for (int j = 0; j < NW; ++j)
 #pragma unroll
-      for (int t = 0; t < MT; ++t)
+      for (int t = 0; t < MT; ++t) {
+        accf[j][t] = 0.0f;
 #pragma unroll
         for (int q = 0; q < 4; ++q) acc_hi[j][t][q] = acc_lo[j][t][q] = 0;
+      }
     auto chunk = [&](const uint4 (&wv)[NW], int64_t c) {
 #pragma unroll
-      for (int j = 0; j < NW; ++j) {
+      for (int j = 0; FL && j < NW; ++j) {
+        const int pj = NP == 1 ? 0 : j;
+        const uint32_t wd[4] = {wv[j].x, wv[j].y, wv[j].z, wv[j].w};
+#pragma unroll
+        for (int t = 0; t < MT; ++t) {
+          const float4* yp = reinterpret_cast<const float4*>(yf + (static_cast<int64_t>(pj) * MT + t) * kp + c * kChunkK);
+#pragma unroll
+          for (int w4 = 0; w4 < 4; ++w4) {  // k = 64c + 16 w4 + 4 g + jj at bit 8 jj + 2 g
+            const float4 y0 = yp[4 * w4], y1 = yp[4 * w4 + 1], y2 = yp[4 * w4 + 2], y3 = yp[4 * w4 + 3];
+            const float yv[16] = {y0.x, y0.y, y0.z, y0.w, y1.x, y1.y, y1.z, y1.w,
+                                  y2.x, y2.y, y2.z, y2.w, y3.x, y3.y, y3.z, y3.w};
+#pragma unroll
+            for (int g = 0; g < 4; ++g)
+#pragma unroll
+              for (int jj = 0; jj < 4; ++jj) {
+                const int code = static_cast<int>((wd[w4] >> (8 * jj + 2 * g)) & 3u);
+                accf[j][t] = __fmaf_rn(yv[4 * g + jj], static_cast<float>(code - 1), accf[j][t]);
+              }
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; !FL && j < NW; ++j) {
         const int pj = NP == 1 ? 0 : j;
         const uint32_t wd[4] = {wv[j].x, wv[j].y, wv[j].z, wv[j].w};
 #pragma unroll
@@ -353,7 +398,7 @@ __device__ __forceinline__ bool dec_body(const DecArgs& a, int cta, int ncta, un
       for (int j = 0; j < NW; ++j) wv[j] = from_smem ? wst[(j * kc + c) * 32 + lane] : __ldg(wrow(u, j) + c * 32);
       chunk(wv, c);
     }
-    // combine the 4 byte-shift groups, then the warps, in shared memory
+    // combine the 4 byte-shift groups (FixedQ510), then the warps, in shared memory
 #pragma unroll
     for (int j = 0; j < NW; ++j)
 #pragma unroll
@@ -364,19 +409,30 @@ __device__ __forceinline__ bool dec_body(const DecArgs& a, int cta, int ncta, un
           v += static_cast<uint32_t>(acc_hi[j][t][q] >> (2 * q)) << 8;
           v += static_cast<uint32_t>(acc_lo[j][t][q] >> (2 * q));
         }
-        red[((warp * NW + j) * MT + t) * 32 + lane] = v;
+        red[((warp * NW + j) * MT + t) * 32 + lane] = FL ? __float_as_uint(accf[j][t]) : v;
       }
     __syncthreads();
     if (warp == 0) {
-      int32_t acc[NW][MT];
+      // dequantised outputs: acc * scale (FixedQ510: 1/(2^f scale_w), exact int32 acc;
+      // Float: 1/scale_w); a SwiGLU unit's two halves share projection 0's scale
+      float val[NW][MT];
 #pragma unroll
       for (int j = 0; j < NW; ++j)
 #pragma unroll
         for (int t = 0; t < MT; ++t) {
-          uint32_t v = 0;
+          const float sc = a.scale[EPI == kDecEpiSwiglu ? 0 : j];
+          if (FL) {
+            float v = 0.0f;
 #pragma unroll
-          for (int w = 0; w < kDecWarps; ++w) v += red[((w * NW + j) * MT + t) * 32 + lane];
-          acc[j][t] = static_cast<int32_t>(v - static_cast<uint32_t>(s_rowsum[NP == 1 ? 0 : j][t]));
+            for (int w = 0; w < kDecWarps; ++w) v += __uint_as_float(red[((w * NW + j) * MT + t) * 32 + lane]);
+            val[j][t] = __fmul_rn(v, sc);
+          } else {
+            uint32_t v = 0;
+#pragma unroll
+            for (int w = 0; w < kDecWarps; ++w) v += red[((w * NW + j) * MT + t) * 32 + lane];
+            val[j][t] = __fmul_rn(__int2float_rn(static_cast<int32_t>(v - static_cast<uint32_t>(
+                                      s_rowsum[NP == 1 ? 0 : j][t]))), sc);
+          }
         }
       const int n = u * 32 + lane;  // output column (first group of the unit)
 #pragma unroll
@@ -384,9 +440,9 @@ __device__ __forceinline__ bool dec_body(const DecArgs& a, int cta, int ncta, un
         if (t >= M) break;
         if (EPI == kDecEpiMixer) {
           if (n < a.N) {
-            const float iv = __fmul_rn(__int2float_rn(acc[0][t]), a.scale[0]);
-            const float fr = __fmul_rn(__int2float_rn(acc[NW > 1 ? 1 : 0][t]), a.scale[NW > 1 ? 1 : 0]);
-            const float gv = __fmul_rn(__int2float_rn(acc[NW > 2 ? 2 : 0][t]), a.scale[NW > 2 ? 2 : 0]);
+            const float iv = val[0][t];
+            const float fr = val[NW > 1 ? 1 : 0][t];
+            const float gv = val[NW > 2 ? 2 : 0][t];
             const int64_t e = static_cast<int64_t>(t) * a.N + n;
             const bool body = in_body(e % a.seg, a.seg);
             const bool first = u == u0;
@@ -401,19 +457,19 @@ __device__ __forceinline__ bool dec_body(const DecArgs& a, int cta, int ncta, un
         } else if (EPI == kDecEpiResid) {
           if (n < a.N) {
             const int64_t e = static_cast<int64_t>(t) * a.N + n;
-            a.out[0][e] = __fadd_rn(__ldcg(a.resid + e), __fmul_rn(__int2float_rn(acc[0][t]), a.scale[0]));
+            a.out[0][e] = __fadd_rn(__ldcg(a.resid + e), val[0][t]);
           }
         } else if (EPI == kDecEpiSwiglu) {
           const int I = a.N / 2;
           if (n < I) {
-            const float ya = __fmul_rn(__int2float_rn(acc[0][t]), a.scale[0]);
-            const float yb = __fmul_rn(__int2float_rn(acc[NW > 1 ? 1 : 0][t]), a.scale[0]);
+            const float ya = val[0][t];
+            const float yb = val[NW > 1 ? 1 : 0][t];
             const int64_t e = static_cast<int64_t>(t) * I + n;
             a.out[0][e] = swiglu_x(ya, yb, in_body(e % a.seg, a.seg));
           }
         } else {  // logits (+ greedy argmax)
           if (n < a.N) {
-            const float v = __fmul_rn(__int2float_rn(acc[0][t]), a.scale[0]);
+            const float v = val[0][t];
             if (a.out[0]) a.out[0][static_cast<int64_t>(t) * a.N + n] = v;
             if (v > best_v[t] || (v == best_v[t] && n < best_i[t])) { best_v[t] = v; best_i[t] = n; }
           }
@@ -479,10 +535,10 @@ __device__ __forceinline__ bool dec_body(const DecArgs& a, int cta, int ncta, un
   return true;
 }
 
-template <int MT, int NP, int NW, int PRO, int EPI>
+template <int MT, int NP, int NW, int PRO, int EPI, bool FL>
 __global__ void __launch_bounds__(dec_threads(MT)) dec_kernel(DecArgs a) {
   extern __shared__ __align__(16) unsigned char dsm[];
-  dec_body<MT, NP, NW, PRO, EPI>(a, blockIdx.x, gridDim.x, dsm, nullptr, [] {
+  dec_body<MT, NP, NW, PRO, EPI, FL>(a, blockIdx.x, gridDim.x, dsm, nullptr, [] {
     grid_dep_wait();
     grid_dep_launch();
     return true;
@@ -533,15 +589,15 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) dec_persist_kernel(const D
     };
     bool ok;
     if (a.epi == kDecEpiMixer)
-      ok = dec_body<MT, 3, 3, kDecProNorm2, kDecEpiMixer>(a, cta, ncta, dsm, next, wait);
+      ok = dec_body<MT, 3, 3, kDecProNorm2, kDecEpiMixer, false>(a, cta, ncta, dsm, next, wait);
     else if (a.epi == kDecEpiSwiglu)
-      ok = dec_body<MT, 1, 2, kDecProNorm2, kDecEpiSwiglu>(a, cta, ncta, dsm, next, wait);
+      ok = dec_body<MT, 1, 2, kDecProNorm2, kDecEpiSwiglu, false>(a, cta, ncta, dsm, next, wait);
     else if (a.epi == kDecEpiLogits)
-      ok = dec_body<MT, 1, 1, kDecProNorm2, kDecEpiLogits>(a, cta, ncta, dsm, next, wait);
+      ok = dec_body<MT, 1, 1, kDecProNorm2, kDecEpiLogits, false>(a, cta, ncta, dsm, next, wait);
     else if (a.pro == kDecProSwish)
-      ok = dec_body<MT, 1, 1, kDecProSwish, kDecEpiResid>(a, cta, ncta, dsm, next, wait);
+      ok = dec_body<MT, 1, 1, kDecProSwish, kDecEpiResid, false>(a, cta, ncta, dsm, next, wait);
     else
-      ok = dec_body<MT, 1, 1, kDecProPlain, kDecEpiResid>(a, cta, ncta, dsm, next, wait);
+      ok = dec_body<MT, 1, 1, kDecProPlain, kDecEpiResid, false>(a, cta, ncta, dsm, next, wait);
     asm volatile("cp.async.wait_all;" ::: "memory");  // the next descriptor has landed
     if (!ok) return;  // a barrier timed out (error flag set): every CTA stops
     // arrive: this CTA's part of phase ph is written
@@ -559,13 +615,13 @@ constexpr size_t kDecSmemMax = 224 * 1024;
 struct DecSmem {
   size_t base, staged;
 };
-static DecSmem dec_smem(int K, int MT, int NP, int NW, int PRO) {
+static DecSmem dec_smem(int K, int MT, int NP, int NW, int PRO, bool FL = false) {
   const int64_t kp = padded_k(K);
   const int K4 = (K + 3) & ~3;
   const int norms = (PRO == kDecProPlain ? 0 : 1) + NP;
   const int rows = PRO == kDecProSwish ? 2 * MT : MT;
   DecSmem d;
-  d.base = static_cast<size_t>(rows + norms) * K4 * 4 + static_cast<size_t>(NP) * MT * 2 * kp +
+  d.base = static_cast<size_t>(rows + norms) * K4 * 4 + static_cast<size_t>(NP) * MT * (FL ? 4 : 2) * kp +
            static_cast<size_t>(dec_threads(MT) / 32) * NW * MT * 32 * 4;
   d.staged = static_cast<size_t>(NW) * kp / kChunkK * kChunkBytes;
   return d;
@@ -592,9 +648,9 @@ static cudaError_t dec_smem_attr(K kernel, size_t smem, size_t (&cache)[64]) {
   return cudaSuccess;
 }
 
-template <int MT, int NP, int NW, int PRO, int EPI>
+template <int MT, int NP, int NW, int PRO, int EPI, bool FL>
 static cudaError_t launch_dec_t(const DecArgs& a, int grid, cudaStream_t s, bool pdl) {
-  const DecSmem d = dec_smem(a.K, MT, NP, NW, PRO);
+  const DecSmem d = dec_smem(a.K, MT, NP, NW, PRO, FL);
   if (d.base > kDecSmemMax) return cudaErrorInvalidValue;
   // stage the first unit's weights in shared memory when they fit
   DecArgs b = a;
@@ -603,9 +659,9 @@ static cudaError_t launch_dec_t(const DecArgs& a, int grid, cudaStream_t s, bool
   b.stage = d.base + d.staged <= kDecSmemMax ? 1 : 0;
   const size_t smem = d.base + (b.stage ? d.staged : 0);
   static size_t cache[64] = {0};
-  cudaError_t e = dec_smem_attr(dec_kernel<MT, NP, NW, PRO, EPI>, smem, cache);
+  cudaError_t e = dec_smem_attr(dec_kernel<MT, NP, NW, PRO, EPI, FL>, smem, cache);
   if (e != cudaSuccess) return e;
-  return launch_k(dec_kernel<MT, NP, NW, PRO, EPI>, dim3(static_cast<unsigned>(grid)), dim3(dec_threads(MT)),
+  return launch_k(dec_kernel<MT, NP, NW, PRO, EPI, FL>, dim3(static_cast<unsigned>(grid)), dim3(dec_threads(MT)),
                   smem, s, pdl, b);
 }
 
@@ -615,14 +671,21 @@ int dec_units(const DecArgs& a, int epi) {
   return epi == kDecEpiSwiglu ? ng / 2 : ng;
 }
 
+template <int MT, bool FL>
+static cudaError_t launch_dec_mf(const DecArgs& a, int pro, int epi, int grid, cudaStream_t s,
+                                 bool pdl) {
+  if (epi == kDecEpiMixer) return launch_dec_t<MT, 3, 3, kDecProNorm2, kDecEpiMixer, FL>(a, grid, s, pdl);
+  if (epi == kDecEpiSwiglu) return launch_dec_t<MT, 1, 2, kDecProNorm2, kDecEpiSwiglu, FL>(a, grid, s, pdl);
+  if (epi == kDecEpiLogits) return launch_dec_t<MT, 1, 1, kDecProNorm2, kDecEpiLogits, FL>(a, grid, s, pdl);
+  if (pro == kDecProSwish) return launch_dec_t<MT, 1, 1, kDecProSwish, kDecEpiResid, FL>(a, grid, s, pdl);
+  return launch_dec_t<MT, 1, 1, kDecProPlain, kDecEpiResid, FL>(a, grid, s, pdl);
+}
+
 template <int MT>
 static cudaError_t launch_dec_mt(const DecArgs& a, int pro, int epi, int grid, cudaStream_t s,
                                  bool pdl) {
-  if (epi == kDecEpiMixer) return launch_dec_t<MT, 3, 3, kDecProNorm2, kDecEpiMixer>(a, grid, s, pdl);
-  if (epi == kDecEpiSwiglu) return launch_dec_t<MT, 1, 2, kDecProNorm2, kDecEpiSwiglu>(a, grid, s, pdl);
-  if (epi == kDecEpiLogits) return launch_dec_t<MT, 1, 1, kDecProNorm2, kDecEpiLogits>(a, grid, s, pdl);
-  if (pro == kDecProSwish) return launch_dec_t<MT, 1, 1, kDecProSwish, kDecEpiResid>(a, grid, s, pdl);
-  return launch_dec_t<MT, 1, 1, kDecProPlain, kDecEpiResid>(a, grid, s, pdl);
+  return a.fl ? launch_dec_mf<MT, true>(a, pro, epi, grid, s, pdl)
+              : launch_dec_mf<MT, false>(a, pro, epi, grid, s, pdl);
 }
 
 cudaError_t launch_dec(const DecArgs& a, int pro, int epi, int grid, cudaStream_t s, bool pdl) {
@@ -636,7 +699,7 @@ cudaError_t launch_dec(const DecArgs& a, int pro, int epi, int grid, cudaStream_
 // ---- persistent decode step
 
 size_t dec_persist_plan(DecArgs* phases, int n) {
-  if (n <= 0) return 0;
+  if (n <= 0 || phases[0].fl) return 0;  // the persistent step is FixedQ510 only
   const int MT = dec_mt(phases[0].M);
   size_t need = 0;
   for (int i = 0; i < n; ++i) {  // rows, norms, planes of every phase must fit

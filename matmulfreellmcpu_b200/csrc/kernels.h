@@ -102,6 +102,7 @@ struct alignas(16) DecArgs {
   int V = 0;
   uint32_t* err = nullptr;
   int pro = 0, epi = 0;           // phase kind (DecPro, DecEpi)
+  int fl = 0;                     // Float activations (scale = 1/scale_w) instead of FixedQ510
   int stage = 0;                  // set by the launcher: first unit staged in shared memory
 };
 int dec_units(const DecArgs& a, int epi);

@@ -512,7 +512,7 @@ void Model::decode_graph_step(int B, int64_t stride) {
 }
 
 bool Model::fused_decode(int B) const {
-  return fixed_ && fused_ok_ && B <= kDecMaxRows && I_ % 32 == 0;
+  return fused_ok_ && B <= kDecMaxRows && I_ % 32 == 0;
 }
 
 std::vector<DecArgs> Model::dec_phases(int B, int64_t stride) {
@@ -523,7 +523,10 @@ std::vector<DecArgs> Model::dec_phases(int B, int64_t stride) {
     a.qs = qs_;
     a.pro = pro;
     a.epi = epi;
+    a.fl = fixed_ ? 0 : 1;
   };
+  // dequant scale: FixedQ510 1/(2^f scale_w) (bitlinear.cpp:89-94), Float 1/scale_w (:113-116)
+  auto scale = [&](float scale_w) { return fixed_ ? 1.0f / (qs_ * scale_w) : 1.0f / scale_w; };
   const size_t BH = static_cast<size_t>(B) * H_;
   for (int l = 0; l < L_; ++l) {
     const Layer& ly = layers_[l];
@@ -534,7 +537,7 @@ std::vector<DecArgs> Model::dec_phases(int B, int64_t stride) {
     for (int j = 0; j < 3; ++j) {
       k1.normw[j] = ly.p[j].normw;
       k1.w[j] = ly.p[j].w;
-      k1.scale[j] = 1.0f / (qs_ * ly.p[j].scale_w);
+      k1.scale[j] = scale(ly.p[j].scale_w);
     }
     k1.K = H_;
     k1.N = H_;
@@ -552,7 +555,7 @@ std::vector<DecArgs> Model::dec_phases(int B, int64_t stride) {
     k2.prew = ly.g_norm;
     k2.normw[0] = ly.p[kO].normw;
     k2.w[0] = ly.p[kO].w;
-    k2.scale[0] = 1.0f / (qs_ * ly.p[kO].scale_w);
+    k2.scale[0] = scale(ly.p[kO].scale_w);
     k2.K = H_;
     k2.N = H_;
     k2.out[0] = resid_;
@@ -565,7 +568,7 @@ std::vector<DecArgs> Model::dec_phases(int B, int64_t stride) {
     k3.prew = ly.mlp_norm;
     k3.normw[0] = ly.p[kGate].normw;
     k3.w[0] = ly.p[kGate].w;
-    k3.scale[0] = 1.0f / (qs_ * ly.p[kGate].scale_w);
+    k3.scale[0] = scale(ly.p[kGate].scale_w);
     k3.K = H_;
     k3.N = 2 * I_;
     k3.out[0] = z_;
@@ -577,7 +580,7 @@ std::vector<DecArgs> Model::dec_phases(int B, int64_t stride) {
     k4.x = z_;
     k4.normw[0] = ly.p[kDown].normw;
     k4.w[0] = ly.p[kDown].w;
-    k4.scale[0] = 1.0f / (qs_ * ly.p[kDown].scale_w);
+    k4.scale[0] = scale(ly.p[kDown].scale_w);
     k4.K = I_;
     k4.N = H_;
     k4.out[0] = h_;
@@ -590,7 +593,7 @@ std::vector<DecArgs> Model::dec_phases(int B, int64_t stride) {
   hd.prew = final_norm_;
   hd.normw[0] = lm_head_.normw;
   hd.w[0] = lm_head_.w;
-  hd.scale[0] = 1.0f / (qs_ * lm_head_.scale_w);
+  hd.scale[0] = scale(lm_head_.scale_w);
   hd.K = H_;
   hd.N = V_;
   hd.out[0] = logits_;

@@ -83,6 +83,22 @@ def test_packed_blob_loads_identically(cuda, tmp_path, blob_cache):
         assert np.array_equal(a, b)
 
 
+def test_float_fused_decode_matches_oracle(models, orc, blob_cache):
+    """Float mode at 1-3 streams runs the fused decode phases (fp32 activations, sums in any
+    order): the greedy ids equal the oracle's float streams, and the last-step logits of a
+    single stream agree within the float tolerance."""
+    m = models("small", "float")
+    om = orc.model(B.Blob.open(B.cached_blob("small", 0, blob_cache)))
+    prompts = [B.seeded_ids(6 + k, 720 + k, 2048) for k in range(3)]
+    ref_ids, ref_logits = om.generate(prompts[0], 10, act_quant=0)
+    got = m.generate(prompts[0], 10)
+    assert np.array_equal(got, ref_ids)
+    assert float_close(m.forward_last(got[:-1]), ref_logits)
+    for k in (2, 3):
+        for a, b in zip(m.generate_serve(prompts[:k], 8), om.generate_serve(prompts[:k], 8, act_quant=0)):
+            assert np.array_equal(a, b)
+
+
 def test_long_prefill_matches_oracle(models, orc, blob_cache):
     """A 1100-token forward through the grouped i/f/g and paired SwiGLU tensor-core launches
     without k-splits, and the fused mixer over 1100 steps; logits bit-identical to the oracle."""
