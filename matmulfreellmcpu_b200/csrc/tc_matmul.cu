@@ -36,6 +36,7 @@
 
 #include <cuda.h>
 #include <cstdint>
+#include <type_traits>
 #include <cstdlib>
 
 namespace mmfree_cuda {
@@ -124,9 +125,11 @@ __device__ __forceinline__ uint32_t cluster_map(uint32_t saddr, int rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
   return r;
 }
+// (no memory clobber: callers read peer data written before a cluster barrier, whose asm
+// orders it; without the clobber a batch of these loads is issued before its first use)
 __device__ __forceinline__ uint32_t ld_cluster_u32(uint32_t addr) {
   uint32_t v;
-  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(addr));
   return v;
 }
 
@@ -333,23 +336,23 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   uint32_t* xtile = reinterpret_cast<uint32_t*>(bst);                 // [BN][128] split-K partials
   float* xch = reinterpret_cast<float*>(bst + BN * 128 * 4);          // [16][64] SwiGLU exchange
   const bool add_resid = a.resid && P.out;
-  auto load16 = [&](int c0, float (&r)[16]) {
+  auto load16 = [&](int c0, float (&r)[16], int cnt = 16) {
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       const int t = t0 + c0 + j;
-      r[j] = (add_resid && n_ok && t < a.M) ? a.resid[static_cast<int64_t>(t) * a.ldr + n] : 0.0f;
+      r[j] = (add_resid && n_ok && j < cnt && t < a.M) ? a.resid[static_cast<int64_t>(t) * a.ldr + n] : 0.0f;
     }
   };
   // dequant (+ residual) of 16 finished int32 accumulators of tokens t0 + c0 + [0, 16);
   // a SwiGLU pair then combines gate row c (thread c) with up row I + c (thread 64 + c).
   // Called by all 128 epilogue threads alike (the pair exchange synchronises them).
-  auto emit16 = [&](int c0, const uint32_t (&v)[16], const float (&r)[16]) {
+  auto emit16 = [&](int c0, const uint32_t (&v)[16], const float (&r)[16], int cnt = 16) {
     float o[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       const int t = t0 + c0 + j;
-      const int32_t acc = static_cast<int32_t>(v[j] - static_cast<uint32_t>(s_rowsum[c0 + j]));
-      if (a.acc_out && n_ok && t < a.M) a.acc_out[static_cast<int64_t>(t) * a.N + n] = acc;
+      const int32_t acc = static_cast<int32_t>(v[j] - static_cast<uint32_t>(s_rowsum[(c0 + j) & (BN - 1)]));
+      if (a.acc_out && n_ok && j < cnt && t < a.M) a.acc_out[static_cast<int64_t>(t) * a.N + n] = acc;
       o[j] = __fmul_rn(__int2float_rn(acc), P.scale);
       if (a.resid) o[j] = __fadd_rn(r[j], o[j]);
     }
@@ -357,7 +360,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       if (P.out)
 #pragma unroll
         for (int j = 0; j < 16; ++j)
-          if (n_ok && t0 + c0 + j < a.M) P.out[static_cast<int64_t>(t0 + c0 + j) * a.ldo + n] = o[j];
+          if (n_ok && j < cnt && t0 + c0 + j < a.M) P.out[static_cast<int64_t>(t0 + c0 + j) * a.ldo + n] = o[j];
       return;
     }
     named_sync(1, 128);  // the previous group has been read
@@ -370,7 +373,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int t = t0 + c0 + j;
-        if (t >= a.M) continue;
+        if (j >= cnt || t >= a.M) continue;
         const int64_t e = static_cast<int64_t>(t) * I + n;
         P.out[static_cast<int64_t>(t) * a.ldo + n] = swiglu_x(o[j], xch[j * 64 + tid], in_body(e % p.seg, p.seg));
       }
@@ -573,23 +576,38 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     // Every CTA reaches both barriers, on the error paths too.
     cluster_sync();
     if (warp < 4 && s_fail == 0 && nk > 0) {
+      // this CTA's tokens: BN / S consecutive ones (all S CTAs work), in groups of C tokens
+      // whose S x C partials (<= 64 values) are all loaded before they are summed
       const uint32_t local = smem_u32(xtile) + 4u * static_cast<uint32_t>(tid);
+      auto reduce = [&](auto S_) {
+        constexpr int S = decltype(S_)::value, G = BN / S;
+        constexpr int C0 = (64 / S < 16) ? 64 / S : 16, C = C0 < G ? C0 : G;
 #pragma unroll 1
-      for (int c0 = 16 * split; c0 < BN; c0 += 16 * p.splits) {
-        float rv[16];
-        load16(c0, rv);
-        uint32_t v[16];
+        for (int c0 = split * G; c0 < (split + 1) * G; c0 += C) {
+          const int cnt = min(C, (split + 1) * G - c0);
+          float rv[16];
+          load16(c0, rv, cnt);
+          uint32_t part[S][C];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = 0;
+          for (int r = 0; r < S; ++r) {
+            const uint32_t src = cluster_map(local + 4u * 128u * c0, r);
 #pragma unroll
-        for (int r = 0; r < 8; ++r) {  // every split's partial (this CTA's through its own map)
-          if (r >= p.splits) break;
-          const uint32_t src = cluster_map(local + 4u * 128u * c0, r);
+            for (int j = 0; j < C; ++j) part[r][j] = j < cnt ? ld_cluster_u32(src + 4u * 128u * j) : 0u;
+          }
+          uint32_t v[16];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] += ld_cluster_u32(src + 4u * 128u * j);
+          for (int j = 0; j < 16; ++j) {
+            v[j] = 0;
+            if (j < C)
+#pragma unroll
+              for (int r = 0; r < S; ++r) v[j] += part[r][j < C ? j : 0];
+          }
+          emit16(c0, v, rv, cnt);
         }
-        emit16(c0, v, rv);
-      }
+      };
+      if (p.splits == 2) reduce(std::integral_constant<int, 2>{});
+      else if (p.splits == 4) reduce(std::integral_constant<int, 4>{});
+      else reduce(std::integral_constant<int, 8>{});
     }
     cluster_sync();
   }
