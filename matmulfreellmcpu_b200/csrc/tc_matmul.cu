@@ -705,12 +705,18 @@ static cudaError_t launch_tc_bn(const TcArgs& p, const MatmulArgs* a, bool pdl, 
 int tc_token_tile(int M) { return M <= 16 ? 16 : (M <= 32 ? 32 : 64); }
 
 int tc_splits(const MatmulArgs& a, int sm_count, int nproj) {
-  // about one CTA per SM (two per SM measured slower: the cluster reduction grows with the
-  // split count); every split keeps >= 2 k-blocks; a cluster holds <= 8 CTAs
+  // up to two CTAs per SM, the residency the kernel is built for (MMFREE_TC_CTAS_PER_SM=1:
+  // one, for comparison): at 64 tokens splitting a long reduction over more CTAs costs less
+  // in the cluster reduction than it saves in the k-loop; every split keeps >= 2 k-blocks; a
+  // cluster holds <= 8 CTAs
+  static const int per_sm = [] {
+    const char* e = std::getenv("MMFREE_TC_CTAS_PER_SM");
+    return (e && std::atoi(e) == 1) ? 1 : 2;
+  }();
   const int64_t tiles = ceil_div(a.N, 128) * ceil_div(a.M, tc_token_tile(a.M)) * nproj;
   const int nkb = static_cast<int>((packed_chunks(a.K) + 1) / 2);
   int splits = 1;
-  while (splits < 8 && tiles * splits * 2 <= sm_count && nkb / (splits * 2) >= 2) splits *= 2;
+  while (splits < 8 && tiles * splits * 2 <= per_sm * sm_count && nkb / (splits * 2) >= 2) splits *= 2;
   return splits;
 }
 
