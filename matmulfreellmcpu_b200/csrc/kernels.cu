@@ -456,11 +456,20 @@ __global__ void __launch_bounds__(128) mixer_kernel(float* __restrict__ out, con
                                                     int64_t seg) {
   grid_dep_launch();
   grid_dep_wait();
-  if (T == 1) {  // one position per lane (decode): a small grid, 4 lanes per thread per round
+  if (T == 1 && H >= 8) {  // one position per lane (decode): a small grid, 4 lanes per thread per round
     const int64_t total = static_cast<int64_t>(nseq) * H, stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    const int64_t body_n = seg & ~int64_t(7);
-    for (int64_t l0 = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; l0 < total; l0 += 4 * stride) {
+    // lane l = (q, c) is in the scalar tail of its segment (seg = seg_rows * H elements) only
+    // in the segment's last row q, at columns c >= tail_from; (q, c) advance by counters
+    const int64_t seg_rows = seg / H;
+    const int tail_from = H - static_cast<int>(seg % 8);
+    int64_t l0 = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    int64_t q = l0 / H;
+    int c = static_cast<int>(l0 % H);
+    const int64_t dq = stride / H;
+    const int dc = static_cast<int>(stride % H);
+    for (; l0 < total; l0 += 4 * stride) {
       float a[4], b[4], s0[4], lv[4];
+      bool body[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {  // all loads of the round first
         const int64_t l = l0 + u * stride;
@@ -468,16 +477,22 @@ __global__ void __launch_bounds__(128) mixer_kernel(float* __restrict__ out, con
         a[u] = ok ? __ldcs(iv + l) : 0.0f;
         b[u] = ok ? __ldcs(fv + l) : 0.0f;
         s0[u] = (ok && state) ? state[l] : 0.0f;
-        lv[u] = (ok && lb) ? __ldg(lb + l % H) : 0.0f;
+        lv[u] = (ok && lb) ? __ldg(lb + c) : 0.0f;
+        body[u] = c < tail_from || (q + 1) % seg_rows != 0;
+        c += dc;
+        q += dq;
+        if (c >= H) {
+          c -= H;
+          ++q;
+        }
       }
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const int64_t l = l0 + u * stride;  // element index = lane (T = 1)
         if (l >= total) break;
-        const bool body = (l % seg) < body_n;
-        float f = sigmoid_x(b[u], body);
+        float f = sigmoid_x(b[u], body[u]);
         if (lb) f = lower_bound_x(f, lv[u]);
-        const float st = hgrn_step_x(f, s0[u], swiglu_x(a[u], __fadd_rn(1.0f, -f), body));
+        const float st = hgrn_step_x(f, s0[u], swiglu_x(a[u], __fadd_rn(1.0f, -f), body[u]));
         out[l] = st;
         if (state) state[l] = st;
       }
@@ -523,7 +538,7 @@ cudaError_t launch_mixer(float* i, float* f, float* recur, float* state, const f
   if (lanes == 0 || len == 0) return cudaSuccess;
   // decode (len 1): about one CTA per SM, so that every CTA is resident (and triggers the
   // dependent launch) while the previous kernel's CTAs still occupy the SMs
-  const int64_t ctas = len == 1 ? std::min<int64_t>(ceil_div(lanes, 128 * 4), sm_count()) : ceil_div(lanes, 128);
+  const int64_t ctas = len == 1 && H >= 8 ? std::min<int64_t>(ceil_div(lanes, 128 * 4), sm_count()) : ceil_div(lanes, 128);
   return launch_k(mixer_kernel, dim3(static_cast<unsigned>(ctas)), dim3(128), 0, s, pdl,
                   recur, static_cast<const float*>(i), static_cast<const float*>(f), state, lb, nseq, len,
                   H, static_cast<int64_t>(seg_rows) * H);

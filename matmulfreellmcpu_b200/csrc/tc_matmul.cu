@@ -132,6 +132,14 @@ __device__ __forceinline__ uint32_t ld_cluster_u32(uint32_t addr) {
   asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(addr));
   return v;
 }
+__device__ __forceinline__ void ld_cluster_v2(uint32_t addr, uint32_t* v) {
+  asm volatile("ld.shared::cluster.v2.u32 {%0, %1}, [%2];" : "=r"(v[0]), "=r"(v[1]) : "r"(addr));
+}
+__device__ __forceinline__ void ld_cluster_v4(uint32_t addr, uint32_t* v) {
+  asm volatile("ld.shared::cluster.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
+               : "r"(addr));
+}
 
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -216,7 +224,8 @@ struct TcArgs {
   TcProj pj[3];
   int nproj;          // grid.z = nproj * splits
   int pair;           // SwiGLU gate_proj: I/32, the first group of the up rows; 0 otherwise
-  int64_t seg;        // SwiGLU: elements of one reference vector call (SIMD tails)
+  int seg_rows;       // SwiGLU: token rows of one reference vector call (SIMD tails) ...
+  int tail_from;      // ... whose last row's columns >= tail_from are its scalar tail
   uint32_t* err;      // bit kErrTimeout on a timed-out wait
   int splits;         // k-block ranges per tile = cluster size along z (1, 2, 4 or 8)
 };
@@ -334,7 +343,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
                        : n0 + tid;
   const bool n_ok = tid < 128 && n < a.N;
   uint32_t* xtile = reinterpret_cast<uint32_t*>(bst);                 // [BN][128] split-K partials
-  float* xch = reinterpret_cast<float*>(bst + BN * 128 * 4);          // [16][64] SwiGLU exchange
+  float* xch = reinterpret_cast<float*>(bst + BN * 128 * 4);          // [8][128] SwiGLU exchange
   const bool add_resid = a.resid && P.out;
   auto load16 = [&](int c0, float (&r)[16], int cnt = 16) {
 #pragma unroll
@@ -364,19 +373,25 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       return;
     }
     named_sync(1, 128);  // the previous group has been read
-    if (tid >= 64)
+    // gate threads (tid < 64) pass up tokens 8..15 of their row, up threads tokens 0..7 of
+    // theirs, so that all 128 threads then combine 8 tokens of gate row c with up row I + c
+    const int c = tid & 63;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) xch[j * 64 + tid - 64] = o[j];
+    for (int jj = 0; jj < 8; ++jj) xch[jj * 128 + tid] = tid < 64 ? o[8 + jj] : o[jj];
     named_sync(1, 128);
-    if (tid < 64) {
-      const int I = p.pair * 32;
+    // element (t, col) is in the scalar tail of its segment only in the segment's last row, at
+    // columns >= tail_from (fewer than 8 columns, so the division is rare)
+    const int col = 64 * blockIdx.x + c;
+    const bool tail_col = col >= p.tail_from;
+    const int jb = tid < 64 ? 0 : 8;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int t = t0 + c0 + j;
-        if (j >= cnt || t >= a.M) continue;
-        const int64_t e = static_cast<int64_t>(t) * I + n;
-        P.out[static_cast<int64_t>(t) * a.ldo + n] = swiglu_x(o[j], xch[j * 64 + tid], in_body(e % p.seg, p.seg));
-      }
+    for (int jj = 0; jj < 8; ++jj) {
+      const int t = t0 + c0 + jb + jj;
+      if (jb + jj >= cnt || t >= a.M || col >= p.pair * 32) continue;
+      const float g = tid < 64 ? o[jj] : xch[jj * 128 + c];
+      const float u = tid < 64 ? xch[jj * 128 + 64 + c] : o[8 + jj];
+      const bool body = !tail_col || (t + 1) % p.seg_rows != 0;
+      P.out[static_cast<int64_t>(t) * a.ldo + col] = swiglu_x(g, u, body);
     }
   };
 
@@ -736,7 +751,15 @@ static cudaError_t launch_tc(const MatmulArgs* a, int nproj, int pair, int64_t s
   p.m = m;
   p.nproj = nproj;
   p.pair = pair;
-  p.seg = seg > 0 ? seg : 1;
+  if (pair) {  // seg = seg_rows * I elements, I = 32 * pair >= 64
+    const int64_t I = 32 * static_cast<int64_t>(pair);
+    if (seg <= 0 || seg % I != 0 || seg / I > INT32_MAX) return cudaErrorInvalidValue;
+    p.seg_rows = static_cast<int>(seg / I);
+    p.tail_from = static_cast<int>(I - seg % 8);
+  } else {
+    p.seg_rows = 1;
+    p.tail_from = INT32_MAX;
+  }
   p.err = m.err;
   p.splits = splits;
   for (int j = 0; j < nproj; ++j) p.pj[j] = TcProj{a[j].w, a[j].rowsum, a[j].out, a[j].scale};
