@@ -444,7 +444,9 @@ __device__ __forceinline__ bool dec_body(const DecArgs& a, int cta, int ncta, un
             const float fr = val[NW > 1 ? 1 : 0][t];
             const float gv = val[NW > 2 ? 2 : 0][t];
             const int64_t e = static_cast<int64_t>(t) * a.N + n;
-            const bool body = in_body(e % a.seg, a.seg);
+            // seg is a whole number of N-element rows: only columns n >= N - seg % 8 of a
+            // segment's last row are in the tail (the division runs for those alone)
+            const bool body = n < a.N - static_cast<int>(a.seg & 7) || in_body(e % a.seg, a.seg);
             const bool first = u == u0;
             float fv = sigmoid_x(fr, body);
             if (a.lb) fv = lower_bound_x(fv, first ? lb_pre : __ldg(a.lb + n));
@@ -465,7 +467,8 @@ __device__ __forceinline__ bool dec_body(const DecArgs& a, int cta, int ncta, un
             const float ya = val[0][t];
             const float yb = val[NW > 1 ? 1 : 0][t];
             const int64_t e = static_cast<int64_t>(t) * I + n;
-            a.out[0][e] = swiglu_x(ya, yb, in_body(e % a.seg, a.seg));
+            const bool body = n < I - static_cast<int>(a.seg & 7) || in_body(e % a.seg, a.seg);  // (as above)
+            a.out[0][e] = swiglu_x(ya, yb, body);
           }
         } else {  // logits (+ greedy argmax)
           if (n < a.N) {

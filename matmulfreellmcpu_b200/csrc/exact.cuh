@@ -35,46 +35,34 @@ __device__ __forceinline__ float pow2_of(float fx) {
   return __uint_as_float(e);
 }
 
-// One lane of the vector exp (simd.hpp:232-249).
-__device__ __forceinline__ float exp_vec(float x) {
-  x = (x > -kExpHi) ? x : -kExpHi;  // vmaxps: a NaN input selects the bound
-  x = (x < kExpHi) ? x : kExpHi;    // vminps
-  float fx = floorf(__fmaf_rn(x, kLog2e, 0.5f));
-  float r = __fmaf_rn(-fx, kLn2Hi, x);
-  r = __fmaf_rn(-fx, kLn2Lo, r);
-  float p = kP0;
-  p = __fmaf_rn(p, r, kP1);
-  p = __fmaf_rn(p, r, kP2);
-  p = __fmaf_rn(p, r, kP3);
-  p = __fmaf_rn(p, r, kP4);
-  p = __fmaf_rn(p, r, kP5);
-  p = __fmaf_rn(p, __fmul_rn(r, r), __fadd_rn(r, 1.0f));
-  return __fmul_rn(p, pow2_of(fx));
-}
-
-// The scalar-tail exp of the compiled reference (simd.hpp:212-229).
-__device__ __forceinline__ float exp_tail(float x) {
-  if (x > kExpHi) x = kExpHi;
-  else if (x < -kExpHi) x = -kExpHi;
-  float fx = floorf(__fmaf_rn(x, kLog2e, 0.5f));
-  float r = __fmaf_rn(-fx, kLn2Hi, x);
-  r = __fmaf_rn(-fx, kLn2Lo, r);
-  float p = kP0;
-  p = __fmaf_rn(p, r, kP1);
-  p = __fmaf_rn(p, r, kP2);
-  p = __fmaf_rn(p, r, kP3);
-  p = __fmaf_rn(p, r, kP4);
-  p = __fmaf_rn(p, r, kP5);
-  p = __fadd_rn(__fmaf_rn(p, __fmul_rn(r, r), r), 1.0f);
-  return __fmul_rn(p, pow2_of(fx));
-}
-
 // Element e of an n-element vector op is in the 8-wide SIMD body iff e < 8*floor(n/8);
-// the rest is the scalar tail, which uses exp_tail.
+// the rest is the scalar tail, whose exp differs (exp_neg).
 __device__ __forceinline__ bool in_body(uint64_t e, uint64_t n) { return e < (n & ~uint64_t(7)); }
 
+// exp(-x) as the vector exp of the SIMD body computes it (simd.hpp:232-249) or, !body, as
+// the scalar-tail exp of the compiled reference (simd.hpp:212-229), without a branch: the
+// two differ only in how a NaN is clamped (vmaxps/vminps select the bound; the tail's
+// compares keep the NaN) and in how the last polynomial step adds 1 (the tail's form is
+// fused by the build).
 __device__ __forceinline__ float exp_neg(float x, bool body) {
-  return body ? exp_vec(-x) : exp_tail(-x);
+  x = -x;
+  float xv = (x > -kExpHi) ? x : -kExpHi;
+  xv = (xv < kExpHi) ? xv : kExpHi;
+  const float xt = (x > kExpHi) ? kExpHi : ((x < -kExpHi) ? -kExpHi : x);
+  x = body ? xv : xt;
+  const float fx = floorf(__fmaf_rn(x, kLog2e, 0.5f));
+  float r = __fmaf_rn(-fx, kLn2Hi, x);
+  r = __fmaf_rn(-fx, kLn2Lo, r);
+  float p = kP0;
+  p = __fmaf_rn(p, r, kP1);
+  p = __fmaf_rn(p, r, kP2);
+  p = __fmaf_rn(p, r, kP3);
+  p = __fmaf_rn(p, r, kP4);
+  p = __fmaf_rn(p, r, kP5);
+  const float rr = __fmul_rn(r, r);
+  const float pv = __fmaf_rn(p, rr, __fadd_rn(r, 1.0f));
+  const float pt = __fadd_rn(__fmaf_rn(p, rr, r), 1.0f);
+  return __fmul_rn(body ? pv : pt, pow2_of(fx));
 }
 
 // simd::sigmoid / silu / swiglu (simd.hpp:270-330), one element.
@@ -86,6 +74,33 @@ __device__ __forceinline__ float silu_x(float x, bool body) {
 }
 __device__ __forceinline__ float swiglu_x(float a, float b, bool body) {
   return __fmul_rn(__fdiv_rn(a, __fadd_rn(1.0f, exp_neg(a, body))), b);
+}
+
+// The same for N elements at a time: the branch-free exps of all N first, then the divisions.
+template <int N>
+__device__ __forceinline__ void sigmoid_n(const float (&x)[N], const bool (&body)[N], float (&out)[N]) {
+  float d[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) d[i] = __fadd_rn(1.0f, exp_neg(x[i], body[i]));
+#pragma unroll
+  for (int i = 0; i < N; ++i) out[i] = __fdiv_rn(1.0f, d[i]);
+}
+template <int N>
+__device__ __forceinline__ void silu_n(const float (&x)[N], const bool (&body)[N], float (&out)[N]) {
+  float d[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) d[i] = __fadd_rn(1.0f, exp_neg(x[i], body[i]));
+#pragma unroll
+  for (int i = 0; i < N; ++i) out[i] = __fdiv_rn(x[i], d[i]);
+}
+template <int N>
+__device__ __forceinline__ void swiglu_n(const float (&a)[N], const float (&b)[N], const bool (&body)[N],
+                                         float (&out)[N]) {
+  float d[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) d[i] = __fadd_rn(1.0f, exp_neg(a[i], body[i]));
+#pragma unroll
+  for (int i = 0; i < N; ++i) out[i] = __fmul_rn(__fdiv_rn(a[i], d[i]), b[i]);
 }
 
 // rstd = 1 / sqrt(sumsq / n + eps)  (rmsnorm.cpp:18, bitlinear.cpp:86).

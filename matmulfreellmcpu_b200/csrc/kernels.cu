@@ -146,11 +146,29 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepArgs a, int mode
     }
     __syncthreads();
     const float r1 = s_rstd;
-    for (int c = tid; c < K; c += blockDim.x) {
-      float t = norm_x(srow[c], r1, prew[c]);
-      if (mode == kPrepSwishgate) t = __fmul_rn(t, silu_x(orow[c], in_body(c, K)));
-      srow[c] = t;
-      if (a.pre_out) a.pre_out[static_cast<int64_t>(m) * K + c] = t;
+    const int nt = blockDim.x;
+    for (int c0 = tid; c0 < K; c0 += 4 * nt) {
+      float sg[4];
+      if (mode == kPrepSwishgate) {  // four gates at a time (their divisions overlap)
+        float xo[4];
+        bool bd[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int c = c0 + u * nt;
+          xo[u] = c < K ? orow[c] : 0.0f;
+          bd[u] = in_body(c, K);
+        }
+        silu_n(xo, bd, sg);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int c = c0 + u * nt;
+        if (c >= K) break;
+        float t = norm_x(srow[c], r1, prew[c]);
+        if (mode == kPrepSwishgate) t = __fmul_rn(t, sg[u]);
+        srow[c] = t;
+        if (a.pre_out) a.pre_out[static_cast<int64_t>(m) * K + c] = t;
+      }
     }
     __syncthreads();
   }
@@ -486,13 +504,19 @@ __global__ void __launch_bounds__(128) mixer_kernel(float* __restrict__ out, con
           ++q;
         }
       }
+      float f[4], om[4], sv[4];
+      sigmoid_n(b, body, f);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (lb) f[u] = lower_bound_x(f[u], lv[u]);
+        om[u] = __fadd_rn(1.0f, -f[u]);
+      }
+      swiglu_n(a, om, body, sv);
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const int64_t l = l0 + u * stride;  // element index = lane (T = 1)
         if (l >= total) break;
-        float f = sigmoid_x(b[u], body[u]);
-        if (lb) f = lower_bound_x(f, lv[u]);
-        const float st = hgrn_step_x(f, s0[u], swiglu_x(a[u], __fadd_rn(1.0f, -f), body[u]));
+        const float st = hgrn_step_x(f[u], s0[u], sv[u]);
         out[l] = st;
         if (state) state[l] = st;
       }
@@ -515,17 +539,27 @@ __global__ void __launch_bounds__(128) mixer_kernel(float* __restrict__ out, con
       a[u] = t0 + u < T ? __ldcs(iv + e) : 0.0f;
       b[u] = t0 + u < T ? __ldcs(fv + e) : 0.0f;
     }
+    // gates and scan inputs of the batch first (independent of the recurrence)
+    bool body[kMixAhead];
+#pragma unroll
+    for (int u = 0; u < kMixAhead; ++u) {
+      body[u] = es < body_n;
+      es += H;
+      if (es >= seg) es -= seg;
+    }
+    float f[kMixAhead], om[kMixAhead], sv[kMixAhead];
+    sigmoid_n(b, body, f);
+#pragma unroll
+    for (int u = 0; u < kMixAhead; ++u) {
+      if (lb) f[u] = lower_bound_x(f[u], lbc);
+      om[u] = __fadd_rn(1.0f, -f[u]);
+    }
+    swiglu_n(a, om, body, sv);
 #pragma unroll
     for (int u = 0; u < kMixAhead; ++u) {
       if (t0 + u >= T) break;
       const int64_t e = base + static_cast<int64_t>(t0 + u) * H;
-      const bool body = es < body_n;
-      es += H;
-      if (es >= seg) es -= seg;
-      float f = sigmoid_x(b[u], body);
-      if (lb) f = lower_bound_x(f, lbc);
-      const float sv = swiglu_x(a[u], __fadd_rn(1.0f, -f), body);
-      st = hgrn_step_x(f, st, sv);
+      st = hgrn_step_x(f[u], st, sv[u]);
       out[e] = st;
     }
   }

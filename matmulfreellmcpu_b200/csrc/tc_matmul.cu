@@ -125,16 +125,9 @@ __device__ __forceinline__ uint32_t cluster_map(uint32_t saddr, int rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
   return r;
 }
-// (no memory clobber: callers read peer data written before a cluster barrier, whose asm
-// orders it; without the clobber a batch of these loads is issued before its first use)
-__device__ __forceinline__ uint32_t ld_cluster_u32(uint32_t addr) {
-  uint32_t v;
-  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(addr));
-  return v;
-}
-__device__ __forceinline__ void ld_cluster_v2(uint32_t addr, uint32_t* v) {
-  asm volatile("ld.shared::cluster.v2.u32 {%0, %1}, [%2];" : "=r"(v[0]), "=r"(v[1]) : "r"(addr));
-}
+// 16-byte load from a peer's shared memory (no memory clobber: callers read peer data
+// written before a cluster barrier, whose asm orders it; without the clobber a batch of
+// these loads is issued before its first use)
 __device__ __forceinline__ void ld_cluster_v4(uint32_t addr, uint32_t* v) {
   asm volatile("ld.shared::cluster.v4.u32 {%0, %1, %2, %3}, [%4];"
                : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
@@ -228,6 +221,7 @@ struct TcArgs {
   int tail_from;      // ... whose last row's columns >= tail_from are its scalar tail
   uint32_t* err;      // bit kErrTimeout on a timed-out wait
   int splits;         // k-block ranges per tile = cluster size along z (1, 2, 4 or 8)
+  int vec;            // outputs, residual and raw accumulators allow 16-byte accesses
 };
 
 struct TcMaps {
@@ -384,14 +378,19 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     const int col = 64 * blockIdx.x + c;
     const bool tail_col = col >= p.tail_from;
     const int jb = tid < 64 ? 0 : 8;
+    float g[8], u[8], z[8];
+    bool body[8];
+#pragma unroll
+    for (int jj = 0; jj < 8; ++jj) {
+      g[jj] = tid < 64 ? o[jj] : xch[jj * 128 + c];
+      u[jj] = tid < 64 ? xch[jj * 128 + 64 + c] : o[8 + jj];
+      body[jj] = !tail_col || (t0 + c0 + jb + jj + 1) % p.seg_rows != 0;
+    }
+    swiglu_n(g, u, body, z);
 #pragma unroll
     for (int jj = 0; jj < 8; ++jj) {
       const int t = t0 + c0 + jb + jj;
-      if (jb + jj >= cnt || t >= a.M || col >= p.pair * 32) continue;
-      const float g = tid < 64 ? o[jj] : xch[jj * 128 + c];
-      const float u = tid < 64 ? xch[jj * 128 + 64 + c] : o[8 + jj];
-      const bool body = !tail_col || (t + 1) % p.seg_rows != 0;
-      P.out[static_cast<int64_t>(t) * a.ldo + col] = swiglu_x(g, u, body);
+      if (jb + jj < cnt && t < a.M && col < p.pair * 32) P.out[static_cast<int64_t>(t) * a.ldo + col] = z[jj];
     }
   };
 
@@ -585,39 +584,138 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   __syncwarp();
   if (p.splits > 1) {
     // split-K over the cluster (the CTAs of one output tile): after the first barrier every
-    // partial tile is in its CTA's shared memory; CTA r then sums token group g (16 tokens)
-    // for g = r, r + S, ... from every peer over distributed shared memory and writes it;
-    // the second barrier keeps each CTA's shared memory alive until its peers have read it.
-    // Every CTA reaches both barriers, on the error paths too.
+    // partial tile is in its CTA's shared memory ([token][row]); CTA r then sums its BN / S
+    // tokens from every peer over distributed shared memory and writes them; the second
+    // barrier keeps each CTA's shared memory alive until its peers have read it. Every CTA
+    // reaches both barriers, on the error paths too.
     cluster_sync();
     if (warp < 4 && s_fail == 0 && nk > 0) {
-      // this CTA's tokens: BN / S consecutive ones (all S CTAs work), in groups of C tokens
-      // whose S x C partials (<= 64 values) are all loaded before they are summed
-      const uint32_t local = smem_u32(xtile) + 4u * static_cast<uint32_t>(tid);
+      // a thread takes 4 consecutive rows of a token: one warp reads a whole token row
+      // (512 contiguous bytes) per 16-byte load, and stores 4 consecutive outputs. All loads
+      // of a thread (<= 64 words) are issued before the first sum.
+      const uint32_t xbase = smem_u32(xtile);
       auto reduce = [&](auto S_) {
         constexpr int S = decltype(S_)::value, G = BN / S;
-        constexpr int C0 = (64 / S < 16) ? 64 / S : 16, C = C0 < G ? C0 : G;
-#pragma unroll 1
-        for (int c0 = split * G; c0 < (split + 1) * G; c0 += C) {
-          const int cnt = min(C, (split + 1) * G - c0);
-          float rv[16];
-          load16(c0, rv, cnt);
-          uint32_t part[S][C];
+        uint32_t pb[S];
 #pragma unroll
-          for (int r = 0; r < S; ++r) {
-            const uint32_t src = cluster_map(local + 4u * 128u * c0, r);
+        for (int r = 0; r < S; ++r) pb[r] = cluster_map(xbase, r);
+        const int tok0 = split * G;  // first token (within the tile) of this CTA
+        if (!p.pair) {
+          constexpr int NI = (G + 3) / 4;
+          const int q = tid & 31, w = tid >> 5;
+          const int nq = n0 + 4 * q;
+          const bool full = p.vec && nq + 3 < a.N;
+          float rv[NI][4];
+          uint32_t part[NI][S][4];
 #pragma unroll
-            for (int j = 0; j < C; ++j) part[r][j] = j < cnt ? ld_cluster_u32(src + 4u * 128u * j) : 0u;
+          for (int i = 0; i < NI; ++i) {
+            const int j = w + 4 * i, t = t0 + tok0 + j;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) rv[i][e] = 0.0f;
+            if (!add_resid || j >= G || t >= a.M) continue;
+            const float* rp = a.resid + static_cast<int64_t>(t) * a.ldr + nq;
+            if (full) {
+              const float4 v4 = *reinterpret_cast<const float4*>(rp);
+              rv[i][0] = v4.x; rv[i][1] = v4.y; rv[i][2] = v4.z; rv[i][3] = v4.w;
+            } else {
+#pragma unroll
+              for (int e = 0; e < 4; ++e) rv[i][e] = nq + e < a.N ? rp[e] : 0.0f;
+            }
           }
-          uint32_t v[16];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            v[j] = 0;
-            if (j < C)
+          for (int i = 0; i < NI; ++i) {
+            const int j = w + 4 * i;
+            const uint32_t off = 4u * static_cast<uint32_t>((tok0 + j) * 128 + 4 * q);
 #pragma unroll
-              for (int r = 0; r < S; ++r) v[j] += part[r][j < C ? j : 0];
+            for (int r = 0; r < S; ++r) {
+              if (j < G) ld_cluster_v4(pb[r] + off, part[i][r]);
+              else part[i][r][0] = part[i][r][1] = part[i][r][2] = part[i][r][3] = 0u;
+            }
           }
-          emit16(c0, v, rv, cnt);
+#pragma unroll
+          for (int i = 0; i < NI; ++i) {
+            const int j = w + 4 * i, t = t0 + tok0 + j;
+            if (j >= G || t >= a.M) continue;
+            const uint32_t rs = static_cast<uint32_t>(s_rowsum[tok0 + j]);
+            float o[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              uint32_t v = 0;
+#pragma unroll
+              for (int r = 0; r < S; ++r) v += part[i][r][e];
+              const int32_t acc = static_cast<int32_t>(v - rs);
+              if (a.acc_out && nq + e < a.N) a.acc_out[static_cast<int64_t>(t) * a.N + nq + e] = acc;
+              o[e] = __fmul_rn(__int2float_rn(acc), P.scale);
+              if (a.resid) o[e] = __fadd_rn(rv[i][e], o[e]);
+            }
+            if (!P.out) continue;
+            float* op = P.out + static_cast<int64_t>(t) * a.ldo + nq;
+            if (full) {
+              *reinterpret_cast<float4*>(op) = make_float4(o[0], o[1], o[2], o[3]);
+            } else {
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                if (nq + e < a.N) op[e] = o[e];
+            }
+          }
+        } else {
+          // SwiGLU pair: tile rows [0, 64) are gate rows, [64, 128) the matching up rows; a
+          // thread combines 4 gate rows with their 4 up rows for its tokens
+          constexpr int NI = (G + 7) / 8;
+          const int q = tid & 15, w = tid >> 4;
+          const int col = 64 * blockIdx.x + 4 * q;  // output column of gate row 4q
+          uint32_t pg[NI][S][4], pu[NI][S][4];
+#pragma unroll
+          for (int i = 0; i < NI; ++i) {
+            const int j = w + 8 * i;
+            const uint32_t off = 4u * static_cast<uint32_t>((tok0 + j) * 128 + 4 * q);
+#pragma unroll
+            for (int r = 0; r < S; ++r) {
+              if (j < G) {
+                ld_cluster_v4(pb[r] + off, pg[i][r]);
+                ld_cluster_v4(pb[r] + off + 4u * 64u, pu[i][r]);
+              } else {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) pg[i][r][e] = pu[i][r][e] = 0u;
+              }
+            }
+          }
+          const int I = p.pair * 32;
+#pragma unroll
+          for (int i = 0; i < NI; ++i) {
+            const int j = w + 8 * i, t = t0 + tok0 + j;
+            if (j >= G || t >= a.M) continue;
+            const uint32_t rs = static_cast<uint32_t>(s_rowsum[tok0 + j]);
+            float g[4], u[4], z[4];
+            bool body[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              uint32_t vg = 0, vu = 0;
+#pragma unroll
+              for (int r = 0; r < S; ++r) {
+                vg += pg[i][r][e];
+                vu += pu[i][r][e];
+              }
+              const int32_t ag = static_cast<int32_t>(vg - rs), au = static_cast<int32_t>(vu - rs);
+              if (a.acc_out) {
+                a.acc_out[static_cast<int64_t>(t) * a.N + col + e] = ag;
+                a.acc_out[static_cast<int64_t>(t) * a.N + I + col + e] = au;
+              }
+              g[e] = __fmul_rn(__int2float_rn(ag), P.scale);
+              u[e] = __fmul_rn(__int2float_rn(au), P.scale);
+              // element (t, col) is in the scalar tail of its segment only in the segment's
+              // last row, at columns >= tail_from (fewer than 8, so the division is rare)
+              body[e] = col + e < p.tail_from || (t + 1) % p.seg_rows != 0;
+            }
+            swiglu_n(g, u, body, z);
+            float* op = P.out + static_cast<int64_t>(t) * a.ldo + col;
+            if (p.vec) {
+              *reinterpret_cast<float4*>(op) = make_float4(z[0], z[1], z[2], z[3]);
+            } else {
+#pragma unroll
+              for (int e = 0; e < 4; ++e) op[e] = z[e];
+            }
+          }
         }
       };
       if (p.splits == 2) reduce(std::integral_constant<int, 2>{});
@@ -762,6 +860,13 @@ static cudaError_t launch_tc(const MatmulArgs* a, int nproj, int pair, int64_t s
   }
   p.err = m.err;
   p.splits = splits;
+  {
+    auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+    bool vec = m.ldo % 4 == 0 && (!m.resid || (al16(m.resid) && m.ldr % 4 == 0)) &&
+               (!m.acc_out || (al16(m.acc_out) && m.N % 4 == 0));
+    for (int j = 0; j < nproj; ++j) vec = vec && (!a[j].out || al16(a[j].out));
+    p.vec = vec ? 1 : 0;
+  }
   for (int j = 0; j < nproj; ++j) p.pj[j] = TcProj{a[j].w, a[j].rowsum, a[j].out, a[j].scale};
   switch (tc_token_tile(m.M)) {
     case 16: return launch_tc_bn<16, 1>(p, a, m.pdl, s);

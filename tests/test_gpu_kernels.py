@@ -118,6 +118,17 @@ def test_bitlinear_many_rows_all_match(cuda, orc):
     assert bits_equal(out, r_out)
 
 
+@pytest.mark.parametrize("M,K,N", [(64, 2048, 101), (40, 2048, 200), (20, 1000, 66), (64, 5632, 256)])
+def test_bitlinear_split_k_tile_edges(cuda, orc, M, K, N):
+    """Few output tiles, so the reduction is split over a cluster: partial row quads
+    (N % 4 != 0, no 16-byte stores), tokens past M in a tile, every split count."""
+    x, nw, wq = sweep_inputs(M, K, N, seed=M + K + N)
+    out, acc, _ = run_gpu(cuda, x, nw, wq, 20.0, "fixed")
+    r_out, r_acc, _ = orc.bitlinear(x, nw, wq, 20.0, act_quant=1)
+    assert np.array_equal(acc, r_acc)
+    assert bits_equal(out, r_out)
+
+
 def test_bitlinear_saturation_and_ragged(cuda, orc):
     """Q5.10 saturation (|y*1024| > 32767), K%8 tails, K%64 and N%32 padding, frac_bits."""
     rng = np.random.default_rng(11)
@@ -186,6 +197,26 @@ def test_swiglu_golden(cuda, n):
     g = golden("ops.npz")
     out = api.swiglu(to_dev(g[f"ew{n}_x"], cuda), to_dev(g[f"ew{n}_b"], cuda))
     assert bits_equal(out.cpu().numpy(), g[f"ew{n}_swiglu"])
+
+
+def test_swiglu_wide_range_matches_oracle(cuda, orc):
+    """The exact exp and the branch-free correctly rounded division over a wide range:
+    magnitudes 2^-40..2^40 of both signs, values around the exp clamp, zeros, subnormals,
+    infinities and NaN, with a SIMD tail; b = 1 on even elements, so those outputs are the
+    quotients themselves. Bit-exact against the reference restatement."""
+    rng = np.random.default_rng(5)
+    n = 1 << 22
+    a = (np.exp2(rng.uniform(-40, 40, n)) * rng.choice([-1.0, 1.0], n)).astype(np.float32)
+    a[: n // 4] = rng.uniform(-100.0, 100.0, n // 4).astype(np.float32)
+    specials = np.array([0.0, -0.0, 1e-45, -1e-45, 1e-38, -1e-38, 88.3762626647949,
+                         -88.3762626647949, 89.0, -89.0, 1e30, -1e30, np.inf, -np.inf, np.nan,
+                         1.0, -1.0, 2.0, 0.5, 27.7, -27.7, 41.6, -41.6], np.float32)
+    a[: specials.size] = specials
+    a = np.concatenate([a, specials[:5]])  # length % 8 == 5: a scalar tail
+    b = np.ones_like(a)
+    b[1::2] = rng.standard_normal(b[1::2].size).astype(np.float32)
+    out = api.swiglu(to_dev(a, cuda), to_dev(b, cuda)).cpu().numpy()
+    assert bits_equal(out, orc.swiglu(a, b))
 
 
 def test_bitlinear_rejects_bad_shapes(cuda):
