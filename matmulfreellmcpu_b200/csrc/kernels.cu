@@ -92,20 +92,36 @@ __device__ __forceinline__ void stage_arrays(float* const (&dst)[NA], const floa
   }
 }
 
-// Shared-memory floats of one prep CTA: the row, plus (when staged) every per-element input.
+// Shared-memory floats of one prep CTA: the row, plus (when staged) every per-element input,
+// each array padded to a multiple of 4 floats (16-byte aligned).
 static int64_t prep_smem_floats(const PrepArgs& a, int mode, bool staged) {
   int arrays = 1;
   if (staged) arrays += (mode != kPrepPlain ? 1 : 0) + (mode == kPrepSwishgate ? 1 : 0) + a.nproj;
-  return static_cast<int64_t>(arrays) * a.K;
+  return static_cast<int64_t>(arrays) * ((a.K + 3) & ~3);
+}
+
+// 4 consecutive floats p[c0..c0+3] (0 past K): one 16-byte load when aligned and in range
+__device__ __forceinline__ void load4(const float* p, int c0, int K, bool vec, float (&v)[4]) {
+  if (vec && c0 + 3 < K) {
+    const float4 t = *reinterpret_cast<const float4*>(p + c0);
+    v[0] = t.x;
+    v[1] = t.y;
+    v[2] = t.z;
+    v[3] = t.w;
+  } else {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) v[u] = c0 + u < K ? p[c0 + u] : 0.0f;
+  }
 }
 
 __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepArgs a, int mode, int staged) {
-  extern __shared__ float sbuf[];
+  extern __shared__ __align__(16) float sbuf[];
   float* srow = sbuf;  // the row being normalized, K floats
   __shared__ float s_rstd;
   __shared__ int s_red[3][kPrepThreads / 32];
   const int m = blockIdx.x, K = a.K, tid = threadIdx.x;
   const int64_t Kp = padded_k(K);
+  const int K4 = (K + 3) & ~3;  // staged arrays start 16-byte aligned
   const float* x = a.x + static_cast<int64_t>(m) * K;
   const float* orow = a.o ? a.o + static_cast<int64_t>(m) * K : nullptr;
 
@@ -115,26 +131,28 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepArgs a, int mode
   const float* nw[3] = {a.normw[0], a.normw[1], a.normw[2]};
   {
     const bool use1 = staged && mode != kPrepPlain, use2 = staged && mode == kPrepSwishgate;
-    float* p1 = sbuf + K;
-    float* p2 = p1 + (use1 ? K : 0);
-    float* p3 = p2 + (use2 ? K : 0);
+    float* p1 = sbuf + K4;
+    float* p2 = p1 + (use1 ? K4 : 0);
+    float* p3 = p2 + (use2 ? K4 : 0);
     // weights first: no earlier kernel writes them, so they load while the predecessor runs
     float* const dw[4] = {use1 ? p1 : nullptr, staged && a.nproj > 0 ? p3 : nullptr,
-                          staged && a.nproj > 1 ? p3 + K : nullptr,
-                          staged && a.nproj > 2 ? p3 + 2 * K : nullptr};
+                          staged && a.nproj > 1 ? p3 + K4 : nullptr,
+                          staged && a.nproj > 2 ? p3 + 2 * K4 : nullptr};
     const float* const sw[4] = {a.prew, a.normw[0], a.normw[1], a.normw[2]};
     stage_arrays<8>(dw, sw, K);
     grid_dep_launch();
     grid_dep_wait();
     float* const dr[2] = {srow, use2 ? p2 : nullptr};
     const float* const sr[2] = {x, orow};
-    stage_arrays<8>(dr, sr, K);
+    // one memory latency per row: 12 loads per thread for rows longer than 8 per thread
+    if (K > 8 * static_cast<int>(blockDim.x)) stage_arrays<12>(dr, sr, K);
+    else stage_arrays<8>(dr, sr, K);
     if (use1) prew = p1;
     if (use2) orow = p2;
     if (staged) {
       nw[0] = p3;
-      nw[1] = p3 + K;
-      nw[2] = p3 + 2 * K;
+      nw[1] = p3 + K4;
+      nw[2] = p3 + 2 * K4;
     }
   }
   __syncthreads();
@@ -181,25 +199,37 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepArgs a, int mode
   __syncthreads();
   const float r2 = s_rstd;
 
+  // 4 consecutive elements per thread: 16-byte loads of the staged arrays, one 4-byte store
+  // per byte plane (Kp is a multiple of 64) or one 16-byte store of fp32 activations
   int local[3] = {0, 0, 0};
-  for (int c = tid; c < Kp; c += blockDim.x) {
-    const float xv = c < K ? srow[c] : 0.0f;
+  for (int c0 = 4 * tid; c0 < Kp; c0 += 4 * static_cast<int>(blockDim.x)) {
+    float xv[4];
+    load4(srow, c0, K, true, xv);
 #pragma unroll
     for (int j = 0; j < 3; ++j) {
       if (j >= a.nproj) break;
-      float y = 0.0f;
-      if (c < K) {
-        y = norm_x(xv, r2, nw[j][c]);
-        if (j == 0 && a.norm_out) a.norm_out[static_cast<int64_t>(m) * K + c] = y;
+      float wv[4], y[4];
+      load4(nw[j], c0, K, staged != 0, wv);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int c = c0 + u;
+        y[u] = c < K ? norm_x(xv[u], r2, wv[u]) : 0.0f;
+        if (j == 0 && a.norm_out && c < K) a.norm_out[static_cast<int64_t>(m) * K + c] = y[u];
       }
       if (a.fixed) {
-        const int32_t q = c < K ? quant_x(y, a.qs, in_body(c, K)) : 0;
-        local[j] += q;
-        a.planes[j][static_cast<int64_t>(m) * Kp + c] = static_cast<int8_t>(q >> 8);
-        a.planes[j][(static_cast<int64_t>(a.M) + m) * Kp + c] =
-            static_cast<int8_t>((q & 0xff) ^ (a.lo_signed ? 0x80 : 0));
+        uint32_t hi = 0, lo = 0;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int c = c0 + u;
+          const int32_t q = c < K ? quant_x(y[u], a.qs, in_body(c, K)) : 0;
+          local[j] += q;
+          hi |= static_cast<uint32_t>((q >> 8) & 0xff) << (8 * u);
+          lo |= static_cast<uint32_t>((q & 0xff) ^ (a.lo_signed ? 0x80 : 0)) << (8 * u);
+        }
+        *reinterpret_cast<uint32_t*>(a.planes[j] + static_cast<int64_t>(m) * Kp + c0) = hi;
+        *reinterpret_cast<uint32_t*>(a.planes[j] + (static_cast<int64_t>(a.M) + m) * Kp + c0) = lo;
       } else {
-        a.yf[j][static_cast<int64_t>(m) * Kp + c] = y;
+        *reinterpret_cast<float4*>(a.yf[j] + static_cast<int64_t>(m) * Kp + c0) = make_float4(y[0], y[1], y[2], y[3]);
       }
     }
   }
@@ -463,6 +493,63 @@ __global__ void scan_kernel(float* __restrict__ out, const float* __restrict__ s
   if (state) state[lane] = st;
 }
 
+// The token mixer of one decode step (one position per lane, H >= 8): a grid of about one
+// 512-thread CTA per SM, each thread taking kMixLanes lanes per round with their loads and
+// their divisions batched (all CTAs start as soon as the previous kernel's CTAs leave).
+constexpr int kMixLanes = 2, kMixDecThreads = 512;
+__global__ void __launch_bounds__(kMixDecThreads) mixer_decode_kernel(
+    float* __restrict__ out, const float* __restrict__ iv, const float* __restrict__ fv,
+    float* __restrict__ state, const float* __restrict__ lb, int nseq, int H, int64_t seg) {
+  grid_dep_launch();
+  grid_dep_wait();
+  const int64_t total = static_cast<int64_t>(nseq) * H, stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  // lane l = (q, c) is in the scalar tail of its segment (seg = seg_rows * H elements) only
+  // in the segment's last row q, at columns c >= tail_from; (q, c) advance by counters
+  const int64_t seg_rows = seg / H;
+  const int tail_from = H - static_cast<int>(seg % 8);
+  int64_t l0 = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  int64_t q = l0 / H;
+  int c = static_cast<int>(l0 % H);
+  const int64_t dq = stride / H;
+  const int dc = static_cast<int>(stride % H);
+  for (; l0 < total; l0 += kMixLanes * stride) {
+    float a[kMixLanes], b[kMixLanes], s0[kMixLanes], lv[kMixLanes];
+    bool body[kMixLanes];
+#pragma unroll
+    for (int u = 0; u < kMixLanes; ++u) {  // all loads of the round first
+      const int64_t l = l0 + u * stride;
+      const bool ok = l < total;
+      a[u] = ok ? __ldcs(iv + l) : 0.0f;
+      b[u] = ok ? __ldcs(fv + l) : 0.0f;
+      s0[u] = (ok && state) ? state[l] : 0.0f;
+      lv[u] = (ok && lb) ? __ldg(lb + c) : 0.0f;
+      body[u] = c < tail_from || (q + 1) % seg_rows != 0;
+      c += dc;
+      q += dq;
+      if (c >= H) {
+        c -= H;
+        ++q;
+      }
+    }
+    float f[kMixLanes], om[kMixLanes], sv[kMixLanes];
+    sigmoid_n(b, body, f);
+#pragma unroll
+    for (int u = 0; u < kMixLanes; ++u) {
+      if (lb) f[u] = lower_bound_x(f[u], lv[u]);
+      om[u] = __fadd_rn(1.0f, -f[u]);
+    }
+    swiglu_n(a, om, body, sv);
+#pragma unroll
+    for (int u = 0; u < kMixLanes; ++u) {
+      const int64_t l = l0 + u * stride;  // element index = lane (T = 1)
+      if (l >= total) break;
+      const float st = hgrn_step_x(f[u], s0[u], sv[u]);
+      out[l] = st;
+      if (state) state[l] = st;
+    }
+  }
+}
+
 // The whole token mixer in one pass, one thread per (sequence, channel) lane: per step the
 // forget gate (sigmoid, lower bound), the SwiGLU scan input and the recurrence step, i.e.
 // the reference's gate loop (hgrn_model.cpp:109-134) followed by its scan (hgrn_scan.cpp:11-19)
@@ -474,55 +561,6 @@ __global__ void __launch_bounds__(128) mixer_kernel(float* __restrict__ out, con
                                                     int64_t seg) {
   grid_dep_launch();
   grid_dep_wait();
-  if (T == 1 && H >= 8) {  // one position per lane (decode): a small grid, 4 lanes per thread per round
-    const int64_t total = static_cast<int64_t>(nseq) * H, stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    // lane l = (q, c) is in the scalar tail of its segment (seg = seg_rows * H elements) only
-    // in the segment's last row q, at columns c >= tail_from; (q, c) advance by counters
-    const int64_t seg_rows = seg / H;
-    const int tail_from = H - static_cast<int>(seg % 8);
-    int64_t l0 = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-    int64_t q = l0 / H;
-    int c = static_cast<int>(l0 % H);
-    const int64_t dq = stride / H;
-    const int dc = static_cast<int>(stride % H);
-    for (; l0 < total; l0 += 4 * stride) {
-      float a[4], b[4], s0[4], lv[4];
-      bool body[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {  // all loads of the round first
-        const int64_t l = l0 + u * stride;
-        const bool ok = l < total;
-        a[u] = ok ? __ldcs(iv + l) : 0.0f;
-        b[u] = ok ? __ldcs(fv + l) : 0.0f;
-        s0[u] = (ok && state) ? state[l] : 0.0f;
-        lv[u] = (ok && lb) ? __ldg(lb + c) : 0.0f;
-        body[u] = c < tail_from || (q + 1) % seg_rows != 0;
-        c += dc;
-        q += dq;
-        if (c >= H) {
-          c -= H;
-          ++q;
-        }
-      }
-      float f[4], om[4], sv[4];
-      sigmoid_n(b, body, f);
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        if (lb) f[u] = lower_bound_x(f[u], lv[u]);
-        om[u] = __fadd_rn(1.0f, -f[u]);
-      }
-      swiglu_n(a, om, body, sv);
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int64_t l = l0 + u * stride;  // element index = lane (T = 1)
-        if (l >= total) break;
-        const float st = hgrn_step_x(f[u], s0[u], sv[u]);
-        out[l] = st;
-        if (state) state[l] = st;
-      }
-    }
-    return;
-  }
   const int64_t lane = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   if (lane >= static_cast<int64_t>(nseq) * H) return;
   const int64_t q = lane / H, c = lane % H;
@@ -570,9 +608,13 @@ cudaError_t launch_mixer(float* i, float* f, float* recur, float* state, const f
                          int nseq, int len, int H, int seg_rows, cudaStream_t s, bool pdl) {
   const int64_t lanes = static_cast<int64_t>(nseq) * H;
   if (lanes == 0 || len == 0) return cudaSuccess;
-  // decode (len 1): about one CTA per SM, so that every CTA is resident (and triggers the
-  // dependent launch) while the previous kernel's CTAs still occupy the SMs
-  const int64_t ctas = len == 1 && H >= 8 ? std::min<int64_t>(ceil_div(lanes, 128 * 4), sm_count()) : ceil_div(lanes, 128);
+  if (len == 1 && H >= 8) {
+    const int64_t ctas = std::min<int64_t>(ceil_div(lanes, kMixDecThreads * kMixLanes), sm_count());
+    return launch_k(mixer_decode_kernel, dim3(static_cast<unsigned>(ctas)), dim3(kMixDecThreads), 0, s,
+                    pdl, recur, static_cast<const float*>(i), static_cast<const float*>(f), state, lb,
+                    nseq, H, static_cast<int64_t>(seg_rows) * H);
+  }
+  const int64_t ctas = ceil_div(lanes, 128);
   return launch_k(mixer_kernel, dim3(static_cast<unsigned>(ctas)), dim3(128), 0, s, pdl,
                   recur, static_cast<const float*>(i), static_cast<const float*>(f), state, lb, nseq, len,
                   H, static_cast<int64_t>(seg_rows) * H);

@@ -133,6 +133,12 @@ __device__ __forceinline__ void ld_cluster_v4(uint32_t addr, uint32_t* v) {
                : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
                : "r"(addr));
 }
+// the same from this CTA's own shared memory
+__device__ __forceinline__ void ld_shared_v4(uint32_t addr, uint32_t* v) {
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
+               : "r"(addr));
+}
 
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -605,57 +611,70 @@ __global__ void __launch_bounds__(kTcThreads, 2)
           const int q = tid & 31, w = tid >> 5;
           const int nq = n0 + 4 * q;
           const bool full = p.vec && nq + 3 < a.N;
-          float rv[NI][4];
-          uint32_t part[NI][S][4];
+          // residuals and partials of token j (zeros for j >= G): the own partial from local
+          // shared memory
+          auto fetch = [&](int j, float (&fr)[4], uint32_t (&fp)[S][4]) {
+            const int t = t0 + tok0 + j;
 #pragma unroll
-          for (int i = 0; i < NI; ++i) {
-            const int j = w + 4 * i, t = t0 + tok0 + j;
+            for (int e = 0; e < 4; ++e) fr[e] = 0.0f;
+            if (add_resid && j < G && t < a.M) {
+              const float* rp = a.resid + static_cast<int64_t>(t) * a.ldr + nq;
+              if (full) {
+                const float4 v4 = *reinterpret_cast<const float4*>(rp);
+                fr[0] = v4.x; fr[1] = v4.y; fr[2] = v4.z; fr[3] = v4.w;
+              } else {
 #pragma unroll
-            for (int e = 0; e < 4; ++e) rv[i][e] = 0.0f;
-            if (!add_resid || j >= G || t >= a.M) continue;
-            const float* rp = a.resid + static_cast<int64_t>(t) * a.ldr + nq;
-            if (full) {
-              const float4 v4 = *reinterpret_cast<const float4*>(rp);
-              rv[i][0] = v4.x; rv[i][1] = v4.y; rv[i][2] = v4.z; rv[i][3] = v4.w;
-            } else {
-#pragma unroll
-              for (int e = 0; e < 4; ++e) rv[i][e] = nq + e < a.N ? rp[e] : 0.0f;
+                for (int e = 0; e < 4; ++e) fr[e] = nq + e < a.N ? rp[e] : 0.0f;
+              }
             }
-          }
-#pragma unroll
-          for (int i = 0; i < NI; ++i) {
-            const int j = w + 4 * i;
             const uint32_t off = 4u * static_cast<uint32_t>((tok0 + j) * 128 + 4 * q);
 #pragma unroll
             for (int r = 0; r < S; ++r) {
-              if (j < G) ld_cluster_v4(pb[r] + off, part[i][r]);
-              else part[i][r][0] = part[i][r][1] = part[i][r][2] = part[i][r][3] = 0u;
+              if (j >= G) fp[r][0] = fp[r][1] = fp[r][2] = fp[r][3] = 0u;
+              else if (r == split) ld_shared_v4(xbase + off, fp[r]);
+              else ld_cluster_v4(pb[r] + off, fp[r]);
             }
-          }
-#pragma unroll
+          };
+          // one token per iteration, rolled (cold instruction cache); the next token's loads
+          // are issued before this one is combined
+          float rv[4];
+          uint32_t part[S][4];
+          fetch(w, rv, part);
+#pragma unroll 1
           for (int i = 0; i < NI; ++i) {
             const int j = w + 4 * i, t = t0 + tok0 + j;
-            if (j >= G || t >= a.M) continue;
-            const uint32_t rs = static_cast<uint32_t>(s_rowsum[tok0 + j]);
-            float o[4];
+            float nr[4];
+            uint32_t np[S][4];
+            fetch(i + 1 < NI ? j + 4 : G, nr, np);
+            if (j < G && t < a.M) {
+              const uint32_t rs = static_cast<uint32_t>(s_rowsum[tok0 + j]);
+              float o[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                uint32_t v = 0;
+#pragma unroll
+                for (int r = 0; r < S; ++r) v += part[r][e];
+                const int32_t acc = static_cast<int32_t>(v - rs);
+                if (a.acc_out && nq + e < a.N) a.acc_out[static_cast<int64_t>(t) * a.N + nq + e] = acc;
+                o[e] = __fmul_rn(__int2float_rn(acc), P.scale);
+                if (a.resid) o[e] = __fadd_rn(rv[e], o[e]);
+              }
+              if (P.out) {
+                float* op = P.out + static_cast<int64_t>(t) * a.ldo + nq;
+                if (full) {
+                  *reinterpret_cast<float4*>(op) = make_float4(o[0], o[1], o[2], o[3]);
+                } else {
+#pragma unroll
+                  for (int e = 0; e < 4; ++e)
+                    if (nq + e < a.N) op[e] = o[e];
+                }
+              }
+            }
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              uint32_t v = 0;
+              rv[e] = nr[e];
 #pragma unroll
-              for (int r = 0; r < S; ++r) v += part[i][r][e];
-              const int32_t acc = static_cast<int32_t>(v - rs);
-              if (a.acc_out && nq + e < a.N) a.acc_out[static_cast<int64_t>(t) * a.N + nq + e] = acc;
-              o[e] = __fmul_rn(__int2float_rn(acc), P.scale);
-              if (a.resid) o[e] = __fadd_rn(rv[i][e], o[e]);
-            }
-            if (!P.out) continue;
-            float* op = P.out + static_cast<int64_t>(t) * a.ldo + nq;
-            if (full) {
-              *reinterpret_cast<float4*>(op) = make_float4(o[0], o[1], o[2], o[3]);
-            } else {
-#pragma unroll
-              for (int e = 0; e < 4; ++e)
-                if (nq + e < a.N) op[e] = o[e];
+              for (int r = 0; r < S; ++r) part[r][e] = np[r][e];
             }
           }
         } else {
@@ -664,57 +683,72 @@ __global__ void __launch_bounds__(kTcThreads, 2)
           constexpr int NI = (G + 7) / 8;
           const int q = tid & 15, w = tid >> 4;
           const int col = 64 * blockIdx.x + 4 * q;  // output column of gate row 4q
-          uint32_t pg[NI][S][4], pu[NI][S][4];
-#pragma unroll
-          for (int i = 0; i < NI; ++i) {
-            const int j = w + 8 * i;
+          const int I = p.pair * 32;
+          // partials of token j (zeros for j >= G): the own one from local shared memory
+          auto fetch = [&](int j, uint32_t (&fg)[S][4], uint32_t (&fu)[S][4]) {
             const uint32_t off = 4u * static_cast<uint32_t>((tok0 + j) * 128 + 4 * q);
 #pragma unroll
             for (int r = 0; r < S; ++r) {
-              if (j < G) {
-                ld_cluster_v4(pb[r] + off, pg[i][r]);
-                ld_cluster_v4(pb[r] + off + 4u * 64u, pu[i][r]);
+              if (j < G && r == split) {
+                ld_shared_v4(xbase + off, fg[r]);
+                ld_shared_v4(xbase + off + 4u * 64u, fu[r]);
+              } else if (j < G) {
+                ld_cluster_v4(pb[r] + off, fg[r]);
+                ld_cluster_v4(pb[r] + off + 4u * 64u, fu[r]);
               } else {
 #pragma unroll
-                for (int e = 0; e < 4; ++e) pg[i][r][e] = pu[i][r][e] = 0u;
+                for (int e = 0; e < 4; ++e) fg[r][e] = fu[r][e] = 0u;
               }
             }
-          }
-          const int I = p.pair * 32;
-#pragma unroll
+          };
+          // one token per iteration, rolled (this code runs once per CTA, from a cold
+          // instruction cache); the next token's partials load while this one is combined
+          uint32_t pg[S][4], pu[S][4];
+          fetch(w, pg, pu);
+#pragma unroll 1
           for (int i = 0; i < NI; ++i) {
             const int j = w + 8 * i, t = t0 + tok0 + j;
-            if (j >= G || t >= a.M) continue;
-            const uint32_t rs = static_cast<uint32_t>(s_rowsum[tok0 + j]);
-            float g[4], u[4], z[4];
-            bool body[4];
+            uint32_t ng[S][4], nu[S][4];
+            fetch(i + 1 < NI ? j + 8 : G, ng, nu);
+            if (j < G && t < a.M) {
+              const uint32_t rs = static_cast<uint32_t>(s_rowsum[tok0 + j]);
+              float g[4], u[4], z[4];
+              bool body[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              uint32_t vg = 0, vu = 0;
+              for (int e = 0; e < 4; ++e) {
+                uint32_t vg = 0, vu = 0;
 #pragma unroll
-              for (int r = 0; r < S; ++r) {
-                vg += pg[i][r][e];
-                vu += pu[i][r][e];
+                for (int r = 0; r < S; ++r) {
+                  vg += pg[r][e];
+                  vu += pu[r][e];
+                }
+                const int32_t ag = static_cast<int32_t>(vg - rs), au = static_cast<int32_t>(vu - rs);
+                if (a.acc_out) {
+                  a.acc_out[static_cast<int64_t>(t) * a.N + col + e] = ag;
+                  a.acc_out[static_cast<int64_t>(t) * a.N + I + col + e] = au;
+                }
+                g[e] = __fmul_rn(__int2float_rn(ag), P.scale);
+                u[e] = __fmul_rn(__int2float_rn(au), P.scale);
+                // element (t, col) is in the scalar tail of its segment only in the segment's
+                // last row, at columns >= tail_from (fewer than 8, so the division is rare)
+                body[e] = col + e < p.tail_from || (t + 1) % p.seg_rows != 0;
               }
-              const int32_t ag = static_cast<int32_t>(vg - rs), au = static_cast<int32_t>(vu - rs);
-              if (a.acc_out) {
-                a.acc_out[static_cast<int64_t>(t) * a.N + col + e] = ag;
-                a.acc_out[static_cast<int64_t>(t) * a.N + I + col + e] = au;
-              }
-              g[e] = __fmul_rn(__int2float_rn(ag), P.scale);
-              u[e] = __fmul_rn(__int2float_rn(au), P.scale);
-              // element (t, col) is in the scalar tail of its segment only in the segment's
-              // last row, at columns >= tail_from (fewer than 8, so the division is rare)
-              body[e] = col + e < p.tail_from || (t + 1) % p.seg_rows != 0;
-            }
-            swiglu_n(g, u, body, z);
-            float* op = P.out + static_cast<int64_t>(t) * a.ldo + col;
-            if (p.vec) {
-              *reinterpret_cast<float4*>(op) = make_float4(z[0], z[1], z[2], z[3]);
-            } else {
+              swiglu_n(g, u, body, z);
+              float* op = P.out + static_cast<int64_t>(t) * a.ldo + col;
+              if (p.vec) {
+                *reinterpret_cast<float4*>(op) = make_float4(z[0], z[1], z[2], z[3]);
+              } else {
 #pragma unroll
-              for (int e = 0; e < 4; ++e) op[e] = z[e];
+                for (int e = 0; e < 4; ++e) op[e] = z[e];
+              }
             }
+#pragma unroll
+            for (int r = 0; r < S; ++r)
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                pg[r][e] = ng[r][e];
+                pu[r][e] = nu[r][e];
+              }
           }
         }
       };
