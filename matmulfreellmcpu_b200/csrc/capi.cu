@@ -142,6 +142,7 @@ void run_bitlinear(int k, float* const* outs, const float* x, const float* const
   p.fixed = fixed;
   // the tensor-core matmul (taken for >= kTcMinRows fixed rows) reads the low plane as lo - 128
   p.lo_signed = fixed && static_cast<int>(rows) >= kTcMinRows;
+  p.err = reinterpret_cast<uint32_t*>(base);
   for (int j = 0; j < k; ++j) {
     char* b = base + 256 + j * per;
     p.normw[j] = nws[j];

@@ -100,6 +100,31 @@ static int64_t prep_smem_floats(const PrepArgs& a, int mode, bool staged) {
   return static_cast<int64_t>(arrays) * ((a.K + 3) & ~3);
 }
 
+constexpr uint32_t kRowSpin = 1u << 22;  // bounded wait for a row's bulk copy
+
+__device__ __forceinline__ uint32_t shared_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+// bulk global -> shared copy of a row, completing on an mbarrier (no multicast)
+__device__ __forceinline__ void row_bulk_copy(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          shared_addr(dst)),
+      "l"(src), "r"(bytes), "r"(shared_addr(bar))
+      : "memory");
+}
+__device__ __forceinline__ bool row_bar_done(uint64_t* bar) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(shared_addr(bar))
+      : "memory");
+  return ok != 0;
+}
+
 // 4 consecutive floats p[c0..c0+3] (0 past K): one 16-byte load when aligned and in range
 __device__ __forceinline__ void load4(const float* p, int c0, int K, bool vec, float (&v)[4]) {
   if (vec && c0 + 3 < K) {
@@ -119,6 +144,7 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepArgs a, int mode
   float* srow = sbuf;  // the row being normalized, K floats
   __shared__ float s_rstd;
   __shared__ int s_red[3][kPrepThreads / 32];
+  __shared__ __align__(8) uint64_t s_rowbar;
   const int m = blockIdx.x, K = a.K, tid = threadIdx.x;
   const int64_t Kp = padded_k(K);
   const int K4 = (K + 3) & ~3;  // staged arrays start 16-byte aligned
@@ -131,6 +157,13 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepArgs a, int mode
   const float* nw[3] = {a.normw[0], a.normw[1], a.normw[2]};
   {
     const bool use1 = staged && mode != kPrepPlain, use2 = staged && mode == kPrepSwishgate;
+    // rows of a multiple of 4 floats at 16-byte aligned addresses arrive by one bulk copy each
+    const bool bulk = (K & 3) == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 &&
+                      (!use2 || (reinterpret_cast<uintptr_t>(a.o) & 15) == 0);
+    if (bulk && tid == 0) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(shared_addr(&s_rowbar)));
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
     float* p1 = sbuf + K4;
     float* p2 = p1 + (use1 ? K4 : 0);
     float* p3 = p2 + (use2 ? K4 : 0);
@@ -140,13 +173,34 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepArgs a, int mode
                           staged && a.nproj > 2 ? p3 + 2 * K4 : nullptr};
     const float* const sw[4] = {a.prew, a.normw[0], a.normw[1], a.normw[2]};
     stage_arrays<8>(dw, sw, K);
+    if (bulk) __syncthreads();  // the barrier's initialisation, before anyone waits on it
     grid_dep_launch();
     grid_dep_wait();
-    float* const dr[2] = {srow, use2 ? p2 : nullptr};
-    const float* const sr[2] = {x, orow};
-    // one memory latency per row: 12 loads per thread for rows longer than 8 per thread
-    if (K > 8 * static_cast<int>(blockDim.x)) stage_arrays<12>(dr, sr, K);
-    else stage_arrays<8>(dr, sr, K);
+    if (bulk) {
+      if (tid == 0) {
+        const uint32_t bytes = static_cast<uint32_t>(K) * 4u;
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(shared_addr(&s_rowbar)),
+                     "r"(use2 ? 2 * bytes : bytes)
+                     : "memory");
+        row_bulk_copy(srow, x, bytes, &s_rowbar);
+        if (use2) row_bulk_copy(p2, orow, bytes, &s_rowbar);
+      }
+      bool done = false;
+      for (uint32_t i = 0; i < kRowSpin && !done; ++i) done = row_bar_done(&s_rowbar);
+      if (__syncthreads_or(!done)) {  // (uniform) report, let the copies land (bounded), and
+                                      // leave the outputs unwritten
+        if (tid == 0 && a.err) atomicOr(a.err, kErrTimeout);
+        for (uint32_t i = 0; i < kRowSpin && !row_bar_done(&s_rowbar); ++i) {
+        }
+        return;
+      }
+    } else {
+      float* const dr[2] = {srow, use2 ? p2 : nullptr};
+      const float* const sr[2] = {x, orow};
+      // one memory latency per row: 12 loads per thread for rows longer than 8 per thread
+      if (K > 8 * static_cast<int>(blockDim.x)) stage_arrays<12>(dr, sr, K);
+      else stage_arrays<8>(dr, sr, K);
+    }
     if (use1) prew = p1;
     if (use2) orow = p2;
     if (staged) {

@@ -32,6 +32,7 @@ struct PrepArgs {
   float qs = 1024.0f;            // 2^frac_bits
   bool fixed = true;
   bool pdl = false;              // launch as a programmatic dependent of the previous kernel
+  uint32_t* err = nullptr;       // optional: bit kErrTimeout on a timed-out wait
 };
 
 struct MatmulArgs {

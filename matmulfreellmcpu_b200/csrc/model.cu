@@ -313,6 +313,7 @@ void Model::prep(const PrepArgs& p) {
                        rows * out_row * p.nproj;
   PrepArgs q = p;
   q.pdl = pdl_;
+  q.err = err_;
   q.lo_signed = tc_rows(q.M);  // the BitLinear of these rows runs on the tensor cores
   timed(kClsPrep, bytes, 0, [&] { CK(launch_prep(q, stream_)); });
 }
