@@ -157,9 +157,10 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepArgs a, int mode
   const float* nw[3] = {a.normw[0], a.normw[1], a.normw[2]};
   {
     const bool use1 = staged && mode != kPrepPlain, use2 = staged && mode == kPrepSwishgate;
+    const bool copy2 = use2 && a.mix_i == nullptr;  // o is read (not computed here)
     // rows of a multiple of 4 floats at 16-byte aligned addresses arrive by one bulk copy each
     const bool bulk = (K & 3) == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 &&
-                      (!use2 || (reinterpret_cast<uintptr_t>(a.o) & 15) == 0);
+                      (!copy2 || (reinterpret_cast<uintptr_t>(a.o) & 15) == 0);
     if (bulk && tid == 0) {
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(shared_addr(&s_rowbar)));
       asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -180,10 +181,10 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepArgs a, int mode
       if (tid == 0) {
         const uint32_t bytes = static_cast<uint32_t>(K) * 4u;
         asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(shared_addr(&s_rowbar)),
-                     "r"(use2 ? 2 * bytes : bytes)
+                     "r"(copy2 ? 2 * bytes : bytes)
                      : "memory");
         row_bulk_copy(srow, x, bytes, &s_rowbar);
-        if (use2) row_bulk_copy(p2, orow, bytes, &s_rowbar);
+        if (copy2) row_bulk_copy(p2, orow, bytes, &s_rowbar);
       }
       bool done = false;
       for (uint32_t i = 0; i < kRowSpin && !done; ++i) done = row_bar_done(&s_rowbar);
@@ -195,7 +196,7 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepArgs a, int mode
         return;
       }
     } else {
-      float* const dr[2] = {srow, use2 ? p2 : nullptr};
+      float* const dr[2] = {srow, copy2 ? p2 : nullptr};
       const float* const sr[2] = {x, orow};
       // one memory latency per row: 12 loads per thread for rows longer than 8 per thread
       if (K > 8 * static_cast<int>(blockDim.x)) stage_arrays<12>(dr, sr, K);
@@ -215,6 +216,41 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepArgs a, int mode
     if (tid < 8) {
       const float r = rstd_of(sumsq_exact8(srow, K, 0xffu), static_cast<float>(K), a.eps);
       if (tid == 0) s_rstd = r;
+    } else if (a.mix_i && tid >= 32) {
+      // the fused token mixer of this row (warps 1.., while warp 0 runs the norm chain): per
+      // lane the forget gate (sigmoid, lower bound), the SwiGLU scan input and one
+      // recurrence step, as mixer_decode_kernel; the recurrence output goes to shared memory
+      // (o of the swish gate), the new state and the output to global memory
+      const int nt = static_cast<int>(blockDim.x) - 32;
+      const int tail_from = K - static_cast<int>((static_cast<int64_t>(a.mix_seg_rows) * K) % 8);
+      const bool last_row = (m + 1) % a.mix_seg_rows == 0;
+      const int64_t rb = static_cast<int64_t>(m) * K;
+      float* ob = const_cast<float*>(orow);  // the o slot in shared memory (staged)
+      for (int c0 = 4 * (tid - 32); c0 < K; c0 += 4 * nt) {
+        const float4 i4 = __ldcs(reinterpret_cast<const float4*>(a.mix_i + rb + c0));
+        const float4 f4 = __ldcs(reinterpret_cast<const float4*>(a.mix_f + rb + c0));
+        const float4 s4 = *reinterpret_cast<const float4*>(a.mix_state + rb + c0);
+        const float4 l4 = a.mix_lb ? __ldg(reinterpret_cast<const float4*>(a.mix_lb + c0)) : make_float4(0, 0, 0, 0);
+        const float iv[4] = {i4.x, i4.y, i4.z, i4.w}, fv[4] = {f4.x, f4.y, f4.z, f4.w};
+        const float sv0[4] = {s4.x, s4.y, s4.z, s4.w}, lv[4] = {l4.x, l4.y, l4.z, l4.w};
+        bool body[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) body[u] = !last_row || c0 + u < tail_from;
+        float f[4], om[4], sw[4], st[4];
+        sigmoid_n(fv, body, f);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (a.mix_lb) f[u] = lower_bound_x(f[u], lv[u]);
+          om[u] = __fadd_rn(1.0f, -f[u]);
+        }
+        swiglu_n(iv, om, body, sw);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) st[u] = hgrn_step_x(f[u], sv0[u], sw[u]);
+        const float4 o4 = make_float4(st[0], st[1], st[2], st[3]);
+        *reinterpret_cast<float4*>(ob + c0) = o4;
+        *reinterpret_cast<float4*>(a.mix_state + rb + c0) = o4;
+        if (a.mix_out) *reinterpret_cast<float4*>(a.mix_out + rb + c0) = o4;
+      }
     }
     __syncthreads();
     const float r1 = s_rstd;
@@ -317,7 +353,7 @@ static void raise_smem_limit(const void* fn) {
 cudaError_t launch_prep(const PrepArgs& a, cudaStream_t s) {
   if (a.M <= 0) return cudaSuccess;
   int mode = kPrepPlain;
-  if (a.prew) mode = a.o ? kPrepSwishgate : kPrepNorm;
+  if (a.prew) mode = (a.o || a.mix_i) ? kPrepSwishgate : kPrepNorm;
   if (a.nproj < 0 || a.nproj > 3) return cudaErrorInvalidValue;
   int staged = 1;
   size_t smem = static_cast<size_t>(prep_smem_floats(a, mode, true)) * sizeof(float);
@@ -326,6 +362,13 @@ cudaError_t launch_prep(const PrepArgs& a, cudaStream_t s) {
     smem = static_cast<size_t>(prep_smem_floats(a, mode, false)) * sizeof(float);
   }
   if (smem > kMaxDynSmem) return cudaErrorInvalidValue;
+  if (a.mix_i) {  // fused token mixer: float4 lanes of staged rows
+    auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+    if (mode != kPrepSwishgate || !staged || a.o || a.K % 4 != 0 || a.K < 8 || a.mix_seg_rows < 1 ||
+        !a.mix_f || !a.mix_state || !al16(a.mix_i) || !al16(a.mix_f) || !al16(a.mix_state) ||
+        !al16(a.mix_lb) || !al16(a.mix_out))
+      return cudaErrorInvalidValue;
+  }
   if (smem > 48 * 1024) raise_smem_limit(reinterpret_cast<const void*>(prep_kernel));
   // few rows: latency-bound, 512 threads per row; many rows: throughput-bound, 128 threads
   // per row so that registers allow several row CTAs per SM

@@ -33,6 +33,15 @@ struct PrepArgs {
   bool fixed = true;
   bool pdl = false;              // launch as a programmatic dependent of the previous kernel
   uint32_t* err = nullptr;       // optional: bit kErrTimeout on a timed-out wait
+  // kPrepSwishgate of one decode step with the token mixer fused in: o is not read but
+  // computed here from the i / f projections and the recurrent state (which is updated), as
+  // launch_mixer does for len 1; needs K % 4 == 0, 16-byte aligned rows and K >= 8
+  const float* mix_i = nullptr;  // [M, K]
+  const float* mix_f = nullptr;  // [M, K]
+  float* mix_state = nullptr;    // [M, K] in / out
+  const float* mix_lb = nullptr; // [K] lower bound (nullable)
+  float* mix_out = nullptr;      // [M, K] recurrence output (nullable)
+  int mix_seg_rows = 1;          // rows of one reference vector call (SIMD tails)
 };
 
 struct MatmulArgs {

@@ -413,16 +413,29 @@ void Model::layers(int nseq, int len, int seg_rows, StateFn state) {
     p.normw[2] = ly.p[kG].normw;
     prep(p);
     bitlinear_ifg(ly, rows);
-    timed(kClsMixer, 4.0 * rows * H_ * 5 + 8.0 * nseq * H_, 0, [&] {
-      CK(launch_mixer(ib_, fb_, recur_, state(l), ly.lb, nseq, len, H_, seg_rows, stream_, pdl_));
-    });
+    // one decode step: the token mixer runs inside the o_proj prep (while its norm chain runs)
+    const bool mix_in_prep = len == 1 && H_ % 4 == 0 && H_ >= 8;
+    if (!mix_in_prep)
+      timed(kClsMixer, 4.0 * rows * H_ * 5 + 8.0 * nseq * H_, 0, [&] {
+        CK(launch_mixer(ib_, fb_, recur_, state(l), ly.lb, nseq, len, H_, seg_rows, stream_, pdl_));
+      });
     // o_proj on g_norm(g) * silu(recurrence); resid = h + o
     p.x = gb_;
-    p.o = recur_;
+    p.o = mix_in_prep ? nullptr : recur_;
     p.prew = ly.g_norm;
     p.nproj = 1;
     p.normw[0] = ly.p[kO].normw;
+    if (mix_in_prep) {
+      p.mix_i = ib_;
+      p.mix_f = fb_;
+      p.mix_state = state(l);
+      p.mix_lb = ly.lb;
+      p.mix_out = recur_;
+      p.mix_seg_rows = seg_rows;
+    }
     prep(p);
+    p.mix_i = p.mix_f = p.mix_lb = nullptr;
+    p.mix_state = p.mix_out = nullptr;
     bitlinear(ly.p[kO], 0, resid_, rows, h_);
     // mlp: gate_proj on rmsnorm(resid) * mlp_norm, swiglu, down_proj; h = resid + down
     p.x = resid_;
