@@ -323,20 +323,18 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepArgs a, int mode
       }
     }
   }
-  if (a.fixed) {
-    const int warp = tid >> 5, lane = tid & 31;
+  if (a.fixed) {  // row sums of the codes: warp reductions, then warp j sums projection j
+    const int warp = tid >> 5, lane = tid & 31, nwarps = static_cast<int>(blockDim.x) >> 5;
 #pragma unroll
     for (int j = 0; j < 3; ++j) {
-      int v = local[j];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (j >= a.nproj) break;
+      const int v = __reduce_add_sync(0xffffffffu, local[j]);
       if (lane == 0) s_red[j][warp] = v;
     }
     __syncthreads();
-    if (tid < a.nproj) {
-      int total = 0;
-      for (int w = 0; w < static_cast<int>(blockDim.x / 32); ++w) total += s_red[tid][w];
-      a.rowsum[tid][m] = total;
+    if (warp < a.nproj) {
+      const int total = __reduce_add_sync(0xffffffffu, lane < nwarps ? s_red[warp][lane] : 0);
+      if (lane == 0) a.rowsum[warp][m] = total;
     }
   }
 }
