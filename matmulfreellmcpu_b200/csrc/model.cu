@@ -59,6 +59,8 @@ Model::Model(const std::string& blob_path, int device, bool fixed, int frac_bits
     pdl_ = !(penv && penv[0] == '0');
     const char* cenv = std::getenv("MMFREE_PERSIST");
     persist_ok_ = cenv && cenv[0] == '1';
+    const char* menv = std::getenv("MMFREE_MIX_IN_PREP");
+    mix_prep_ok_ = !(menv && menv[0] == '0');
   }
   CK(cudaMalloc(&dec_part_v_, sizeof(float) * kDecMaxRows * 2 * 1024));
   CK(cudaMalloc(&dec_part_i_, sizeof(int) * kDecMaxRows * 2 * 1024));
@@ -414,7 +416,7 @@ void Model::layers(int nseq, int len, int seg_rows, StateFn state) {
     prep(p);
     bitlinear_ifg(ly, rows);
     // one decode step: the token mixer runs inside the o_proj prep (while its norm chain runs)
-    const bool mix_in_prep = len == 1 && H_ % 4 == 0 && H_ >= 8;
+    const bool mix_in_prep = mix_prep_ok_ && len == 1 && H_ % 4 == 0 && H_ >= 8;
     if (!mix_in_prep)
       timed(kClsMixer, 4.0 * rows * H_ * 5 + 8.0 * nseq * H_, 0, [&] {
         CK(launch_mixer(ib_, fb_, recur_, state(l), ly.lb, nseq, len, H_, seg_rows, stream_, pdl_));

@@ -123,6 +123,7 @@ class Model {
   bool fused_ok_ = true;           // MMFREE_FUSED_DECODE=0 selects the unfused decode step
   bool pdl_ = true;                // MMFREE_PDL=0: plain stream order between kernels
   bool persist_ok_ = false;        // MMFREE_PERSIST=1: the whole fused step in one launch
+  bool mix_prep_ok_ = true;        // MMFREE_MIX_IN_PREP=0: the decode mixer as its own kernel
   DecArgs* persist_tab_ = nullptr; // device copy of the persistent step's phase table
   int persist_n_ = 0, persist_grid_ = 0, persist_b_ = 0;
   int64_t persist_stride_ = -1;

@@ -145,6 +145,26 @@ def test_persistent_step_matches_per_launch_step(cuda, monkeypatch, blob_cache, 
             assert np.array_equal(b, c)
 
 
+def test_mixer_in_prep_matches_mixer_kernel(cuda, monkeypatch, blob_cache, orc):
+    """A decode step runs the token mixer inside the o_proj prep; MMFREE_MIX_IN_PREP=0 runs
+    it as its own kernel (mixer_decode_kernel). Both give the oracle's ids, through the
+    tensor-core path (20 streams) and the per-op few-row path (3 streams, unfused)."""
+    path = B.cached_blob("small", 0, blob_cache)
+    om = orc.model(B.Blob.open(path))
+    prompts = [B.seeded_ids(5, 700 + k, 2048) for k in range(20)]
+    monkeypatch.setenv("MMFREE_FUSED_DECODE", "0")
+    out = {}
+    for flag in ("0", "1"):
+        monkeypatch.setenv("MMFREE_MIX_IN_PREP", flag)
+        with api.Model(path, "fixed") as m:
+            out[flag] = (m.generate_serve(prompts, 6), m.generate_serve(prompts[:3], 6))
+    for k, ps in ((0, prompts), (1, prompts[:3])):
+        ref = om.generate_serve(ps, 6)
+        for a, b, c in zip(out["0"][k], out["1"][k], ref):
+            assert np.array_equal(a, b)
+            assert np.array_equal(b, c)
+
+
 def test_serve_many_streams_matches_oracle(models, orc, blob_cache):
     """20 lockstep streams: decode rows go through the tensor-core matmul (ragged tile)."""
     m = models("small", "fixed")
