@@ -45,6 +45,9 @@ CONFIGS = {
     "tiny": dict(vocab_size=512, hidden_size=64, num_hidden_layers=2, intermediate_size=96),
     "small": dict(vocab_size=2048, hidden_size=256, num_hidden_layers=4, intermediate_size=704),
     "ragged": dict(vocab_size=300, hidden_size=36, num_hidden_layers=2, intermediate_size=52),
+    # the 1.3B intermediate size on a narrow, one-layer model: at 64 decode rows its gate_proj
+    # (SwiGLU pair epilogue), i/f/g, o and down run split-K over 2- and 8-CTA clusters
+    "wide": dict(vocab_size=512, hidden_size=768, num_hidden_layers=1, intermediate_size=5632),
 }
 
 

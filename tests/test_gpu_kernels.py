@@ -118,10 +118,11 @@ def test_bitlinear_many_rows_all_match(cuda, orc):
     assert bits_equal(out, r_out)
 
 
-@pytest.mark.parametrize("M,K,N", [(64, 2048, 101), (40, 2048, 200), (20, 1000, 66), (64, 5632, 256)])
+@pytest.mark.parametrize("M,K,N", [(64, 2048, 101), (40, 2048, 200), (20, 1000, 66), (64, 5632, 256),
+                                   (64, 2048, 6144), (64, 2048, 11264), (48, 1536, 5632)])
 def test_bitlinear_split_k_tile_edges(cuda, orc, M, K, N):
     """Few output tiles, so the reduction is split over a cluster: partial row quads
-    (N % 4 != 0, no 16-byte stores), tokens past M in a tile, every split count."""
+    (N % 4 != 0, no 16-byte stores), tokens past M in a tile, cluster sizes 8, 4 and 2."""
     x, nw, wq = sweep_inputs(M, K, N, seed=M + K + N)
     out, acc, _ = run_gpu(cuda, x, nw, wq, 20.0, "fixed")
     r_out, r_acc, _ = orc.bitlinear(x, nw, wq, 20.0, act_quant=1)

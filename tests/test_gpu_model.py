@@ -165,6 +165,19 @@ def test_mixer_in_prep_matches_mixer_kernel(cuda, monkeypatch, blob_cache, orc):
             assert np.array_equal(b, c)
 
 
+def test_wide_serve_64_streams_matches_oracle(cuda, orc, blob_cache):
+    """64 lockstep streams of the "wide" model (H 768, I 5632): the tensor-core BitLinears
+    with their cluster split-K reductions (the SwiGLU pair epilogue of gate_proj included)
+    against the oracle, bit for bit."""
+    path = B.cached_blob("wide", 0, blob_cache)
+    om = orc.model(B.Blob.open(path))
+    prompts = [B.seeded_ids(3 + k % 3, 800 + k, 512) for k in range(64)]
+    with api.Model(path, "fixed") as m:
+        got = m.generate_serve(prompts, 3)
+    for a, c in zip(got, om.generate_serve(prompts, 3)):
+        assert np.array_equal(a, c)
+
+
 def test_serve_many_streams_matches_oracle(models, orc, blob_cache):
     """20 lockstep streams: decode rows go through the tensor-core matmul (ragged tile)."""
     m = models("small", "fixed")
