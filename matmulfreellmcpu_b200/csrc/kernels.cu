@@ -8,7 +8,8 @@
 //           fp32 FMA (float), dequant and optional residual add in the epilogue.
 //           Restates ternary_backend.hpp:96-103 + simd.hpp:191-206 (+ hgrn_model.cpp:161-166,
 //           :189-194 for the residual).
-// mixer    the HGRN token mixer (hgrn_model.cpp:109-150): gate + scan in one pass.
+// mixer    the HGRN token mixer (hgrn_model.cpp:109-150): gate + scan in one pass (a decode
+//           step runs it inside the o_proj prep instead, unless MMFREE_MIX_IN_PREP=0).
 // others    swiglu split (hgrn_model.cpp:171-185), embedding gather, greedy argmax.
 #include "common.cuh"
 #include "exact.cuh"
@@ -565,10 +566,9 @@ cudaError_t launch_matmul(const MatmulArgs& a, cudaStream_t s) {
 }
 
 // ------------------------------------------------------------------------------ mixer
-// In place: f <- lower-bounded sigmoid(f); i <- silu(i) * (1 - f). The SIMD body/tail split
-// of element e is taken within its segment of seg elements (one reference block() call).
-// state = fma(f, state, s) along t for each of nseq x H lanes; x layout [nseq][T][H],
-// state [nseq][H] (nullable: zero start, not written back).
+// The scan alone (the C-ABI hgrn_scan, hgrn_scan.cpp:11-19): state = fma(f, state, s) along
+// t for each of nseq x H lanes; x layout [nseq][T][H], state [nseq][H] (nullable: zero
+// start, not written back).
 __global__ void scan_kernel(float* __restrict__ out, const float* __restrict__ s,
                             const float* __restrict__ f, float* __restrict__ state, int nseq,
                             int T, int H) {
