@@ -5,7 +5,8 @@
 // CpuBackend (ternary_backend.hpp:96-103), so every output is bit-identical.
 //
 // Per CTA: a tile of 128 weight rows (4 packed 32-row groups) x BN tokens, K in blocks of
-// 128, split-K over blockIdx.z. Warp-specialised, every hand-off through an mbarrier ring:
+// 128, split-K over blockIdx.z (the S CTAs of a tile form one thread-block cluster).
+// Warp-specialised, every hand-off through an mbarrier ring:
 //   warp 4  weight producer    one bulk async copy per group and k-block (the packed format
 //                              keeps a group's chunks contiguous) into an 8-stage ring; the
 //                              weights depend on no earlier kernel, so this runs ahead of
@@ -24,9 +25,12 @@
 //                              D[:, BN:2BN] += u x (lo - 128) (u8 x s8, M=128, N=2*BN),
 //                              int32 accumulators in TMEM; tcgen05.commit releases the rings
 //   epilogue (warps 0-3)       tcgen05.ld of D; acc = 256*D_hi + D_lo' + 128*sum_k u - sum_k q
-//                              (exact modulo 2^32, hence in int32); split-K partials are
-//                              combined with integer atomics (exact, order free) and the last
-//                              CTA of a tile applies dequant (+ residual, or the SwiGLU pair).
+//                              (exact modulo 2^32, hence in int32); with split-K each CTA
+//                              leaves its partial tile in shared memory, and after a cluster
+//                              barrier CTA r sums its BN/S tokens from every peer over
+//                              distributed shared memory (integer sums: exact, order free) and
+//                              applies dequant (+ residual, or the SwiGLU pair); a second
+//                              barrier keeps the partials alive until every peer has read them.
 // Every wait on an mbarrier is bounded; on timeout the CTA sets an error flag, the other roles
 // stop, producers wait (bounded) for their copies in flight, the MMA issuer's final commit
 // covers its MMAs, and the tensor memory is freed.
