@@ -817,9 +817,23 @@ __device__ int block_argmax(const float* __restrict__ l, int V) {
   if (isnan(first)) return 0;
   float bv = first;
   int bi = 0;
-  for (int v = threadIdx.x; v < V; v += blockDim.x) {
-    const float x = l[v];
-    if (x > bv) { bv = x; bi = v; }
+  // each thread visits v = tid, tid + blockDim, ... in increasing order; the loads of 8 such
+  // elements are issued before their compares (one memory latency per 8, not per element);
+  // a padding NaN never wins
+  constexpr int kArgBatch = 8;
+  for (int v0 = threadIdx.x; v0 < V; v0 += kArgBatch * blockDim.x) {
+    float x[kArgBatch];
+#pragma unroll
+    for (int u = 0; u < kArgBatch; ++u) {
+      const int v = v0 + u * static_cast<int>(blockDim.x);
+      x[u] = v < V ? l[v] : __int_as_float(0x7fc00000);
+    }
+#pragma unroll
+    for (int u = 0; u < kArgBatch; ++u)
+      if (x[u] > bv) {
+        bv = x[u];
+        bi = v0 + u * static_cast<int>(blockDim.x);
+      }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
