@@ -907,7 +907,21 @@ __global__ void embed_at_kernel(float* __restrict__ h, const float* __restrict__
   if (!ok && threadIdx.x == 0 && err) atomicOr(err, kErrBadToken);
   const float* src = emb + (ok ? id : 0) * static_cast<int64_t>(H);
   float* dst = h + static_cast<int64_t>(b) * H;
-  for (int c = threadIdx.x; c < H; c += blockDim.x) dst[c] = ok ? __ldg(src + c) : 0.0f;
+  // 8 loads per thread issued before their stores (one memory latency per 8 elements)
+  constexpr int kEmbBatch = 8;
+  for (int c0 = threadIdx.x; c0 < H; c0 += kEmbBatch * blockDim.x) {
+    float v[kEmbBatch];
+#pragma unroll
+    for (int u = 0; u < kEmbBatch; ++u) {
+      const int c = c0 + u * static_cast<int>(blockDim.x);
+      v[u] = (ok && c < H) ? __ldg(src + c) : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < kEmbBatch; ++u) {
+      const int c = c0 + u * static_cast<int>(blockDim.x);
+      if (c < H) dst[c] = v[u];
+    }
+  }
 }
 
 cudaError_t launch_embed_at(float* h, const float* emb, const int64_t* ids, int64_t stride,
