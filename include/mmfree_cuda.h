@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define MMFREE_CUDA_ABI_VERSION 1
+#define MMFREE_CUDA_ABI_VERSION 2
 
 enum {
   MMFREE_OK = 0,
@@ -37,7 +37,8 @@ enum {
   MMFREE_E_IO = -3,      /* blob file missing, unreadable or malformed */
   MMFREE_E_RANGE = -4,   /* token id outside [0, vocab_size) or code outside int16 */
   MMFREE_E_STATE = -5,   /* call out of order (e.g. serve_step without serve_begin) */
-  MMFREE_E_INTERNAL = -6
+  MMFREE_E_INTERNAL = -6,
+  MMFREE_E_TIMEOUT = -7  /* a bounded wait inside a kernel gave up (its outputs are undefined) */
 };
 
 enum { MMFREE_ACT_FLOAT = 0, MMFREE_ACT_FIXED_Q510 = 1 };
@@ -71,7 +72,25 @@ int mmfree_cuda_bitlinear(float* out, const float* x, const float* norm_weight,
                           size_t out_dim, float eps, float* norm_out, int act_quant,
                           int frac_bits, int32_t* acc_out, void* stream);
 
-/* Size of the static device scratch used by mmfree_cuda_bitlinear_noalloc (4 MiB). */
+/* Status of the asynchronous kernel entry points (mmfree_cuda_bitlinear,
+ * mmfree_cuda_bitlinear_cluster, mmfree_cuda_bitlinear_noalloc). They return once their
+ * kernels are queued; a failure inside a kernel (a bounded wait that gave up) is recorded in
+ * a device error word instead. This call synchronizes `stream` (the stream those calls used),
+ * reads and clears the calling device's words and returns MMFREE_OK, or MMFREE_E_TIMEOUT when
+ * a call since the last check failed -- the outputs of those calls are then undefined. It
+ * allocates nothing. No reference counterpart: the reference kernels are synchronous host
+ * code that cannot time out. */
+int mmfree_cuda_kernel_status(void* stream);
+
+/* Diagnostic switch: the number of polls after which the BitLinear prologue's wait for its
+ * staged input row gives up (raising the error mmfree_cuda_kernel_status reports) in kernels
+ * launched from now on, by this process; a negative value restores the default (2^22).
+ * 0 makes every staged wait give up at once: a way to test a caller's error handling without
+ * faulting the GPU. Model handles capture the value in force when they build a decode graph. */
+void mmfree_cuda_set_wait_limit(int64_t polls);
+
+/* Size of the static device scratch used by mmfree_cuda_bitlinear_noalloc (4 MiB, of which
+ * the first 256 bytes hold the calls' error word). */
 #define MMFREE_CUDA_NOALLOC_SCRATCH_BYTES (4u << 20)
 
 /* mmfree_cuda_bitlinear for callers that cannot allocate device memory. It has no
@@ -87,15 +106,19 @@ int mmfree_cuda_bitlinear(float* out, const float* x, const float* norm_weight,
  * a fixed array compiled into the library (one per device that loads it, held until the
  * process exits) and calls no allocating routine on its success path.
  *
- * Same arguments, semantics and results as mmfree_cuda_bitlinear. Limits and rules:
- *   - scratch need: FixedQ510 2*rows*ceil64(in_dim) + 4*rows bytes, Float
- *     4*rows*ceil64(in_dim) bytes (each rounded up to 256); a call needing more than
- *     MMFREE_CUDA_NOALLOC_SCRATCH_BYTES fails with MMFREE_E_INVALID and allocates nothing;
+ * Same arguments, semantics, kernels and results as mmfree_cuda_bitlinear. Limits and rules:
+ *   - scratch need: 256 bytes of error word, plus FixedQ510 2*rows*ceil64(in_dim) + 4*rows
+ *     bytes or Float 4*rows*ceil64(in_dim) bytes (each rounded up to 256); a call needing
+ *     more than MMFREE_CUDA_NOALLOC_SCRATCH_BYTES fails with MMFREE_E_INVALID and allocates
+ *     nothing;
  *   - the first call on a device looks up that device's copy of the array
- *     (cudaGetSymbolAddress, which can load the module): make it before any stream capture;
+ *     (cudaGetSymbolAddress, which can load the module) and zeroes its error word: make it
+ *     before any stream capture (a failed lookup is retried by the next call);
  *   - every call on a device shares the one array, which keeps the last call's contents;
- *     nothing in it has to start at zero (each call writes all it reads), but calls whose
- *     kernels overlap on the GPU (different streams, or different host threads) race on it.
+ *     the planes need not start at zero (each call writes all it reads), but calls whose
+ *     kernels overlap on the GPU (different streams, or different host threads) race on it;
+ *   - a kernel that gives up a bounded wait sets the array's error word and leaves the
+ *     call's outputs undefined; mmfree_cuda_kernel_status reports and clears it.
  */
 int mmfree_cuda_bitlinear_noalloc(float* out, const float* x, const float* norm_weight,
                                   const void* wpacked, float scale_w, size_t rows,
@@ -116,6 +139,21 @@ int mmfree_cuda_bitlinear_cluster(float* const* outs, const float* x,
  * sum_n x[i*N + n] * wq[m, n] for b rows of int32 activations in int16 range. */
 int mmfree_cuda_ternary_matmul(int32_t* acc, const int32_t* x, const void* wpacked, size_t N,
                                size_t M, size_t b, void* stream);
+
+/* The TernaryBackend seam on HOST buffers (ternary_backend.hpp:26-59), for callers that keep
+ * the reference's own Model and offload only the integer accumulate, as an accelerator
+ * backend does (include/mmfree_cuda_backend.hpp wraps it as a mmfree::TernaryBackend).
+ * seam_matmul: acc[i*M + m] = sum_n x[i*N + n] * wq[m*N + n] for b rows (the arguments of
+ * TernaryBackend::matmul_batch, ternary_backend.hpp:43-48); returns when acc is written.
+ * wq is uploaded and repacked on the GPU the first time its (pointer, M, N) is seen and kept
+ * until seam_close: the weights behind a pointer must not change meanwhile (the reference's
+ * are an immutable mmap, weights.cpp:191-254). Codes outside int16 give MMFREE_E_RANGE.
+ * A seam is used by one host thread at a time. */
+typedef struct mmfree_cuda_seam mmfree_cuda_seam;
+int mmfree_cuda_seam_open(int device, mmfree_cuda_seam** out);
+int mmfree_cuda_seam_matmul(mmfree_cuda_seam* s, const int8_t* wq, size_t N, size_t M,
+                            const int32_t* x, int32_t* acc, size_t b);
+void mmfree_cuda_seam_close(mmfree_cuda_seam* s);
 
 /* Replaces mmfree::rmsnorm (kernels.hpp:29-30, rmsnorm.cpp:11-22). */
 int mmfree_cuda_rmsnorm(float* y, const float* x, const float* weight, size_t rows,

@@ -13,7 +13,7 @@ from . import build as _build
 LIB_PATH = _build.LIB
 
 OK = 0
-E_INVALID, E_CUDA, E_IO, E_RANGE, E_STATE, E_INTERNAL = -1, -2, -3, -4, -5, -6
+E_INVALID, E_CUDA, E_IO, E_RANGE, E_STATE, E_INTERNAL, E_TIMEOUT = -1, -2, -3, -4, -5, -6, -7
 ACT_FLOAT, ACT_FIXED_Q510 = 0, 1
 MAX_IN_DIM = 57344
 
@@ -28,8 +28,13 @@ SIGNATURES = {
     "mmfree_cuda_pack_ternary_host": (I, [VP, VP, SZ, SZ]),
     "mmfree_cuda_bitlinear": (I, [VP, VP, VP, VP, F, SZ, SZ, SZ, F, VP, I, I, VP, VP]),
     "mmfree_cuda_bitlinear_noalloc": (I, [VP, VP, VP, VP, F, SZ, SZ, SZ, F, VP, I, I, VP, VP]),
+    "mmfree_cuda_kernel_status": (I, [VP]),
+    "mmfree_cuda_set_wait_limit": (None, [I64]),
     "mmfree_cuda_bitlinear_cluster": (I, [VP, VP, VP, VP, VP, I, SZ, SZ, SZ, F, I, VP, VP]),
     "mmfree_cuda_ternary_matmul": (I, [VP, VP, VP, SZ, SZ, SZ, VP]),
+    "mmfree_cuda_seam_open": (I, [I, C.POINTER(VP)]),
+    "mmfree_cuda_seam_matmul": (I, [VP, VP, SZ, SZ, VP, VP, SZ]),
+    "mmfree_cuda_seam_close": (None, [VP]),
     "mmfree_cuda_rmsnorm": (I, [VP, VP, VP, SZ, SZ, F, VP]),
     "mmfree_cuda_swiglu": (I, [VP, VP, VP, SZ, VP]),
     "mmfree_cuda_hgrn_scan": (I, [VP, VP, VP, SZ, SZ, VP, VP]),

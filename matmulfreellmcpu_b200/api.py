@@ -241,6 +241,19 @@ def bitlinear(x, norm_weight, wpacked, scale_w: float, out_dim: int, eps: float 
     return out, acc, norm
 
 
+def kernel_status(stream=None) -> None:
+    """Synchronizes ``stream`` and raises MmfreeError (code E_TIMEOUT) when a kernel of an
+    asynchronous entry point (bitlinear, bitlinear_cluster, bitlinear_noalloc) gave up a
+    bounded wait since the last check; the recorded error is cleared."""
+    check(lib().mmfree_cuda_kernel_status(_stream(stream)))
+
+
+def set_wait_limit(polls: int) -> None:
+    """Diagnostic: polls of the BitLinear prologue's row wait before it gives up (negative =
+    default); 0 makes the staged waits give up at once."""
+    lib().mmfree_cuda_set_wait_limit(int(polls))
+
+
 def bitlinear_cluster(x, norm_weights, wpacked, scale_w, out_dim: int, eps: float = 1e-6,
                       frac_bits: int = 10, want_acc: bool = False, stream=None):
     import torch

@@ -2,10 +2,12 @@
 #include <cuda_runtime.h>
 
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <new>
 #include <stdexcept>
 #include <string>
+#include <tuple>
 #include <vector>
 
 #include "../../include/mmfree_cuda.h"
@@ -25,6 +27,9 @@ namespace {
 thread_local std::string g_last_error;
 
 struct CudaError : std::runtime_error {
+  using std::runtime_error::runtime_error;
+};
+struct TimeoutError : std::runtime_error {
   using std::runtime_error::runtime_error;
 };
 
@@ -50,6 +55,9 @@ int guard(F&& f) {
   } catch (const CudaError& e) {
     g_last_error = e.what();
     return MMFREE_E_CUDA;
+  } catch (const TimeoutError& e) {
+    g_last_error = e.what();
+    return MMFREE_E_TIMEOUT;
   } catch (const std::bad_alloc&) {
     g_last_error = "host out of memory";
     return MMFREE_E_INTERNAL;
@@ -69,14 +77,18 @@ void need(bool ok, const char* what) {
 
 cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 
-// Library-owned scratch of the kernel entry points: one grow-only arena per device, plus a
-// device word of error flags at its start.
+// Library-owned scratch of the kernel entry points: one grow-only arena per device. Its first
+// 256 bytes hold two words of device error flags: word 0 for the synchronous entry points
+// (repack, ternary_matmul: checked and cleared before they return), word 1 for the
+// asynchronous ones (bitlinear, bitlinear_cluster: read and cleared by
+// mmfree_cuda_kernel_status).
 struct Scratch {
   void* base = nullptr;
   size_t bytes = 0;
 };
 std::mutex g_scratch_mu;
 Scratch g_scratch[64];
+constexpr size_t kAsyncFlagWord = 1;  // index of the asynchronous entry points' word
 
 char* scratch(size_t bytes) {
   int dev = 0;
@@ -85,29 +97,43 @@ char* scratch(size_t bytes) {
   Scratch& s = g_scratch[dev & 63];
   bytes += 256;
   if (bytes > s.bytes) {
-    if (s.base) ck(cudaFree(s.base), "cudaFree");  // synchronizes with work still using it
+    uint32_t words[2] = {0, 0};  // flags not yet reported survive the move to a larger arena
+    if (s.base) {
+      ck(cudaMemcpy(words, s.base, sizeof(words), cudaMemcpyDeviceToHost), "cudaMemcpy(flags)");
+      ck(cudaFree(s.base), "cudaFree");  // synchronizes with work still using it
+    }
     s.base = nullptr;
     s.bytes = 0;
     const size_t grow = bytes < (size_t(1) << 20) ? (size_t(1) << 20) : bytes;
     ck(cudaMalloc(&s.base, grow), "cudaMalloc(scratch)");
     ck(cudaMemset(s.base, 0, 256), "cudaMemset(scratch)");
+    ck(cudaMemcpy(s.base, words, sizeof(words), cudaMemcpyHostToDevice), "cudaMemcpy(flags)");
     ck(cudaDeviceSynchronize(), "cudaDeviceSynchronize");  // order before any caller stream
     s.bytes = grow;
   }
   return static_cast<char*>(s.base);
 }
 
+// Reads and clears one device flag word on `st` (synchronizing it); returns the flags.
+uint32_t take_flags(uint32_t* word, cudaStream_t st) {
+  uint32_t f = 0;
+  ck(cudaMemcpyAsync(&f, word, 4, cudaMemcpyDeviceToHost, st), "cudaMemcpyAsync(flags)");
+  ck(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+  if (f) {
+    ck(cudaMemsetAsync(word, 0, 4, st), "cudaMemsetAsync(flags)");
+    ck(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+  }
+  return f;
+}
+
 size_t a256(size_t n) { return (n + 255) / 256 * 256; }
 
 void check_flags(uint32_t* flags, cudaStream_t st) {
-  uint32_t f = 0;
-  ck(cudaMemcpyAsync(&f, flags, 4, cudaMemcpyDeviceToHost, st), "cudaMemcpyAsync(flags)");
-  ck(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+  const uint32_t f = take_flags(flags, st);
   if (f) {
-    ck(cudaMemsetAsync(flags, 0, 4, st), "cudaMemsetAsync(flags)");
-    ck(cudaStreamSynchronize(st), "cudaStreamSynchronize");
     if (f & kErrRange) throw std::out_of_range("activation code outside int16");
     if (f & kErrNotTernary) throw std::out_of_range("weight outside {-1,0,+1}");
+    if (f & kErrTimeout) throw TimeoutError("a bounded wait inside a kernel gave up");
     throw std::runtime_error("device error flag set");
   }
 }
@@ -142,7 +168,8 @@ void run_bitlinear(int k, float* const* outs, const float* x, const float* const
   p.fixed = fixed;
   // the tensor-core matmul (taken for >= kTcMinRows fixed rows) reads the low plane as lo - 128
   p.lo_signed = fixed && static_cast<int>(rows) >= kTcMinRows;
-  p.err = reinterpret_cast<uint32_t*>(base);
+  uint32_t* err = reinterpret_cast<uint32_t*>(base) + kAsyncFlagWord;
+  p.err = err;
   for (int j = 0; j < k; ++j) {
     char* b = base + 256 + j * per;
     p.normw[j] = nws[j];
@@ -170,9 +197,42 @@ void run_bitlinear(int k, float* const* outs, const float* x, const float* const
     a.fixed = fixed;
     a.allow_tc = true;
     a.lo_signed = p.lo_signed;
-    a.err = reinterpret_cast<uint32_t*>(base);
+    a.err = err;
     ck(launch_matmul(a, st), "matmul kernel");
   }
+}
+
+}  // namespace
+
+// ---- allocation-free BitLinear scratch ------------------------------------------------------
+// Compiled into the library: each device that loads this module holds one copy until the
+// process exits. Bytes [0, 256) hold the calls' device error word; the activation planes
+// follow. Host code must not use the symbol as an address (it names a host-side stand-in);
+// the device address comes from cudaGetSymbolAddress, looked up per device with that device
+// current and kept only once the lookup succeeded.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[MMFREE_CUDA_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr size_t kNoallocHeader = 256;
+std::mutex g_noalloc_mu;
+char* g_noalloc_addr[64];
+
+char* noalloc_base(int dev) {
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    char* p = nullptr;
+    ck(cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_noalloc_scratch),
+       "cudaGetSymbolAddress(noalloc scratch)");
+    ck(cudaMemset(p, 0, kNoallocHeader), "cudaMemset(noalloc error word)");
+    ck(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+    g_noalloc_addr[dev] = p;
+  }
+  return g_noalloc_addr[dev];
+}
+
+char* noalloc_base_if_ready(int dev) {
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  return g_noalloc_addr[dev];
 }
 
 }  // namespace
@@ -240,18 +300,6 @@ int mmfree_cuda_bitlinear(float* out, const float* x, const float* norm_weight,
 }
 
 // ---- allocation-free BitLinear -------------------------------------------------------------
-// Scratch compiled into the library: each device that loads this module holds one copy until
-// the process exits. Host code must not use the symbol as an address (it names a host-side
-// stand-in); the device address comes from cudaGetSymbolAddress, looked up once per device
-// with that device current.
-static __device__ __align__(256) unsigned char g_noalloc_scratch[MMFREE_CUDA_NOALLOC_SCRATCH_BYTES];
-
-namespace {
-std::once_flag g_noalloc_once[64];
-cudaError_t g_noalloc_status[64];
-char* g_noalloc_addr[64];
-}  // namespace
-
 int mmfree_cuda_bitlinear_noalloc(float* out, const float* x, const float* norm_weight,
                                   const void* wpacked, float scale_w, size_t rows,
                                   size_t in_dim, size_t out_dim, float eps, float* norm_out,
@@ -265,19 +313,16 @@ int mmfree_cuda_bitlinear_noalloc(float* out, const float* x, const float* norm_
     const bool fixed = act_quant == MMFREE_ACT_FIXED_Q510;
     const size_t kp = static_cast<size_t>(padded_k(static_cast<int64_t>(in_dim)));
     const size_t planes_bytes = fixed ? a256(2 * rows * kp) : a256(rows * kp * 4);
-    const size_t need_bytes = planes_bytes + (fixed ? a256(rows * 4) : 0);
+    const size_t need_bytes = kNoallocHeader + planes_bytes + (fixed ? a256(rows * 4) : 0);
     need(need_bytes <= MMFREE_CUDA_NOALLOC_SCRATCH_BYTES,
          "bitlinear_noalloc: rows x in_dim needs more scratch than "
          "MMFREE_CUDA_NOALLOC_SCRATCH_BYTES (use mmfree_cuda_bitlinear or fewer rows per call)");
     int dev = 0;
     ck(cudaGetDevice(&dev), "cudaGetDevice");
     need(dev >= 0 && dev < 64, "device index above 63");
-    std::call_once(g_noalloc_once[dev], [dev] {
-      g_noalloc_status[dev] =
-          cudaGetSymbolAddress(reinterpret_cast<void**>(&g_noalloc_addr[dev]), g_noalloc_scratch);
-    });
-    ck(g_noalloc_status[dev], "cudaGetSymbolAddress(noalloc scratch)");
-    char* base = g_noalloc_addr[dev];
+    char* const head = noalloc_base(dev);
+    auto* err = reinterpret_cast<uint32_t*>(head);
+    char* const base = head + kNoallocHeader;
     cudaStream_t st = as_stream(stream);
     PrepArgs p;
     p.x = x;
@@ -289,6 +334,9 @@ int mmfree_cuda_bitlinear_noalloc(float* out, const float* x, const float* norm_
     p.eps = eps;
     p.qs = static_cast<float>(1u << frac_bits);
     p.fixed = fixed;
+    // the same kernels as mmfree_cuda_bitlinear: tensor cores from kTcMinRows fixed rows
+    p.lo_signed = fixed && static_cast<int>(rows) >= kTcMinRows;
+    p.err = err;
     if (fixed) {
       p.planes[0] = reinterpret_cast<int8_t*>(base);
       p.rowsum[0] = reinterpret_cast<int32_t*>(base + planes_bytes);
@@ -309,9 +357,35 @@ int mmfree_cuda_bitlinear_noalloc(float* out, const float* x, const float* norm_
     a.ldo = static_cast<int>(out_dim);
     a.acc_out = fixed ? acc_out : nullptr;
     a.fixed = fixed;
+    a.allow_tc = true;
+    a.lo_signed = p.lo_signed;
+    a.err = err;
     ck(launch_matmul(a, st), "matmul kernel");
   });
 }
+
+int mmfree_cuda_kernel_status(void* stream) {
+  return guard([&] {
+    int dev = 0;
+    ck(cudaGetDevice(&dev), "cudaGetDevice");
+    need(dev >= 0 && dev < 64, "device index above 63");
+    cudaStream_t st = as_stream(stream);
+    uint32_t f = 0;
+    char* arena = nullptr;
+    {
+      std::lock_guard<std::mutex> lock(g_scratch_mu);
+      arena = static_cast<char*>(g_scratch[dev].base);
+    }
+    if (arena) f |= take_flags(reinterpret_cast<uint32_t*>(arena) + kAsyncFlagWord, st);
+    if (char* head = noalloc_base_if_ready(dev)) f |= take_flags(reinterpret_cast<uint32_t*>(head), st);
+    if (f & kErrTimeout)
+      throw TimeoutError("a bounded wait inside a BitLinear kernel gave up: the outputs of the "
+                         "kernel calls since the last status check are undefined");
+    if (f) throw std::runtime_error("device error flag set");
+  });
+}
+
+void mmfree_cuda_set_wait_limit(int64_t polls) { set_wait_limit(polls); }
 
 int mmfree_cuda_bitlinear_cluster(float* const* outs, const float* x,
                                   const float* const* norm_weights,
@@ -352,6 +426,109 @@ int mmfree_cuda_ternary_matmul(int32_t* acc, const int32_t* x, const void* wpack
     a.fixed = true;
     ck(launch_matmul(a, st), "matmul kernel");
     check_flags(flags, st);
+  });
+}
+
+// ---- TernaryBackend seam over host buffers ------------------------------------------------
+struct mmfree_cuda_seam {
+  int device = 0;
+  cudaStream_t st = nullptr;
+  // packed weights per (host wq pointer, out_dim, in_dim), uploaded on first sight
+  std::map<std::tuple<const int8_t*, size_t, size_t>, void*> packed;
+  char* dev = nullptr;  // flags (256 B), x codes, planes, row sums, accumulators
+  size_t dev_bytes = 0;
+  int8_t* stage = nullptr;  // int8 upload buffer of the repack
+  size_t stage_bytes = 0;
+};
+
+int mmfree_cuda_seam_open(int device, mmfree_cuda_seam** out) {
+  return guard([&] {
+    need(out != nullptr, "null pointer");
+    *out = nullptr;
+    int n = 0;
+    ck(cudaGetDeviceCount(&n), "cudaGetDeviceCount");
+    need(device >= 0 && device < n, "no such CUDA device");
+    ck(cudaSetDevice(device), "cudaSetDevice");
+    auto* s = new mmfree_cuda_seam;
+    s->device = device;
+    if (cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking) != cudaSuccess) {
+      delete s;
+      throw CudaError("cudaStreamCreate failed");
+    }
+    *out = s;
+  });
+}
+
+void mmfree_cuda_seam_close(mmfree_cuda_seam* s) {
+  if (!s) return;
+  cudaSetDevice(s->device);
+  cudaStreamSynchronize(s->st);
+  for (auto& kv : s->packed) cudaFree(kv.second);
+  cudaFree(s->dev);
+  cudaFree(s->stage);
+  cudaStreamDestroy(s->st);
+  delete s;
+}
+
+int mmfree_cuda_seam_matmul(mmfree_cuda_seam* s, const int8_t* wq, size_t N, size_t M,
+                            const int32_t* x, int32_t* acc, size_t b) {
+  return guard([&] {
+    need(s && wq && x && acc, "null pointer");
+    check_dims(b, N, M);
+    if (b == 0) return;
+    ck(cudaSetDevice(s->device), "cudaSetDevice");
+    cudaStream_t st = s->st;
+    const size_t kp = static_cast<size_t>(padded_k(static_cast<int64_t>(N)));
+    const size_t o_x = 256, o_pl = o_x + a256(4 * b * N), o_rs = o_pl + a256(2 * b * kp),
+                 o_acc = o_rs + a256(4 * b), total = o_acc + a256(4 * b * M);
+    if (total > s->dev_bytes) {
+      ck(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+      cudaFree(s->dev);
+      s->dev = nullptr;
+      s->dev_bytes = 0;
+      ck(cudaMalloc(&s->dev, total), "cudaMalloc(seam)");
+      ck(cudaMemsetAsync(s->dev, 0, 256, st), "cudaMemsetAsync(seam flags)");
+      s->dev_bytes = total;
+    }
+    auto* flags = reinterpret_cast<uint32_t*>(s->dev);
+    const auto key = std::make_tuple(wq, M, N);
+    auto it = s->packed.find(key);
+    if (it == s->packed.end()) {
+      if (M * N > s->stage_bytes) {
+        ck(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+        cudaFree(s->stage);
+        s->stage = nullptr;
+        s->stage_bytes = 0;
+        ck(cudaMalloc(&s->stage, M * N), "cudaMalloc(seam staging)");
+        s->stage_bytes = M * N;
+      }
+      void* p = nullptr;
+      ck(cudaMalloc(&p, static_cast<size_t>(packed_bytes(M, N))), "cudaMalloc(seam weights)");
+      ck(cudaMemcpyAsync(s->stage, wq, M * N, cudaMemcpyHostToDevice, st), "cudaMemcpyAsync(wq)");
+      ck(launch_repack(p, s->stage, static_cast<int64_t>(M), static_cast<int64_t>(N), flags, st),
+         "repack kernel");
+      it = s->packed.emplace(key, p).first;
+    }
+    auto* dx = reinterpret_cast<int32_t*>(s->dev + o_x);
+    auto* planes = reinterpret_cast<int8_t*>(s->dev + o_pl);
+    auto* rowsum = reinterpret_cast<int32_t*>(s->dev + o_rs);
+    auto* dacc = reinterpret_cast<int32_t*>(s->dev + o_acc);
+    ck(cudaMemcpyAsync(dx, x, 4 * b * N, cudaMemcpyHostToDevice, st), "cudaMemcpyAsync(x)");
+    ck(launch_codes_to_planes(planes, rowsum, dx, static_cast<int>(b), static_cast<int>(N), flags,
+                              st),
+       "codes kernel");
+    MatmulArgs a;
+    a.w = it->second;
+    a.planes = planes;
+    a.rowsum = rowsum;
+    a.M = static_cast<int>(b);
+    a.N = static_cast<int>(M);
+    a.K = static_cast<int>(N);
+    a.acc_out = dacc;
+    a.fixed = true;
+    ck(launch_matmul(a, st), "matmul kernel");
+    ck(cudaMemcpyAsync(acc, dacc, 4 * b * M, cudaMemcpyDeviceToHost, st), "cudaMemcpyAsync(acc)");
+    check_flags(flags, st);  // synchronizes: acc is final on return
   });
 }
 

@@ -15,6 +15,7 @@
 #include "exact.cuh"
 #include "kernels.h"
 
+#include <atomic>
 #include <cfloat>
 #include <cstdlib>
 #include <mutex>
@@ -101,7 +102,17 @@ static int64_t prep_smem_floats(const PrepArgs& a, int mode, bool staged) {
   return static_cast<int64_t>(arrays) * ((a.K + 3) & ~3);
 }
 
-constexpr uint32_t kRowSpin = 1u << 22;  // bounded wait for a row's bulk copy
+// Polls of a row's bulk-copy wait before the prep gives up (kErrTimeout). Host code may lower
+// it (set_wait_limit) to make the wait give up on purpose; the drain of a copy still in flight
+// after giving up always uses the full limit.
+constexpr uint32_t kRowSpin = 1u << 22;
+static std::atomic<int64_t> g_row_polls{-1};
+
+void set_wait_limit(int64_t polls) { g_row_polls.store(polls < 0 ? -1 : polls); }
+static uint32_t row_polls() {
+  const int64_t v = g_row_polls.load();
+  return v < 0 ? kRowSpin : static_cast<uint32_t>(v > 0xffffffffLL ? 0xffffffffLL : v);
+}
 
 __device__ __forceinline__ uint32_t shared_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -188,10 +199,11 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepArgs a, int mode
         if (copy2) row_bulk_copy(p2, orow, bytes, &s_rowbar);
       }
       bool done = false;
-      for (uint32_t i = 0; i < kRowSpin && !done; ++i) done = row_bar_done(&s_rowbar);
+      for (uint32_t i = 0; i < a.row_polls && !done; ++i) done = row_bar_done(&s_rowbar);
       if (__syncthreads_or(!done)) {  // (uniform) report, let the copies land (bounded), and
                                       // leave the outputs unwritten
         if (tid == 0 && a.err) atomicOr(a.err, kErrTimeout);
+        // the copy itself is still in flight: drain it with the full limit before leaving
         for (uint32_t i = 0; i < kRowSpin && !row_bar_done(&s_rowbar); ++i) {
         }
         return;
@@ -369,10 +381,12 @@ cudaError_t launch_prep(const PrepArgs& a, cudaStream_t s) {
       return cudaErrorInvalidValue;
   }
   if (smem > 48 * 1024) raise_smem_limit(reinterpret_cast<const void*>(prep_kernel));
+  PrepArgs q = a;
+  q.row_polls = row_polls();
   // few rows: latency-bound, 512 threads per row; many rows: throughput-bound, 128 threads
   // per row so that registers allow several row CTAs per SM
   const int threads = a.M >= kPrepManyRows ? kPrepThreadsMany : kPrepThreads;
-  return launch_k(prep_kernel, dim3(a.M), dim3(threads), smem, s, a.pdl, a, mode, staged);
+  return launch_k(prep_kernel, dim3(a.M), dim3(threads), smem, s, a.pdl, q, mode, staged);
 }
 
 __device__ __forceinline__ int block_sum_int(int v, int* red) {

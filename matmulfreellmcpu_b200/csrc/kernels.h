@@ -33,6 +33,7 @@ struct PrepArgs {
   bool fixed = true;
   bool pdl = false;              // launch as a programmatic dependent of the previous kernel
   uint32_t* err = nullptr;       // optional: bit kErrTimeout on a timed-out wait
+  uint32_t row_polls = 0;        // set by launch_prep: polls of the row-staging wait
   // kPrepSwishgate of one decode step with the token mixer fused in: o is not read but
   // computed here from the i / f projections and the recurrent state (which is updated), as
   // launch_mixer does for len 1; needs K % 4 == 0, 16-byte aligned rows and K >= 8
@@ -142,6 +143,10 @@ cudaError_t launch_matmul_tc_group(const MatmulArgs* a, int nproj, int swiglu_I,
 cudaError_t launch_repack(void* dst, const int8_t* wq, int64_t n, int64_t k, uint32_t* err,
                           cudaStream_t s);
 cudaError_t launch_prep(const PrepArgs& a, cudaStream_t s);
+// Polls of the prep's row-staging wait before it gives up and raises kErrTimeout, for the
+// launches that follow (negative: the default limit). A diagnostic switch: 0 makes every
+// staged wait give up at once, which exercises the error path without a fault.
+void set_wait_limit(int64_t polls);
 // int32 activation codes [M, K] (int16 range) -> high/low byte planes [2][M][Kp] + row sums;
 // codes outside int16 set kErrRange in *err.
 cudaError_t launch_codes_to_planes(int8_t* planes, int32_t* rowsum, const int32_t* x, int M,

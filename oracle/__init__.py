@@ -32,9 +32,25 @@ SZ = C.c_size_t
 VP = C.c_void_p
 
 
-def build(ref: bool = True) -> None:
-    """Run the oracle Makefile (the restatement always, the reference when present)."""
-    subprocess.run(["make", "-s", "-C", HERE, "oracle"] + (["ref"] if ref else []), check=True)
+SEAM_CHECK = os.path.join(HERE, "_ref", "seam_check")
+
+
+def reference_tree() -> str:
+    """The reference checkout: $MMFREE_REFERENCE, else a sibling of this repository named
+    ``reference`` (the Makefile's default too)."""
+    return os.environ.get("MMFREE_REFERENCE",
+                          os.path.abspath(os.path.join(HERE, "..", "..", "reference")))
+
+
+def build(ref: bool | None = None) -> None:
+    """Run the oracle Makefile: the restatement always; the reference engine, and the seam
+    check that runs it with the CUDA backend injected, where the reference tree is present
+    (``ref`` None: detect it)."""
+    if ref is None:
+        ref = os.path.isdir(os.path.join(reference_tree(), "cpp"))
+    targets = ["oracle"] + (["ref", "seam"] if ref else [])
+    env = dict(os.environ, MMFREE_REFERENCE=reference_tree())
+    subprocess.run(["make", "-s", "-C", HERE] + targets, check=True, env=env)
 
 
 def _f(a):

@@ -9,6 +9,9 @@ sources by ``oracle/Makefile``) through ``oracle/ref_ops.cpp``. Run from the rep
 ``--big`` also records the 370M (16-token prompt, 32 greedy tokens) and 1.3B (128-token
 prompt, 256 greedy tokens) streams of the benchmark configurations; those need the seeded
 blobs (about 0.5 GB and 1.6 GB, written to $MMFREE_BLOB_CACHE or /tmp/mmfree_blobs).
+``--bench-configs`` (or ``--only-bench-configs``) records the benchmarked configurations at
+their full sizes: config 3 (1.3B, 64 streams x 256-id prompts, generate_serve) and config 4
+(2.7B, a 2048-id prefill); they need the 1.3B and 2.7B blobs (1.6 GB and 3.2 GB).
 """
 from __future__ import annotations
 
@@ -131,16 +134,56 @@ def make_big(R: oracle.Reference, cache) -> None:
         np.savez_compressed(os.path.join(OUT, f"config_{name}.npz"), **arrays)
 
 
+#: configuration 3: 64 streams with 256-id prompts (seeds 1000 + b), first token + 16 steps
+SERVE_STREAMS, SERVE_PROMPT, SERVE_GEN = 64, 256, 17
+#: configuration 4: one of the 8 prefill sequences (2048 ids, seed 4000)
+PREFILL_LEN, PREFILL_SEED = 2048, 4000
+
+
+def make_bench_configs(R: oracle.Reference, cache) -> None:
+    """The two benchmarked workloads at their own sizes: config 3 (1.3B, 64 x 256-id prompts,
+    Model::generate_serve, fixed) and config 4 (2.7B, a 2048-id sequence, the last row of
+    Model::forward in fixed and float mode). Takes several minutes of CPU."""
+    path = B.cached_blob("1.3B", 0, cache)
+    prompts = [B.seeded_ids(SERVE_PROMPT, 1000 + b) for b in range(SERVE_STREAMS)]
+    m = R.model(path, 1)
+    streams = m.generate_serve(prompts, SERVE_GEN)
+    m.close()
+    gen = np.stack([s[SERVE_PROMPT:] for s in streams])  # [64, 17]: first id + 16 steps
+    np.savez_compressed(os.path.join(OUT, "config3_serve_1.3B.npz"),
+                        blob_sha256=np.frombuffer(bytes.fromhex(sha256_file(path)), np.uint8),
+                        prompt_seeds=np.arange(1000, 1000 + SERVE_STREAMS), gen_ids=gen)
+    path = B.cached_blob("2.7B", 0, cache)
+    ids = B.seeded_ids(PREFILL_LEN, PREFILL_SEED)
+    arrays = {"blob_sha256": np.frombuffer(bytes.fromhex(sha256_file(path)), np.uint8),
+              "ids": ids}
+    for aq, mode in ((1, "fixed"), (0, "float")):
+        m = R.model(path, aq)
+        last = m.forward(ids)[-1].copy()
+        m.close()
+        arrays[f"{mode}_logits"] = last
+        arrays[f"{mode}_argmax"] = np.array([int(np.argmax(last))], np.int64)
+    np.savez_compressed(os.path.join(OUT, "config4_prefill_2.7B.npz"), **arrays)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--big", action="store_true")
+    ap.add_argument("--bench-configs", action="store_true",
+                    help="also record configurations 3 and 4 at their full sizes")
+    ap.add_argument("--only-bench-configs", action="store_true")
     ap.add_argument("--cache", default=os.environ.get("MMFREE_BLOB_CACHE", "/tmp/mmfree_blobs"))
     a = ap.parse_args()
     R = oracle.Reference()
+    if a.only_bench_configs:
+        make_bench_configs(R, a.cache)
+        return
     make_ops(R)
     make_models(R, ("tiny", "ragged", "small"), a.cache)
     if a.big:
         make_big(R, a.cache)
+    if a.bench_configs:
+        make_bench_configs(R, a.cache)
 
 
 if __name__ == "__main__":

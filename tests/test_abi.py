@@ -30,7 +30,7 @@ def test_library_exports_every_declared_symbol():
     for name in declared:
         assert hasattr(lib, name), f"{name} declared but not exported"
     assert declared == set(_lib.SIGNATURES), "binding table and header disagree"
-    assert lib.mmfree_cuda_abi_version() == 1
+    assert lib.mmfree_cuda_abi_version() == 2
 
 
 def numpy_pack(wq: np.ndarray) -> np.ndarray:

@@ -71,6 +71,44 @@ def test_noalloc_matches_bitlinear_on_consecutive_calls(cuda, mode):
                 assert np.abs(out - ref_out).max() <= FLOAT_TOL * max(1.0, float(np.abs(ref_out).max()))
 
 
+@pytest.mark.parametrize("M", [3, 40])  # dp4a and tensor-core kernels
+def test_noalloc_matches_oracle(cuda, orc, M):
+    # pinned to the CPU oracle directly, not only through mmfree_cuda_bitlinear
+    K, N = 2048, 2048
+    x, nw, wq = _inputs(M, K, N, seed=7 + M)
+    xd, nwd = _dev(x, cuda), _dev(nw, cuda)
+    wp = api.repack_ternary(_dev(wq, cuda))
+    r_out, r_acc, r_norm = orc.bitlinear(x, nw, wq, 20.0, act_quant=1, want_norm=True)
+    for _ in range(2):
+        out, acc, norm = _noalloc(cuda, xd, nwd, wp, 20.0, N, "fixed")
+        assert np.array_equal(acc, r_acc)
+        assert bits_equal(out, r_out)
+        assert bits_equal(norm, r_norm)
+
+
+def test_noalloc_timeout_is_reported_then_cleared(cuda):
+    # a kernel that gives up a bounded wait records it in the array's own error word; the
+    # status call reports it once, and the next call is correct again
+    M, K, N = 4, 1024, 256
+    x, nw, wq = _inputs(M, K, N, seed=11)
+    xd, nwd = _dev(x, cuda), _dev(nw, cuda)
+    wp = api.repack_ternary(_dev(wq, cuda))
+    ref_out, _, _ = api.bitlinear(xd, nwd, wp, 20.0, N)
+    api.kernel_status()
+    api.set_wait_limit(0)
+    try:
+        _noalloc(cuda, xd, nwd, wp, 20.0, N, "fixed")
+    finally:
+        api.set_wait_limit(-1)
+    with pytest.raises(_lib.MmfreeError) as e:
+        api.kernel_status()
+    assert e.value.code == _lib.E_TIMEOUT
+    api.kernel_status()
+    out, _, _ = _noalloc(cuda, xd, nwd, wp, 20.0, N, "fixed")
+    api.kernel_status()
+    assert bits_equal(out, ref_out.cpu().numpy())
+
+
 def test_noalloc_rejects_oversize_calls(cuda):
     import torch
     M, K, N = 4096, 2560, 64  # 2 * 4096 * 2560 bytes of planes > 4 MiB
