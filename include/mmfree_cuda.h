@@ -188,6 +188,27 @@ int mmfree_cuda_blob_config(const char* blob_path, mmfree_cuda_config* out);
 int mmfree_cuda_model_open(const char* blob_path, int device, int act_quant, int frac_bits,
                            mmfree_cuda_model** out);
 void mmfree_cuda_model_close(mmfree_cuda_model* m);
+
+/* ---- tensor-parallel prefill (configuration 4: one process per GPU, NCCL over NVLink) ---
+ * No reference counterpart: the reference is one CPU process. A TP handle is rank `rank` of
+ * `world` and holds only its shards of the per-layer BitLinear weights; its prefill
+ * (mmfree_cuda_forward, _forward_last, _serve_begin -- every rank calls it with the same
+ * ids, and every rank gets the full result) splits each layer of hgrn_model.cpp:80-195:
+ *   FixedQ510: every projection column-parallel, an NCCL all-gather of the column slices
+ *              before each exact full-row norm; bit-identical to one GPU;
+ *   Float:     i/f/g/gate column-parallel, o/down row-parallel; an NCCL all-reduce of
+ *              per-row partial sums of squares before g_norm, o_proj and down_proj, and one
+ *              of the row-parallel outputs; within the Float tolerance of one GPU.
+ * Decode calls on a TP handle fail with MMFREE_E_STATE. hidden_size and intermediate_size
+ * must be multiples of 32 * world; the blob must be the int8 model.mmfree. NCCL
+ * (libnccl.so.2) is loaded when the first TP call needs it.
+ * nccl_unique_id: 128 bytes that rank 0 creates and the caller sends to every rank (for
+ * example with MPI_Bcast or torch.distributed.broadcast) before each calls model_open_tp;
+ * model_open_tp is collective: it returns on a rank once every rank has called it. */
+int mmfree_cuda_nccl_unique_id(unsigned char* out);
+int mmfree_cuda_model_open_tp(const char* blob_path, int device, int act_quant, int frac_bits,
+                              int rank, int world, const unsigned char* nccl_id,
+                              mmfree_cuda_model** out);
 int mmfree_cuda_model_config(const mmfree_cuda_model* m, mmfree_cuda_config* out);
 size_t mmfree_cuda_model_weight_bytes(const mmfree_cuda_model* m); /* packed ternary bytes */
 

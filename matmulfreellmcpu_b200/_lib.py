@@ -41,6 +41,8 @@ SIGNATURES = {
     "mmfree_cuda_rmsnorm_swishgate": (I, [VP, VP, VP, VP, SZ, SZ, F, VP]),
     "mmfree_cuda_model_open": (I, [C.c_char_p, I, I, I, C.POINTER(VP)]),
     "mmfree_cuda_model_close": (None, [VP]),
+    "mmfree_cuda_nccl_unique_id": (I, [VP]),
+    "mmfree_cuda_model_open_tp": (I, [C.c_char_p, I, I, I, I, I, VP, C.POINTER(VP)]),
     "mmfree_cuda_model_config": (I, [VP, VP]),
     "mmfree_cuda_blob_config": (I, [C.c_char_p, VP]),
     "mmfree_cuda_model_weight_bytes": (SZ, [VP]),

@@ -85,6 +85,25 @@ class Model:
         self.config = _config(c)
         self.device = device
 
+    @classmethod
+    def open_tp(cls, blob_path: str, act_quant, rank: int, world: int, nccl_id: bytes,
+                frac_bits: int = 10, device: int = 0) -> "Model":
+        """Rank ``rank`` of a ``world``-way tensor-parallel prefill handle (collective: every
+        rank opens its handle with the same NCCL id; see ``matmulfreellmcpu_b200.tp``)."""
+        if len(nccl_id) != 128:
+            raise ValueError("an NCCL unique id has 128 bytes")
+        self = cls.__new__(cls)
+        h = C.c_void_p()
+        buf = (C.c_ubyte * 128).from_buffer_copy(nccl_id)
+        check(lib().mmfree_cuda_model_open_tp(blob_path.encode(), device, _aq(act_quant), frac_bits,
+                                              rank, world, buf, C.byref(h)))
+        self._h = h
+        c = _CConfig()
+        check(lib().mmfree_cuda_model_config(self._h, C.byref(c)))
+        self.config = _config(c)
+        self.device = device
+        return self
+
     def close(self) -> None:
         if getattr(self, "_h", None):
             lib().mmfree_cuda_model_close(self._h)
@@ -239,6 +258,13 @@ def bitlinear(x, norm_weight, wpacked, scale_w: float, out_dim: int, eps: float 
                                       _ptr(norm), _aq(act_quant), frac_bits, _ptr(acc),
                                       _stream(stream)))
     return out, acc, norm
+
+
+def nccl_unique_id() -> bytes:
+    """128 bytes that identify a new NCCL communicator (rank 0 makes it, every rank uses it)."""
+    buf = (C.c_ubyte * 128)()
+    check(lib().mmfree_cuda_nccl_unique_id(buf))
+    return bytes(buf)
 
 
 def kernel_status(stream=None) -> None:

@@ -15,6 +15,7 @@
 #include "kernels.h"
 #include "blob.h"
 #include "model.h"
+#include "tp.h"
 
 using namespace mmfree_cuda;
 
@@ -587,6 +588,40 @@ int mmfree_cuda_model_open(const char* blob_path, int device, int act_quant, int
     auto* h = new mmfree_cuda_model{nullptr};
     try {
       h->impl = new Model(blob_path, device, act_quant == MMFREE_ACT_FIXED_Q510, frac_bits);
+    } catch (...) {
+      delete h;
+      throw;
+    }
+    *out = h;
+  });
+}
+
+int mmfree_cuda_nccl_unique_id(unsigned char* out) {
+  return guard([&] {
+    need(out != nullptr, "null pointer");
+    TpComm::unique_id(out);
+  });
+}
+
+int mmfree_cuda_model_open_tp(const char* blob_path, int device, int act_quant, int frac_bits,
+                              int rank, int world, const unsigned char* nccl_id,
+                              mmfree_cuda_model** out) {
+  return guard([&] {
+    need(blob_path && out && nccl_id, "null pointer");
+    need(act_quant == MMFREE_ACT_FLOAT || act_quant == MMFREE_ACT_FIXED_Q510, "bad act_quant");
+    need(frac_bits >= 0 && frac_bits <= 30, "frac_bits must be in [0, 30]");
+    need(world >= 1 && rank >= 0 && rank < world, "bad rank / world size");
+    *out = nullptr;
+    int n = 0;
+    ck(cudaGetDeviceCount(&n), "cudaGetDeviceCount");
+    need(device >= 0 && device < n, "no such CUDA device");
+    TpSpec tp;
+    tp.rank = rank;
+    tp.world = world;
+    tp.nccl_id = nccl_id;
+    auto* h = new mmfree_cuda_model{nullptr};
+    try {
+      h->impl = new Model(blob_path, device, act_quant == MMFREE_ACT_FIXED_Q510, frac_bits, tp);
     } catch (...) {
       delete h;
       throw;

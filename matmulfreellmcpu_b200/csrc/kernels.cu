@@ -583,6 +583,10 @@ cudaError_t launch_matmul(const MatmulArgs& a, cudaStream_t s) {
 // The scan alone (the C-ABI hgrn_scan, hgrn_scan.cpp:11-19): state = fma(f, state, s) along
 // t for each of nseq x H lanes; x layout [nseq][T][H], state [nseq][H] (nullable: zero
 // start, not written back).
+// The serial chain is one FMA per step; the loads of the next kScanAhead steps are issued
+// before the chain consumes the current batch, so one memory latency covers a whole batch
+// (few lanes run per SM: each must keep many loads in flight).
+constexpr int kScanAhead = 32;
 __global__ void scan_kernel(float* __restrict__ out, const float* __restrict__ s,
                             const float* __restrict__ f, float* __restrict__ state, int nseq,
                             int T, int H) {
@@ -593,13 +597,137 @@ __global__ void scan_kernel(float* __restrict__ out, const float* __restrict__ s
   const int64_t q = lane / H, c = lane % H;
   const int64_t base = q * T * H + c;
   float st = state ? state[lane] : 0.0f;
-#pragma unroll 4
-  for (int t = 0; t < T; ++t) {
-    const int64_t e = base + static_cast<int64_t>(t) * H;
-    st = hgrn_step_x(f[e], st, s[e]);
-    out[e] = st;
+  float fa[kScanAhead], sa[kScanAhead];
+#pragma unroll
+  for (int u = 0; u < kScanAhead; ++u) {
+    const int64_t e = base + static_cast<int64_t>(u) * H;
+    fa[u] = u < T ? __ldcs(f + e) : 0.0f;
+    sa[u] = u < T ? __ldcs(s + e) : 0.0f;
+  }
+  for (int t0 = 0; t0 < T; t0 += kScanAhead) {
+    float fn[kScanAhead], sn[kScanAhead];
+#pragma unroll
+    for (int u = 0; u < kScanAhead; ++u) {  // the next batch, in flight during this one
+      const int t = t0 + kScanAhead + u;
+      const int64_t e = base + static_cast<int64_t>(t) * H;
+      fn[u] = t < T ? __ldcs(f + e) : 0.0f;
+      sn[u] = t < T ? __ldcs(s + e) : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < kScanAhead; ++u) {
+      if (t0 + u >= T) break;
+      st = hgrn_step_x(fa[u], st, sa[u]);
+      __stcs(out + base + static_cast<int64_t>(t0 + u) * H, st);
+    }
+#pragma unroll
+    for (int u = 0; u < kScanAhead; ++u) {
+      fa[u] = fn[u];
+      sa[u] = sn[u];
+    }
   }
   if (state) state[lane] = st;
+}
+
+// The gates of a prefill, element-parallel (hgrn_model.cpp:109-134): f = sigmoid(fraw), lower
+// bounded, and the scan input swiglu(i, 1 - f), written in place over fraw and i. Element e of
+// [nseq][T][H] is in the SIMD body of its reference vector call (seg elements) unless it is
+// among the call's last seg % 8 elements. Four consecutive elements per thread.
+__global__ void gates_kernel(float* __restrict__ iv, float* __restrict__ fv,
+                             const float* __restrict__ lb, int64_t n, int H, int64_t seg) {
+  grid_dep_launch();
+  grid_dep_wait();
+  const int64_t e0 = 4 * (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x);
+  if (e0 >= n) return;
+  const int64_t body_n = seg & ~int64_t(7);
+  float a[4], b[4], l[4];
+  bool body[4];
+  const bool vec = e0 + 3 < n;
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int64_t e = e0 + u;
+    a[u] = (vec || e < n) ? __ldcs(iv + e) : 0.0f;
+    b[u] = (vec || e < n) ? __ldcs(fv + e) : 0.0f;
+    l[u] = lb ? __ldg(lb + e % H) : 0.0f;
+    body[u] = e % seg < body_n;
+  }
+  float f[4], om[4], x[4];
+  sigmoid_n(b, body, f);
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    if (lb) f[u] = lower_bound_x(f[u], l[u]);
+    om[u] = __fadd_rn(1.0f, -f[u]);
+  }
+  swiglu_n(a, om, body, x);
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    if (e0 + u >= n) break;
+    fv[e0 + u] = f[u];
+    iv[e0 + u] = x[u];
+  }
+}
+
+// Chunked parallel scan (Float mode): the recurrence h_t = f_t h_{t-1} + x_t over chunks of
+// kChunkT steps. Pass 1, one thread per (sequence, chunk, channel): the chunk's scan from a
+// zero state (written to out) and its summary (prod f, end state). Pass 2, one thread per
+// lane: carries in chunk order. Pass 3, one thread per (sequence, chunk, channel): out_t +=
+// (prod_{s <= t} f_s) * carry-in. Sums are re-associated, which the Float tolerance allows.
+constexpr int kChunkT = 64;
+__global__ void chunk_scan_kernel(float* __restrict__ out, float2* __restrict__ summ,
+                                  const float* __restrict__ x, const float* __restrict__ f,
+                                  int nseq, int T, int H, int nch) {
+  grid_dep_launch();
+  grid_dep_wait();
+  const int64_t id = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (id >= static_cast<int64_t>(nseq) * nch * H) return;
+  const int c = static_cast<int>(id % H);
+  const int64_t qk = id / H;
+  const int k = static_cast<int>(qk % nch), q = static_cast<int>(qk / nch);
+  const int t0 = k * kChunkT, t1 = min(T, t0 + kChunkT);
+  const int64_t base = static_cast<int64_t>(q) * T * H + c;
+  float st = 0.0f, pr = 1.0f;
+  for (int t = t0; t < t1; ++t) {
+    const int64_t e = base + static_cast<int64_t>(t) * H;
+    const float ft = f[e];
+    st = __fmaf_rn(ft, st, x[e]);
+    pr = __fmul_rn(pr, ft);
+    out[e] = st;
+  }
+  summ[id] = make_float2(pr, st);
+}
+
+__global__ void chunk_carry_kernel(float2* __restrict__ summ, float* __restrict__ state, int nseq,
+                                   int H, int nch) {
+  const int64_t lane = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (lane >= static_cast<int64_t>(nseq) * H) return;
+  const int c = static_cast<int>(lane % H);
+  const int64_t q = lane / H;
+  float carry = state ? state[lane] : 0.0f;
+  for (int k = 0; k < nch; ++k) {
+    const int64_t id = (q * nch + k) * H + c;
+    const float2 s = summ[id];
+    summ[id].y = carry;  // becomes this chunk's carry-in
+    carry = __fmaf_rn(s.x, carry, s.y);
+  }
+  if (state) state[lane] = carry;
+}
+
+__global__ void chunk_fix_kernel(float* __restrict__ out, const float2* __restrict__ summ,
+                                 const float* __restrict__ f, int nseq, int T, int H, int nch) {
+  const int64_t id = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (id >= static_cast<int64_t>(nseq) * nch * H) return;
+  const int c = static_cast<int>(id % H);
+  const int64_t qk = id / H;
+  const int k = static_cast<int>(qk % nch), q = static_cast<int>(qk / nch);
+  const float carry = summ[id].y;
+  if (carry == 0.0f) return;
+  const int t0 = k * kChunkT, t1 = min(T, t0 + kChunkT);
+  const int64_t base = static_cast<int64_t>(q) * T * H + c;
+  float pr = 1.0f;
+  for (int t = t0; t < t1; ++t) {
+    const int64_t e = base + static_cast<int64_t>(t) * H;
+    pr = __fmul_rn(pr, f[e]);
+    out[e] = __fmaf_rn(pr, carry, out[e]);
+  }
 }
 
 // The token mixer of one decode step (one position per lane, H >= 8): a grid of about one
@@ -714,7 +842,8 @@ __global__ void __launch_bounds__(128) mixer_kernel(float* __restrict__ out, con
 }
 
 cudaError_t launch_mixer(float* i, float* f, float* recur, float* state, const float* lb,
-                         int nseq, int len, int H, int seg_rows, cudaStream_t s, bool pdl) {
+                         int nseq, int len, int H, int seg_rows, cudaStream_t s, bool pdl,
+                         void* chunk_ws) {
   const int64_t lanes = static_cast<int64_t>(nseq) * H;
   if (lanes == 0 || len == 0) return cudaSuccess;
   if (len == 1 && H >= 8) {
@@ -723,10 +852,40 @@ cudaError_t launch_mixer(float* i, float* f, float* recur, float* state, const f
                     pdl, recur, static_cast<const float*>(i), static_cast<const float*>(f), state, lb,
                     nseq, H, static_cast<int64_t>(seg_rows) * H);
   }
-  const int64_t ctas = ceil_div(lanes, 128);
-  return launch_k(mixer_kernel, dim3(static_cast<unsigned>(ctas)), dim3(128), 0, s, pdl,
-                  recur, static_cast<const float*>(i), static_cast<const float*>(f), state, lb, nseq, len,
-                  H, static_cast<int64_t>(seg_rows) * H);
+  static const bool fused = [] {
+    const char* e = std::getenv("MMFREE_MIXER_FUSED");
+    return e && e[0] == '1';
+  }();
+  if (fused && !chunk_ws) {  // one pass, one thread per lane (gates and chain in one thread)
+    const int64_t ctas = ceil_div(lanes, 128);
+    return launch_k(mixer_kernel, dim3(static_cast<unsigned>(ctas)), dim3(128), 0, s, pdl,
+                    recur, static_cast<const float*>(i), static_cast<const float*>(f), state, lb, nseq,
+                    len, H, static_cast<int64_t>(seg_rows) * H);
+  }
+  // the gates element-parallel, then the scan: the exact serial chain per lane, or (Float, with
+  // chunk_ws) the chunked parallel scan
+  const int64_t n = lanes * len;
+  cudaError_t e = launch_k(gates_kernel, dim3(static_cast<unsigned>(ceil_div(n, 4 * 256))), dim3(256),
+                           0, s, pdl, i, f, lb, n, H, static_cast<int64_t>(seg_rows) * H);
+  if (e != cudaSuccess) return e;
+  if (!chunk_ws) {
+    return launch_k(scan_kernel, dim3(static_cast<unsigned>(ceil_div(lanes, 128))), dim3(128), 0, s,
+                    pdl, recur, static_cast<const float*>(i), static_cast<const float*>(f), state, nseq,
+                    len, H);
+  }
+  const int nch = static_cast<int>(ceil_div(len, kChunkT));
+  auto* summ = static_cast<float2*>(chunk_ws);
+  const int64_t items = static_cast<int64_t>(nseq) * nch * H;
+  chunk_scan_kernel<<<static_cast<unsigned>(ceil_div(items, 256)), 256, 0, s>>>(recur, summ, i, f, nseq,
+                                                                                len, H, nch);
+  chunk_carry_kernel<<<static_cast<unsigned>(ceil_div(lanes, 128)), 128, 0, s>>>(summ, state, nseq, H, nch);
+  chunk_fix_kernel<<<static_cast<unsigned>(ceil_div(items, 256)), 256, 0, s>>>(recur, summ, f, nseq, len,
+                                                                               H, nch);
+  return cudaGetLastError();
+}
+
+size_t mixer_chunk_bytes(int nseq, int len, int H) {
+  return static_cast<size_t>(nseq) * static_cast<size_t>(ceil_div(len, kChunkT)) * H * sizeof(float2);
 }
 
 cudaError_t launch_scan(float* out, const float* i, const float* f, int T, int D, float* state,

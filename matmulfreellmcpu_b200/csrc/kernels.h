@@ -159,8 +159,13 @@ cudaError_t launch_matmul(const MatmulArgs& a, cudaStream_t s);
 // sequences from state [nseq][H] (nullable: zero start, not written back). The reference's
 // SIMD body/tail split is taken over segments of seg_rows * H elements: the rows of one
 // reference block() call.
+// For len > 1 the gates run element-parallel, then the scan: the reference's serial chain per
+// lane (bit-exact), or with chunk_ws (mixer_chunk_bytes of device memory; Float mode) a
+// chunked parallel scan over time that re-associates the recurrence.
 cudaError_t launch_mixer(float* i, float* f, float* recur, float* state, const float* lb,
-                         int nseq, int len, int H, int seg_rows, cudaStream_t s, bool pdl = false);
+                         int nseq, int len, int H, int seg_rows, cudaStream_t s, bool pdl = false,
+                         void* chunk_ws = nullptr);
+size_t mixer_chunk_bytes(int nseq, int len, int H);
 // z[t, c] = silu(y[t, c]) * y[t, I + c]  (hgrn_model.cpp:171-185), tails per seg_rows rows.
 cudaError_t launch_swiglu_split(float* z, const float* y, int rows, int I, int seg_rows,
                                 cudaStream_t s, bool pdl = false);

@@ -18,6 +18,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "tp.h"
 
 namespace mmfree_cuda {
 
@@ -35,7 +36,7 @@ const char* kProjTags[6] = {"i_proj", "f_proj", "g_proj", "o_proj", "gate_proj",
 
 }  // namespace
 
-Model::Model(const std::string& blob_path, int device, bool fixed, int frac_bits)
+Model::Model(const std::string& blob_path, int device, bool fixed, int frac_bits, const TpSpec& tp)
     : device_(device), fixed_(fixed) {
   if (frac_bits < 0 || frac_bits > 30) throw std::runtime_error("frac_bits must be in [0, 30]");
   qs_ = static_cast<float>(1u << frac_bits);
@@ -48,6 +49,22 @@ Model::Model(const std::string& blob_path, int device, bool fixed, int frac_bits
   L_ = static_cast<int>(cfg_.num_hidden_layers);
   eps_ = cfg_.rms_norm_eps;
   if (H_ <= 0 || I_ <= 0 || V_ <= 0 || L_ <= 0) throw std::runtime_error("weights: bad config");
+  if (tp.world > 1) {
+    // shards of whole 32-row weight groups, and no SIMD tails inside a shard (H, I multiples
+    // of 8 keep every elementwise call of the reference free of tails)
+    if (tp.rank < 0 || tp.rank >= tp.world || !tp.nccl_id)
+      throw std::invalid_argument("tensor parallel: bad rank, world size or NCCL id");
+    if (H_ % (32 * tp.world) != 0 || I_ % (32 * tp.world) != 0)
+      throw std::invalid_argument("tensor parallel: hidden and intermediate sizes must be "
+                                  "multiples of 32 x world size");
+    tp_rank_ = tp.rank;
+    tp_world_ = tp.world;
+    Hs_ = H_ / tp.world;
+    Is_ = I_ / tp.world;
+  } else {
+    Hs_ = H_;
+    Is_ = I_;
+  }
   if (padded_k(std::max(H_, I_)) * 4 > 227 * 1024)
     throw std::runtime_error("hidden/intermediate size too large for the prep kernel");
   CK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
@@ -121,17 +138,29 @@ Model::Model(const std::string& blob_path, int device, bool fixed, int frac_bits
   }
   for (int l = 0; l < L_; ++l) layers_[l].lb = (use_lb && l > 0) ? lb_base + size_t(l) * H : nullptr;
 
-  // ---- ternary weights: upload int8, repack to the tiled 2-bit format
-  struct WItem { std::string tag; size_t out, in; Proj* p; };
+  // ---- ternary weights: upload int8, repack to the tiled 2-bit format. With tensor
+  // parallelism a projection holds this rank's shard: whole (lm_head), a block of output rows
+  // (column-parallel), the two row blocks of a SwiGLU pair (gate_proj), or a block of input
+  // columns (row-parallel o/down in Float).
+  enum ShardKind { kWhole = 0, kRows, kGatePair, kCols };
+  struct WItem { std::string tag; size_t out, in; Proj* p; int kind; size_t sout, sin, off; };
   std::vector<WItem> ws;
-  ws.push_back({"lm_head", V, H, &lm_head_});
+  const size_t Hs = Hs_, Is = Is_, r = tp_rank_;
+  ws.push_back({"lm_head", V, H, &lm_head_, kWhole, V, H, 0});
   for (int l = 0; l < L_; ++l) {
     const std::string p = "model.layers." + std::to_string(l);
     for (int j = 0; j < 6; ++j) {
       size_t out = H, in = H;
       if (j == kGate) out = 2 * I;
       if (j == kDown) in = I;
-      ws.push_back({p + "." + kProjTags[j], out, in, &layers_[l].p[j]});
+      WItem w{p + "." + kProjTags[j], out, in, &layers_[l].p[j], kWhole, out, in, 0};
+      if (tp_world_ > 1) {
+        if (j == kGate) w = {w.tag, out, in, w.p, kGatePair, 2 * Is, in, r * Is};
+        else if (j == kDown && !fixed_) w = {w.tag, out, in, w.p, kCols, H, Is, r * Is};
+        else if (j == kO && !fixed_) w = {w.tag, out, in, w.p, kCols, H, Hs, r * Hs};
+        else w = {w.tag, out, in, w.p, kRows, Hs, in, r * Hs};
+      }
+      ws.push_back(w);
     }
   }
   size_t max_i8 = 0;
@@ -140,9 +169,11 @@ Model::Model(const std::string& blob_path, int device, bool fixed, int frac_bits
     const BlobTensor& t = blob.get(w.tag + ".wq");
     if (!(t.is_int8 || t.is_packed) || t.shape.size() != 2 || t.shape[0] != w.out || t.shape[1] != w.in)
       throw std::runtime_error("weights: unexpected dtype/shape for " + w.tag + ".wq");
+    if (t.is_packed && w.kind != kWhole)
+      throw std::invalid_argument("tensor parallel: needs the int8 model.mmfree blob, not model.mmfree2");
     expect(w.tag + ".scale_w", {1}, false);
-    if (!t.is_packed) max_i8 = std::max(max_i8, w.out * w.in);
-    packed_bytes_ += static_cast<size_t>(packed_bytes(w.out, w.in));
+    if (!t.is_packed) max_i8 = std::max(max_i8, w.sout * w.sin);
+    packed_bytes_ += static_cast<size_t>(packed_bytes(w.sout, w.sin));
   }
   CK(cudaMalloc(&arena_, packed_bytes_));
   int8_t* staging = nullptr;  // int8 upload buffer of the repack (none for model.mmfree2)
@@ -151,19 +182,38 @@ Model::Model(const std::string& blob_path, int device, bool fixed, int frac_bits
     char* cur = static_cast<char*>(arena_);
     for (auto& w : ws) {
       const BlobTensor& t = blob.get(w.tag + ".wq");
+      const auto* src = static_cast<const int8_t*>(blob.data(t));
       if (t.is_packed) {  // model.mmfree2: already in the device format
-        CK(cudaMemcpyAsync(cur, blob.data(t), packed_bytes(w.out, w.in), cudaMemcpyHostToDevice, stream_));
+        CK(cudaMemcpyAsync(cur, src, packed_bytes(w.out, w.in), cudaMemcpyHostToDevice, stream_));
       } else {
-        CK(cudaMemcpyAsync(staging, blob.data(t), w.out * w.in, cudaMemcpyHostToDevice, stream_));
-        CK(launch_repack(cur, staging, w.out, w.in, err_, stream_));
+        switch (w.kind) {
+          case kWhole:
+            CK(cudaMemcpyAsync(staging, src, w.out * w.in, cudaMemcpyHostToDevice, stream_));
+            break;
+          case kRows:
+            CK(cudaMemcpyAsync(staging, src + w.off * w.in, w.sout * w.in, cudaMemcpyHostToDevice, stream_));
+            break;
+          case kGatePair: {  // gate rows [off, off + Is) then up rows [I + off, I + off + Is)
+            const size_t half = w.sout / 2 * w.in;
+            CK(cudaMemcpyAsync(staging, src + w.off * w.in, half, cudaMemcpyHostToDevice, stream_));
+            CK(cudaMemcpyAsync(staging + half, src + (I + w.off) * w.in, half, cudaMemcpyHostToDevice,
+                               stream_));
+            break;
+          }
+          case kCols:
+            CK(cudaMemcpy2DAsync(staging, w.sin, src + w.off, w.in, w.sin, w.sout,
+                                 cudaMemcpyHostToDevice, stream_));
+            break;
+        }
+        CK(launch_repack(cur, staging, w.sout, w.sin, err_, stream_));
       }
       float s;
       std::memcpy(&s, blob.data(blob.get(w.tag + ".scale_w")), 4);
       w.p->w = cur;
       w.p->scale_w = s;
-      w.p->in = static_cast<int>(w.in);
-      w.p->out = static_cast<int>(w.out);
-      cur += packed_bytes(w.out, w.in);
+      w.p->in = static_cast<int>(w.sin);
+      w.p->out = static_cast<int>(w.sout);
+      cur += packed_bytes(w.sout, w.sin);
     }
   }
   uint32_t err = 0;
@@ -171,6 +221,8 @@ Model::Model(const std::string& blob_path, int device, bool fixed, int frac_bits
   CK(cudaStreamSynchronize(stream_));
   cudaFree(staging);
   if (err & kErrNotTernary) throw std::runtime_error("weights: a wq entry is outside {-1,0,1}");
+  // every rank reaches this point: the communicator's set-up is collective
+  if (tp_world_ > 1) tp_ = std::make_unique<TpComm>(tp.nccl_id, tp.rank, tp.world);
 }
 
 Model::~Model() {
@@ -187,6 +239,9 @@ Model::~Model() {
   cudaFree(dec_part_v_);
   cudaFree(dec_part_i_);
   cudaFree(persist_tab_);
+  cudaFree(tp_ws_);
+  cudaFree(chunk_ws_);
+  tp_.reset();
   if (pinned_) cudaFreeHost(pinned_);
   if (stream_) cudaStreamDestroy(stream_);
 }
@@ -239,6 +294,20 @@ void Model::ensure_ws(size_t rows) {
     yf_[j] = fixed_ ? nullptr : reinterpret_cast<float*>(b + o_yf[j]);
   }
   ws_rows_ = rows;
+}
+
+void* Model::chunk_ws(int nseq, int len, int H) {
+  if (fixed_ || len <= 1) return nullptr;  // FixedQ510 keeps the reference's serial order
+  const size_t need = mixer_chunk_bytes(nseq, len, H);
+  if (need > chunk_bytes_) {
+    CK(cudaStreamSynchronize(stream_));
+    cudaFree(chunk_ws_);
+    chunk_ws_ = nullptr;
+    chunk_bytes_ = 0;
+    CK(cudaMalloc(&chunk_ws_, need));
+    chunk_bytes_ = need;
+  }
+  return chunk_ws_;
 }
 
 void Model::float_state(size_t elems) {
@@ -392,6 +461,10 @@ void Model::bitlinear_gate_swiglu(const Layer& ly, int M, int seg_rows) {
 
 template <class StateFn>
 void Model::layers(int nseq, int len, int seg_rows, StateFn state) {
+  if (tp_) {
+    layers_tp(nseq, len, seg_rows);
+    return;
+  }
   const int rows = nseq * len;
   for (int l = 0; l < L_; ++l) {
     const Layer& ly = layers_[l];
@@ -419,7 +492,8 @@ void Model::layers(int nseq, int len, int seg_rows, StateFn state) {
     const bool mix_in_prep = mix_prep_ok_ && len == 1 && H_ % 4 == 0 && H_ >= 8;
     if (!mix_in_prep)
       timed(kClsMixer, 4.0 * rows * H_ * 5 + 8.0 * nseq * H_, 0, [&] {
-        CK(launch_mixer(ib_, fb_, recur_, state(l), ly.lb, nseq, len, H_, seg_rows, stream_, pdl_));
+        CK(launch_mixer(ib_, fb_, recur_, state(l), ly.lb, nseq, len, H_, seg_rows, stream_, pdl_,
+                        chunk_ws(nseq, len, H_)));
       });
     // o_proj on g_norm(g) * silu(recurrence); resid = h + o
     p.x = gb_;
@@ -462,7 +536,141 @@ void Model::layers(int nseq, int len, int seg_rows, StateFn state) {
   }
 }
 
+void Model::tp_only_prefill(const char* what) const {
+  if (tp_)
+    throw std::logic_error(std::string(what) + ": a tensor-parallel handle runs prefills only "
+                                               "(forward, forward_last, serve_begin)");
+}
+
+void Model::ensure_tp_ws(size_t rows) {
+  if (rows <= tp_rows_) return;
+  CK(cudaStreamSynchronize(stream_));
+  cudaFree(tp_ws_);
+  tp_ws_ = nullptr;
+  const size_t H = H_, I = I_, Hs = Hs_, Is = Is_;
+  size_t sz = 0;
+  auto carve = [&](size_t floats) { size_t o = sz; sz += align256(floats * 4); return o; };
+  const size_t o_g = carve(rows * H), o_rec = carve(rows * H), o_st = carve(rows * std::max(H, I)),
+               o_rs = carve(rows * Hs), o_zs = carve(rows * Is), o_hs = carve(rows * Hs),
+               o_ts = carve(rows * Hs), o_ss = carve(rows * 4);
+  CK(cudaMalloc(&tp_ws_, sz));
+  char* b = static_cast<char*>(tp_ws_);
+  tp_g_ = reinterpret_cast<float*>(b + o_g);
+  tp_rec_ = reinterpret_cast<float*>(b + o_rec);
+  tp_stage_ = reinterpret_cast<float*>(b + o_st);
+  tp_rs_ = reinterpret_cast<float*>(b + o_rs);
+  tp_zs_ = reinterpret_cast<float*>(b + o_zs);
+  tp_hs_ = reinterpret_cast<float*>(b + o_hs);
+  tp_ts_ = reinterpret_cast<float*>(b + o_ts);
+  tp_ss_ = reinterpret_cast<float*>(b + o_ss);
+  tp_rows_ = rows;
+}
+
+void Model::tp_gather(float* full, const float* slice, int rows, int n) {
+  tp_->all_gather(slice, tp_stage_, static_cast<size_t>(rows) * n * 4, stream_);
+  CK(launch_interleave(full, tp_stage_, tp_world_, rows, n, stream_));
+}
+
+// One prefill over this rank's shards (hgrn_model.cpp:80-195 split as tp.h describes). The
+// row transforms and exact norms run on whole rows (replicated on every rank); h, the residual
+// and z are whole on every rank between the exchanges.
+void Model::layers_tp(int nseq, int len, int seg_rows) {
+  const int rows = nseq * len;
+  ensure_tp_ws(static_cast<size_t>(rows));
+  const int H = H_, Hs = Hs_, Is = Is_;
+  const size_t hoff = static_cast<size_t>(tp_rank_) * Hs, ioff = static_cast<size_t>(tp_rank_) * Is;
+  float* ss_a = tp_ss_;          // [rows] sums of squares
+  float* ss_b = tp_ss_ + rows;
+  auto prep_full = [&](const float* x, const float* o, const float* prew, int K, int nproj,
+                       const float* nw0, const float* nw1, const float* nw2) {
+    PrepArgs p;
+    p.fixed = fixed_;
+    p.qs = qs_;
+    p.eps = eps_;
+    p.M = rows;
+    p.x = x;
+    p.o = o;
+    p.prew = prew;
+    p.K = K;
+    p.nproj = nproj;
+    p.normw[0] = nw0;
+    p.normw[1] = nw1;
+    p.normw[2] = nw2;
+    for (int j = 0; j < 3; ++j) {
+      p.planes[j] = planes_[j];
+      p.rowsum[j] = rowsum_[j];
+      p.yf[j] = yf_[j];
+    }
+    prep(p);
+  };
+  // a shard's BitLinear into out (row stride ldo), optionally + resid (row stride ldr)
+  auto shard_mm = [&](const Proj& pj, int plane, float* out, int ldo, const float* resid, int ldr) {
+    MatmulArgs a = mm_args(pj, plane, out, rows, resid);
+    a.ldo = ldo;
+    a.ldr = ldr;
+    timed(kClsMatmul, 0, 2.0 * rows * pj.in * pj.out, [&] { CK(launch_matmul(a, stream_)); });
+  };
+  for (int l = 0; l < L_; ++l) {
+    const Layer& ly = layers_[l];
+    const float* lb = ly.lb ? ly.lb + hoff : nullptr;
+    // i/f/g column shards on whole rows of rmsnorm(h) * attn_norm
+    prep_full(h_, nullptr, ly.attn_norm, H, 3, ly.p[kI].normw, ly.p[kF].normw, ly.p[kG].normw);
+    bitlinear_ifg(ly, rows);  // shards: N = Hs each, into ib_ / fb_ / gb_ [rows][Hs]
+    CK(launch_mixer(ib_, fb_, recur_, nullptr, lb, nseq, len, Hs, seg_rows, stream_, pdl_,
+                    chunk_ws(nseq, len, Hs)));
+    if (fixed_) {
+      // whole rows of g and the recurrence for the exact g_norm chain, then o_proj columns
+      tp_gather(tp_g_, gb_, rows, Hs);
+      tp_gather(tp_rec_, recur_, rows, Hs);
+      prep_full(tp_g_, tp_rec_, ly.g_norm, H, 1, ly.p[kO].normw, nullptr, nullptr);
+      shard_mm(ly.p[kO], 0, tp_rs_, Hs, h_ + hoff, H);
+      tp_gather(resid_, tp_rs_, rows, Hs);
+    } else {
+      // g_norm and o_proj's norm from all-reduced partial sums of squares; o_proj rows
+      CK(launch_row_sumsq(ss_a, gb_, rows, Hs, Hs, stream_));
+      tp_->all_reduce_f32(ss_a, rows, stream_);
+      CK(launch_gate_slice(tp_ts_, ss_b, gb_, recur_, ss_a, ly.g_norm + hoff, rows, Hs, H, eps_,
+                           stream_));
+      tp_->all_reduce_f32(ss_b, rows, stream_);
+      const int kp = static_cast<int>(padded_k(Hs));
+      CK(launch_norm_slice(yf_[0], tp_ts_, ss_b, ly.p[kO].normw + hoff, rows, Hs, kp, H, eps_, stream_));
+      shard_mm(ly.p[kO], 0, resid_, H, nullptr, 0);  // partial [rows][H]
+      tp_->all_reduce_f32(resid_, static_cast<size_t>(rows) * H, stream_);
+      CK(launch_add(resid_, h_, resid_, static_cast<int64_t>(rows) * H, stream_));
+    }
+    // gate_proj SwiGLU pairs of this rank's Is columns of z
+    prep_full(resid_, nullptr, ly.mlp_norm, H, 1, ly.p[kGate].normw, nullptr, nullptr);
+    if (tc_rows(rows) && Is % 64 == 0) {
+      MatmulArgs a = mm_args(ly.p[kGate], 0, tp_zs_, rows, nullptr);
+      a.ldo = Is;
+      timed(kClsMatmul, 0, 2.0 * rows * H * 2.0 * Is, [&] {
+        CK(launch_matmul_tc_group(&a, 1, Is, static_cast<int64_t>(seg_rows) * Is, sms_, stream_));
+      });
+    } else {
+      shard_mm(ly.p[kGate], 0, y_, 2 * Is, nullptr, 0);
+      CK(launch_swiglu_split(tp_zs_, y_, rows, Is, seg_rows, stream_, pdl_));
+    }
+    if (fixed_) {
+      // whole rows of z for the exact down_proj norm, then down_proj columns; h whole again
+      tp_gather(z_, tp_zs_, rows, Is);
+      prep_full(z_, nullptr, nullptr, I_, 1, ly.p[kDown].normw, nullptr, nullptr);
+      shard_mm(ly.p[kDown], 0, tp_hs_, Hs, resid_ + hoff, H);
+      tp_gather(h_, tp_hs_, rows, Hs);
+    } else {
+      CK(launch_row_sumsq(ss_a, tp_zs_, rows, Is, Is, stream_));
+      tp_->all_reduce_f32(ss_a, rows, stream_);
+      const int kp = static_cast<int>(padded_k(Is));
+      CK(launch_norm_slice(yf_[0], tp_zs_, ss_a, ly.p[kDown].normw + ioff, rows, Is, kp, I_, eps_,
+                           stream_));
+      shard_mm(ly.p[kDown], 0, h_, H, nullptr, 0);  // partial [rows][H]
+      tp_->all_reduce_f32(h_, static_cast<size_t>(rows) * H, stream_);
+      CK(launch_add(h_, resid_, h_, static_cast<int64_t>(rows) * H, stream_));
+    }
+  }
+}
+
 void Model::forward_trace(const int64_t* ids, size_t T, float* logits, float* trace) {
+  tp_only_prefill("forward_trace");
   CK(cudaSetDevice(device_));
   if (T == 0) throw std::invalid_argument("forward: empty input");
   for (size_t t = 0; t < T; ++t)
@@ -668,6 +876,7 @@ void Model::fused_step(int B, int64_t stride) {
 }
 
 std::vector<Model::ClassStats> Model::serve_profile(size_t steps) {
+  tp_only_prefill("serve_profile");
   if (serve_b_ == 0) throw std::logic_error("serve_profile without serve_begin");
   const int B = serve_b_;
   const int64_t stride = static_cast<int64_t>(steps) + 1;
@@ -744,6 +953,7 @@ struct Sampler {
 
 std::vector<int64_t> Model::generate(const int64_t* ids, size_t n, size_t new_tokens,
                                      int64_t eos_id, const Sampling& samp) {
+  tp_only_prefill("generate");
   CK(cudaSetDevice(device_));
   if (n == 0) throw std::invalid_argument("generate: empty prompt");
   for (size_t t = 0; t < n; ++t)
@@ -885,6 +1095,7 @@ void Model::serve_begin(const std::vector<std::vector<int64_t>>& prompts, int64_
 }
 
 void Model::serve_step(const int64_t* in_ids, int64_t* out_ids) {
+  tp_only_prefill("serve_step");
   if (serve_b_ == 0) throw std::logic_error("serve_step without serve_begin");
   const int B = serve_b_;
   // one lockstep step: ids [B][2], position 0 holds the inputs
@@ -914,6 +1125,7 @@ void Model::serve_step(const int64_t* in_ids, int64_t* out_ids) {
 }
 
 void Model::serve_run(size_t steps, int64_t* out) {
+  tp_only_prefill("serve_run");
   if (serve_b_ == 0) throw std::logic_error("serve_run without serve_begin");
   const int B = serve_b_;
   int64_t stride = static_cast<int64_t>(steps) + 1;
@@ -956,6 +1168,7 @@ void Model::serve_end() { serve_b_ = 0; }
 std::vector<std::vector<int64_t>> Model::generate_serve(
     const std::vector<std::vector<int64_t>>& prompts, size_t new_tokens, int64_t eos_id,
     const Sampling& samp) {
+  tp_only_prefill("generate_serve");
   const size_t B = prompts.size();
   std::vector<std::vector<int64_t>> streams = prompts;
   if (B == 0) return streams;

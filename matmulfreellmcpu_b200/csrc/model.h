@@ -27,15 +27,26 @@ struct Sampling {  // model.hpp:27-31
   uint64_t seed = 0;
 };
 
+// Tensor-parallel prefill: this handle is rank `rank` of `world`, all sharing the NCCL unique
+// id (TpComm::unique_id on one rank, distributed by the caller). world = 1: no parallelism.
+struct TpSpec {
+  int rank = 0, world = 1;
+  const unsigned char* nccl_id = nullptr;
+};
+
+class TpComm;
+
 class Model {
  public:
-  Model(const std::string& blob_path, int device, bool fixed, int frac_bits);
+  Model(const std::string& blob_path, int device, bool fixed, int frac_bits,
+        const TpSpec& tp = TpSpec());
   ~Model();
   Model(const Model&) = delete;
   Model& operator=(const Model&) = delete;
 
   const BlobConfig& config() const { return cfg_; }
   int device() const { return device_; }
+  int tp_world() const { return tp_world_; }
   cudaStream_t stream() const { return stream_; }
   size_t weight_bytes() const { return packed_bytes_; }
 
@@ -108,6 +119,11 @@ class Model {
   // layer's state base ([nseq][H]) or nullptr; seg_rows = rows of one reference block call.
   template <class StateFn>
   void layers(int nseq, int len, int seg_rows, StateFn state);
+  // The same over this rank's shards (no recurrent state is kept: prefill only).
+  void layers_tp(int nseq, int len, int seg_rows);
+  void ensure_tp_ws(size_t rows);
+  void tp_gather(float* full, const float* slice, int rows, int n);  // all-gather of columns
+  void tp_only_prefill(const char* what) const;  // throws for calls a TP handle cannot serve
   void head(const float* rows, int M);  // final norm + lm_head into logits_
   void check_errors();
   void decode_graph_step(int B, int64_t stride);  // embed_at, layers (streams), head, argmax_at
@@ -183,10 +199,24 @@ class Model {
   int serve_b_ = 0;                // active serving session batch (0 = none)
   std::vector<int64_t> serve_last_;
 
+  // Float-mode prefill: workspace of the chunked scan (nullptr: the exact serial scan)
+  void* chunk_ws(int nseq, int len, int H);
+  void* chunk_ws_ = nullptr;
+  size_t chunk_bytes_ = 0;
   void float_state(size_t elems);
   void loop_ids(size_t elems);
   void pinned(size_t elems);
   void drop_graph();
+
+  // tensor parallelism (tp_ == nullptr: one GPU). Shard widths Hs = H / P, Is = I / P; the
+  // projections in layers_ hold this rank's shards (column shards of i/f/g/gate, and of o/down
+  // in FixedQ510; row shards of o/down in Float), lm_head is whole on every rank.
+  std::unique_ptr<TpComm> tp_;
+  int tp_rank_ = 0, tp_world_ = 1, Hs_ = 0, Is_ = 0;
+  size_t tp_rows_ = 0;
+  void* tp_ws_ = nullptr;
+  float *tp_g_ = nullptr, *tp_rec_ = nullptr, *tp_stage_ = nullptr, *tp_rs_ = nullptr;
+  float *tp_zs_ = nullptr, *tp_hs_ = nullptr, *tp_ts_ = nullptr, *tp_ss_ = nullptr;
 };
 
 }  // namespace mmfree_cuda

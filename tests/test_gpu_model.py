@@ -108,6 +108,25 @@ def test_long_prefill_matches_oracle(models, orc, blob_cache):
     assert bits_equal(m.forward(ids), om.forward(ids))
 
 
+def test_long_float_prefill_chunked_scan(models, orc, blob_cache):
+    """Float mode runs the prefill recurrence as a chunked parallel scan (64-step chunks, 18
+    of them here, carries propagated between chunks); every position's logits stay within
+    the Float tolerance of the oracle's sequential scan, and a multi-sequence batch gives each
+    sequence the logits it gets alone."""
+    m = models("small", "float")
+    om = orc.model(B.Blob.open(B.cached_blob("small", 0, blob_cache)))
+    ids = B.seeded_ids(1100, 31, 2048)
+    got, ref = m.forward(ids), om.forward(ids, act_quant=0)
+    span = float(ref.max() - ref.min())
+    assert float(np.abs(got - ref).max()) <= 1e-3 * span
+    seqs = [ids[:300], ids[300:700], ids[700:1000]]  # equal lengths batch in one prefill
+    seqs = [s[:300] for s in seqs]
+    first = m.serve_begin(seqs)
+    m.serve_end()
+    for k, s in enumerate(seqs):
+        assert first[k] == int(np.argmax(m.forward_last(s)))
+
+
 def test_fused_and_unfused_decode_agree(cuda, blob_cache, monkeypatch):
     """The fused few-row decode kernels (<= 4 streams) and the general per-op path give
     identical ids (both are bit-exact restatements)."""
