@@ -61,6 +61,14 @@ __device__ __forceinline__ int dp4a_uu(uint32_t a, uint32_t b, int c) {
   return d;
 }
 
+// The ternary weight (code - 1) of byte jj of m (codes 0..2 in the low bits of each byte) as
+// an exact float, without an int-to-float conversion: the byte is placed in the mantissa of
+// 2^23 (bits 0x4B0000cc = 2^23 + code), and 2^23 + 1 is subtracted.
+__device__ __forceinline__ float ternary_f32(uint32_t m, int jj) {
+  const float f = __uint_as_float(__byte_perm(m, 0x4B000000u, 0x7540u | static_cast<unsigned>(jj)));
+  return __fadd_rn(f, -8388609.0f);
+}
+
 // Device-side error flags (bitmask), raised by kernels instead of trapping.
 enum : uint32_t {
   kErrBadToken = 1u,     // a token id outside [0, vocab)

@@ -237,11 +237,34 @@ __device__ __forceinline__ bool dec_body(const DecArgs& a, int cta, int ncta, un
       for (int c = tid; c < K; c += kDecThreads) a.xcopy[static_cast<int64_t>(t) * K + c] = xs[t * K4 + c];
   const int myrow = (lane >> 3) < MT ? (lane >> 3) : MT - 1;  // warp 0: 8 lanes per row
   const float* nproj = nws + (PRO == kDecProPlain ? 0 : K4);    // projection norm weights
-  if (PRO != kDecProPlain) {
-    if (warp == 0) {
+  // rstd of every row into s_r (a __syncthreads must follow): FixedQ510 in the reference's
+  // serial 8-chain order on warp 0 (bit-exact); Float as a block-parallel sum, which
+  // re-associates the row's sum of squares within the Float tolerance
+  __shared__ float s_part[kDecWarps][MT];
+  auto row_rstd = [&] {
+    if (FL) {
+      float part[MT];
+#pragma unroll
+      for (int t = 0; t < MT; ++t) {
+        part[t] = 0.0f;
+        for (int c = tid; c < K; c += kDecThreads) part[t] = __fmaf_rn(xs[t * K4 + c], xs[t * K4 + c], part[t]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) part[t] += __shfl_xor_sync(0xffffffffu, part[t], o);
+        if (lane == 0) s_part[warp][t] = part[t];
+      }
+      __syncthreads();
+      if (tid < MT) {
+        float s = 0.0f;
+        for (int w = 0; w < kDecWarps; ++w) s += s_part[w][tid];
+        s_r[tid] = rstd_of(s, static_cast<float>(K), a.eps);
+      }
+    } else if (warp == 0) {
       const float r = rstd_of(sumsq_exact8(xs + myrow * K4, K, 0xffffffffu), static_cast<float>(K), a.eps);
       if ((lane & 7) == 0 && (lane >> 3) < MT) s_r[lane >> 3] = r;
     }
+  };
+  if (PRO != kDecProPlain) {
+    row_rstd();
     __syncthreads();
     for (int t = 0; t < MT; ++t) {
       const float r1 = s_r[t];
@@ -253,10 +276,7 @@ __device__ __forceinline__ bool dec_body(const DecArgs& a, int cta, int ncta, un
     }
     __syncthreads();
   }
-  if (warp == 0) {
-    const float r = rstd_of(sumsq_exact8(xs + myrow * K4, K, 0xffffffffu), static_cast<float>(K), a.eps);
-    if ((lane & 7) == 0 && (lane >> 3) < MT) s_r[lane >> 3] = r;
-  }
+  row_rstd();
   __syncthreads();
   {
     int local[NP][MT];
@@ -357,12 +377,12 @@ __device__ __forceinline__ bool dec_body(const DecArgs& a, int cta, int ncta, un
             const float yv[16] = {y0.x, y0.y, y0.z, y0.w, y1.x, y1.y, y1.z, y1.w,
                                   y2.x, y2.y, y2.z, y2.w, y3.x, y3.y, y3.z, y3.w};
 #pragma unroll
-            for (int g = 0; g < 4; ++g)
+            for (int g = 0; g < 4; ++g) {
+              const uint32_t m = (wd[w4] >> (2 * g)) & 0x03030303u;  // byte jj: code of k 4g + jj
 #pragma unroll
-              for (int jj = 0; jj < 4; ++jj) {
-                const int code = static_cast<int>((wd[w4] >> (8 * jj + 2 * g)) & 3u);
-                accf[j][t] = __fmaf_rn(yv[4 * g + jj], static_cast<float>(code - 1), accf[j][t]);
-              }
+              for (int jj = 0; jj < 4; ++jj)
+                accf[j][t] = __fmaf_rn(yv[4 * g + jj], ternary_f32(m, jj), accf[j][t]);
+            }
           }
         }
       }

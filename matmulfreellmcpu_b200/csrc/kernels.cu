@@ -19,6 +19,8 @@
 #include <cfloat>
 #include <cstdlib>
 #include <mutex>
+#include <set>
+#include <utility>
 
 namespace mmfree_cuda {
 
@@ -352,13 +354,15 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepArgs a, int mode
   }
 }
 
+// Opts a kernel in to kMaxDynSmem of dynamic shared memory, once per (device, kernel).
 static void raise_smem_limit(const void* fn) {
-  static std::once_flag flags[64];
+  static std::mutex mu;
+  static std::set<std::pair<int, const void*>> done;
   int dev = 0;
   cudaGetDevice(&dev);
-  std::call_once(flags[dev & 63], [&] {
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.insert({dev, fn}).second)
     cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
-  });
 }
 
 cudaError_t launch_prep(const PrepArgs& a, cudaStream_t s) {
@@ -524,12 +528,9 @@ __global__ void __launch_bounds__(kMatmulThreads) matmul_float_kernel(MatmulArgs
         for (int q4 = 0; q4 < 4; ++q4) {
           const float4 y = __ldg(yp + 4 * w4 + q4);
           const float yv[4] = {y.x, y.y, y.z, y.w};
+          const uint32_t m = (wd[w4] >> (2 * q4)) & 0x03030303u;  // byte e: weight 4 q4 + e
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int i = 4 * q4 + e;  // weight i of the 16 in word w4
-            const int code = static_cast<int>((wd[w4] >> (8 * (i & 3) + 2 * (i >> 2))) & 3u);
-            acc[mi] = __fmaf_rn(__int2float_rn(code - 1), yv[e], acc[mi]);
-          }
+          for (int e = 0; e < 4; ++e) acc[mi] = __fmaf_rn(ternary_f32(m, e), yv[e], acc[mi]);
         }
       }
     }
@@ -1067,6 +1068,185 @@ cudaError_t launch_argmax_at(int64_t* ids, int64_t stride, int64_t* pos, unsigne
                              const float* logits, int B, int V, int ld, cudaStream_t s, bool pdl) {
   if (B == 0) return cudaSuccess;
   return launch_k(argmax_at_kernel, dim3(B), dim3(1024), 0, s, pdl, ids, stride, pos, done, logits, V, ld);
+}
+
+// ------------------------------------------------------------------------------ sampling
+// Temperature / top-k sampling of one logits row per CTA (hgrn_model.cpp:274-300, :382-405):
+// the k highest logits are the candidates (ties at the k-th value go to the lower index),
+// p_j = exp((l_j - max) / temperature) in float (computed as a double exp rounded to float),
+// summed in double, and the first candidate in ascending index order whose running sum
+// reaches u * sum is drawn, u being the stream's uniform for this position (drawn on the host
+// from the stream's mt19937_64, as the reference draws it). With k = V the candidates are in
+// the reference's own order (all of them, ascending), so the draw is the reference's.
+constexpr int kSampleThreads = 1024;
+
+__device__ __forceinline__ uint32_t order_key(float v) {  // monotone in v; NaN lowest
+  if (isnan(v)) return 0u;
+  const uint32_t u = __float_as_uint(v);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+template <class T>
+__device__ __forceinline__ T block_excl_scan(T v, T* sh, T& total) {  // 1024 threads
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  T x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const T y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) sh[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    T w = sh[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const T y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    sh[lane] = w;
+  }
+  __syncthreads();
+  total = sh[31];
+  const T before = warp ? sh[warp - 1] : T(0);
+  __syncthreads();
+  return before + x - v;
+}
+
+__global__ void __launch_bounds__(kSampleThreads) sample_at_kernel(
+    int64_t* __restrict__ ids, int64_t stride, int64_t* pos, unsigned* done, int advance, int row0,
+    const float* __restrict__ logits, int V, int ld, const double* __restrict__ uni,
+    int64_t ustride, float temperature, int top_k) {
+  grid_dep_launch();
+  grid_dep_wait();
+  extern __shared__ __align__(16) float s_l[];  // the row, V floats
+  __shared__ uint32_t s_hist[256];
+  __shared__ double s_d[32];
+  __shared__ int s_i[32];
+  __shared__ uint32_t s_u[4];
+  __shared__ int s_pick;
+  const int tid = threadIdx.x, b = row0 + blockIdx.x;
+  const float* lg = logits + static_cast<int64_t>(blockIdx.x) * ld;
+  for (int j = tid; j < V; j += kSampleThreads) s_l[j] = lg[j];
+  if (tid == 0) s_pick = 0x7fffffff;
+  __syncthreads();
+  // candidates: keys above the k-th largest key, plus the first (k - above) equal to it
+  const int k = (top_k > 0 && top_k < V) ? top_k : V;
+  uint32_t kth = 0;  // every key >= 0: all candidates when k == V
+  int above = 0;
+  if (k < V) {
+    uint32_t prefix = 0, mask = 0;
+    int want = k;  // rank (1-based, from the top) of the k-th largest within the prefix class
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      for (int i = tid; i < 256; i += kSampleThreads) s_hist[i] = 0;
+      __syncthreads();
+      for (int j = tid; j < V; j += kSampleThreads) {
+        const uint32_t key = order_key(s_l[j]);
+        if ((key & mask) == prefix) atomicAdd(&s_hist[(key >> shift) & 255u], 1u);
+      }
+      __syncthreads();
+      if (tid == 0) {
+        uint32_t acc = 0;
+        int d = 255;
+        for (; d > 0; --d) {
+          if (acc + s_hist[d] >= static_cast<uint32_t>(want)) break;
+          acc += s_hist[d];
+        }
+        s_u[0] = static_cast<uint32_t>(d);
+        s_u[1] = acc;
+      }
+      __syncthreads();
+      prefix |= s_u[0] << shift;
+      mask |= 255u << shift;
+      want -= static_cast<int>(s_u[1]);
+      above += static_cast<int>(s_u[1]);
+      __syncthreads();
+    }
+    kth = prefix;
+  }
+  const int need_eq = k - above;  // equal keys to take, lowest indices first
+  // maximum over the candidates = the maximum of the row (the top element is a candidate)
+  float mx = -INFINITY;
+  for (int j = tid; j < V; j += kSampleThreads) mx = fmaxf(mx, s_l[j]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((tid & 31) == 0) s_d[tid >> 5] = mx;
+  __syncthreads();
+  if (tid < 32) {
+    float m = static_cast<float>(s_d[tid]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (tid == 0) s_d[0] = m;
+  }
+  __syncthreads();
+  const float maxl = static_cast<float>(s_d[0]);
+  __syncthreads();
+  // each thread owns a contiguous chunk of indices: ranks of equal keys, then p and sums
+  const int per = (V + kSampleThreads - 1) / kSampleThreads;
+  const int j0 = tid * per, j1 = min(V, j0 + per);
+  int eq_local = 0;
+  for (int j = j0; j < j1; ++j) eq_local += order_key(s_l[j]) == kth;
+  int eq_total;
+  int eq_before = block_excl_scan<int>(eq_local, s_i, eq_total);
+  double part = 0.0;
+  for (int j = j0; j < j1; ++j) {
+    const uint32_t key = order_key(s_l[j]);
+    bool cand = key > kth;
+    if (key == kth) cand = eq_before++ < need_eq;
+    float p = 0.0f;
+    if (cand) p = __double2float_rn(exp(static_cast<double>(__fdiv_rn(__fsub_rn(s_l[j], maxl), temperature))));
+    s_l[j] = cand ? p : -1.0f;  // candidate weights (p >= 0), -1 marks the others
+    part += static_cast<double>(p);
+  }
+  __syncthreads();
+  double sum;
+  const double before = block_excl_scan<double>(part, s_d, sum);
+  const double r = uni[static_cast<int64_t>(b) * ustride + (*pos + 1)] * sum;
+  // first candidate whose running sum reaches r; else the last candidate
+  double acc = before;
+  int last_cand = -1;
+  for (int j = j0; j < j1; ++j) {
+    const float p = s_l[j];
+    if (p < 0.0f) continue;
+    last_cand = j;
+    acc += static_cast<double>(p);
+    if (r <= acc) {
+      atomicMin(&s_pick, j);
+      break;
+    }
+  }
+  __syncthreads();
+  int lc = last_cand;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) lc = max(lc, __shfl_xor_sync(0xffffffffu, lc, o));
+  if ((tid & 31) == 0) s_i[tid >> 5] = lc;
+  __syncthreads();
+  if (tid == 0) {
+    int l = -1;
+    for (int w = 0; w < kSampleThreads / 32; ++w) l = max(l, s_i[w]);
+    const int chosen = s_pick != 0x7fffffff ? s_pick : max(l, 0);
+    const int64_t p = *pos;
+    ids[b * stride + p + 1] = chosen;
+    if (advance) {
+      __threadfence();
+      if (atomicAdd(done, 1u) == gridDim.x - 1) {  // last block: advance the position
+        *done = 0;
+        *pos = p + 1;
+      }
+    }
+  }
+}
+
+cudaError_t launch_sample_at(int64_t* ids, int64_t stride, int64_t* pos, unsigned* done,
+                             bool advance, int row0, const float* logits, int B, int V, int ld,
+                             const double* uni, int64_t ustride, float temperature, int top_k,
+                             cudaStream_t s, bool pdl) {
+  if (B == 0) return cudaSuccess;
+  const size_t smem = static_cast<size_t>(V) * sizeof(float);
+  if (smem > kMaxDynSmem || !(temperature > 0.0f)) return cudaErrorInvalidValue;
+  if (smem > 48 * 1024) raise_smem_limit(reinterpret_cast<const void*>(sample_at_kernel));
+  return launch_k(sample_at_kernel, dim3(B), dim3(kSampleThreads), smem, s, pdl, ids, stride, pos,
+                  done, advance ? 1 : 0, row0, logits, V, ld, uni, ustride, temperature, top_k);
 }
 
 __global__ void embed_at_kernel(float* __restrict__ h, const float* __restrict__ emb,

@@ -187,6 +187,16 @@ cudaError_t launch_embed(float* h, const float* emb, const int64_t* ids, int T, 
 cudaError_t launch_argmax(int64_t* ids, const float* logits, int M, int V, int ld,
                           cudaStream_t s);
 
+// Temperature / top-k sampling (hgrn_model.cpp:274-300): row i of logits [B][ld] (V used)
+// draws for stream row0 + i into ids[(row0 + i) * stride + *pos + 1] with the uniform
+// uni[(row0 + i) * ustride + *pos + 1]; with `advance`, the last block advances *pos. The k
+// highest logits are the candidates (ties to the lower index), walked in ascending index
+// order; temperature > 0.
+cudaError_t launch_sample_at(int64_t* ids, int64_t stride, int64_t* pos, unsigned* done,
+                             bool advance, int row0, const float* logits, int B, int V, int ld,
+                             const double* uni, int64_t ustride, float temperature, int top_k,
+                             cudaStream_t s, bool pdl = false);
+
 // Device-resident decode loop helpers. Stream b's token at position *pos lives at
 // ids[b * stride + *pos]. embed_at gathers those B rows; argmax_at writes the greedy pick of
 // logits row b to ids[b * stride + *pos + 1] and the last block to finish advances *pos.

@@ -78,6 +78,8 @@ Model::Model(const std::string& blob_path, int device, bool fixed, int frac_bits
     persist_ok_ = cenv && cenv[0] == '1';
     const char* menv = std::getenv("MMFREE_MIX_IN_PREP");
     mix_prep_ok_ = !(menv && menv[0] == '0');
+    const char* senv = std::getenv("MMFREE_HOST_SAMPLING");
+    host_sampling_ = senv && senv[0] == '1';
   }
   CK(cudaMalloc(&dec_part_v_, sizeof(float) * kDecMaxRows * 2 * 1024));
   CK(cudaMalloc(&dec_part_i_, sizeof(int) * kDecMaxRows * 2 * 1024));
@@ -241,6 +243,7 @@ Model::~Model() {
   cudaFree(persist_tab_);
   cudaFree(tp_ws_);
   cudaFree(chunk_ws_);
+  cudaFree(uni_);
   tp_.reset();
   if (pinned_) cudaFreeHost(pinned_);
   if (stream_) cudaStreamDestroy(stream_);
@@ -712,7 +715,19 @@ void Model::head(const float* rows, int M) {
 }
 
 void Model::decode_graph_step(int B, int64_t stride) {
-  if (fused_decode(B) && persist_ok_ && persist_b_ == B && persist_stride_ == stride &&
+  auto pick = [&] {  // the next token of every stream: sampled, or the greedy argmax
+    if (samp_) {
+      timed(kClsArgmax, 4.0 * B * V_, 0, [&] {
+        CK(launch_sample_at(loop_ids_, stride, pos_, done_, true, 0, logits_, B, V_, V_, uni_, stride,
+                            samp_->temperature, samp_->top_k, stream_, pdl_));
+      });
+    } else {
+      timed(kClsArgmax, 4.0 * B * V_, 0, [&] {
+        CK(launch_argmax_at(loop_ids_, stride, pos_, done_, logits_, B, V_, V_, stream_, pdl_));
+      });
+    }
+  };
+  if (!samp_ && fused_decode(B) && persist_ok_ && persist_b_ == B && persist_stride_ == stride &&
       persist_grid_ > 0) {
     // the whole step in one cooperative launch (table prepared by persist_ready)
     timed(kClsStep, static_cast<double>(packed_bytes_), 0, [&] {
@@ -725,14 +740,13 @@ void Model::decode_graph_step(int B, int64_t stride) {
     CK(launch_embed_at(h_, emb_, loop_ids_, stride, pos_, B, H_, V_, err_, stream_, pdl_));
   });
   if (fused_decode(B)) {
-    fused_step(B, stride);
+    fused_step(B, stride);  // with samp_ its head phase writes logits only
+    if (samp_) pick();
     return;
   }
   layers(B, 1, B, [&](int l) { return state_ + static_cast<size_t>(l) * B * H_; });
   head(h_, B);
-  timed(kClsArgmax, 4.0 * B * V_, 0, [&] {
-    CK(launch_argmax_at(loop_ids_, stride, pos_, done_, logits_, B, V_, V_, stream_, pdl_));
-  });
+  pick();
 }
 
 bool Model::fused_decode(int B) const {
@@ -821,7 +835,7 @@ std::vector<DecArgs> Model::dec_phases(int B, int64_t stride) {
   hd.K = H_;
   hd.N = V_;
   hd.out[0] = logits_;
-  hd.ids = loop_ids_;
+  hd.ids = samp_ ? nullptr : loop_ids_;  // sampled steps: logits only, sample_at follows
   hd.stride = stride;
   hd.pos = pos_;
   hd.done = done_;
@@ -832,7 +846,7 @@ std::vector<DecArgs> Model::dec_phases(int B, int64_t stride) {
 }
 
 bool Model::persist_ready(int B, int64_t stride) {
-  if (!fused_decode(B) || !persist_ok_) return false;
+  if (!fused_decode(B) || !persist_ok_ || samp_) return false;
   if (persist_b_ == B && persist_stride_ == stride) return persist_grid_ > 0;
   std::vector<DecArgs> ph = dec_phases(B, stride);
   // the first phase gathers its rows from the embedding table (and writes h for o_proj)
@@ -970,6 +984,27 @@ std::vector<int64_t> Model::generate(const int64_t* ids, size_t n, size_t new_to
 
   const int64_t stride = static_cast<int64_t>(new_tokens);
   loop_ids(new_tokens);
+  if (samp.temperature > 0.0f && !host_sampling_) {
+    // Sampling on the device: the uniforms the reference's emit() draws, one per token
+    // (hgrn_model.cpp:263-264, :292), made here up front and uploaded once.
+    std::mt19937_64 rng(samp.seed);
+    std::uniform_real_distribution<double> uni(0.0, 1.0);
+    std::vector<double> u(new_tokens);
+    for (double& v : u) v = uni(rng);
+    upload_uniforms(u);
+    SampScope scope(this, &samp);
+    const int64_t minus1 = -1;
+    CK(cudaMemcpyAsync(pos_, &minus1, 8, cudaMemcpyHostToDevice, stream_));
+    sample_first(1, 0, stride, false);
+    int64_t first = 0;
+    CK(cudaMemcpyAsync(&first, loop_ids_, 8, cudaMemcpyDeviceToHost, stream_));
+    CK(cudaStreamSynchronize(stream_));
+    check_errors();
+    std::vector<std::vector<int64_t>> st = {stream};
+    st[0].push_back(first);
+    if (first != eos_id && new_tokens > 1) sampled_loop(1, stride, new_tokens - 1, eos_id, st);
+    return st[0];
+  }
   if (samp.temperature > 0.0f) {
     // Host sampling: one logits row back per step, same draws as the reference.
     std::mt19937_64 rng(samp.seed);
@@ -1050,6 +1085,14 @@ void Model::forward(const int64_t* ids, size_t T, float* logits, bool last_row_o
 }
 
 void Model::serve_begin(const std::vector<std::vector<int64_t>>& prompts, int64_t* first_ids) {
+  prefill_runs(prompts, first_ids, 0);
+  const size_t B = prompts.size();
+  serve_b_ = static_cast<int>(B);
+  serve_last_.assign(first_ids, first_ids + B);
+}
+
+void Model::prefill_runs(const std::vector<std::vector<int64_t>>& prompts, int64_t* first_ids,
+                         int64_t stride) {
   CK(cudaSetDevice(device_));
   const size_t B = prompts.size();
   if (B == 0) throw std::invalid_argument("serve: no prompts");
@@ -1085,13 +1128,80 @@ void Model::serve_begin(const std::vector<std::vector<int64_t>>& prompts, int64_
     CK(cudaMemcpy2DAsync(hl_, H_ * 4, h_ + (T0 - 1) * H_, T0 * H_ * 4, H_ * 4, G,
                          cudaMemcpyDeviceToDevice, stream_));
     head(hl_, static_cast<int>(G));
+    if (samp_) {
+      sample_first(static_cast<int>(G), static_cast<int>(b0), stride, false);
+      continue;
+    }
     CK(launch_argmax(ids_, logits_, static_cast<int>(G), V_, V_, stream_));
     CK(cudaMemcpyAsync(first_ids + b0, ids_, G * 8, cudaMemcpyDeviceToHost, stream_));
     CK(cudaStreamSynchronize(stream_));
   }
   check_errors();
-  serve_b_ = static_cast<int>(B);
-  serve_last_.assign(first_ids, first_ids + B);
+}
+
+void Model::upload_uniforms(const std::vector<double>& u) {
+  if (u.size() > uni_elems_) {
+    CK(cudaStreamSynchronize(stream_));
+    cudaFree(uni_);
+    uni_ = nullptr;
+    uni_elems_ = 0;
+    CK(cudaMalloc(&uni_, u.size() * sizeof(double)));
+    uni_elems_ = u.size();
+  }
+  CK(cudaMemcpyAsync(uni_, u.data(), u.size() * sizeof(double), cudaMemcpyHostToDevice, stream_));
+  CK(cudaStreamSynchronize(stream_));  // u is a host vector that the caller may release
+}
+
+// The sampled first token of streams row0 .. row0 + B - 1 from logits_ rows 0 .. B - 1,
+// written at loop_ids_[b * stride + *pos_ + 1] (*pos_ is -1 here).
+void Model::sample_first(int B, int row0, int64_t stride, bool advance) {
+  CK(launch_sample_at(loop_ids_, stride, pos_, done_, advance, row0, logits_, B, V_, V_, uni_, stride,
+                      samp_->temperature, samp_->top_k, stream_));
+}
+
+// `steps` sampled lockstep steps of B streams from the tokens at position 0 of loop_ids_,
+// graph-replayed on the device; ids are read back every 32 steps to stop once every stream
+// has emitted eos_id (a finished stream keeps its slot; its later ids are dropped, as the
+// reference drops them, hgrn_model.cpp:432-452).
+void Model::sampled_loop(int B, int64_t stride, size_t steps, int64_t eos_id,
+                         std::vector<std::vector<int64_t>>& streams) {
+  const int64_t zero = 0;
+  CK(cudaMemcpyAsync(pos_, &zero, 8, cudaMemcpyHostToDevice, stream_));
+  drop_graph();  // the graph bakes the sampling parameters: capture one for this call
+  CK(cudaStreamSynchronize(stream_));
+  cudaGraph_t g;
+  CK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+  decode_graph_step(B, stride);
+  CK(cudaStreamEndCapture(stream_, &g));
+  CK(cudaGraphInstantiate(&graph_, g, 0));
+  cudaGraphDestroy(g);
+  graph_b_ = B;
+  graph_stride_ = -stride;  // never matches a greedy call's key
+  pinned(static_cast<size_t>(stride) * B);
+  std::vector<char> done(B, 0);
+  for (int b = 0; b < B; ++b) done[b] = streams[b].back() == eos_id;
+  size_t s = 0;
+  const size_t chunk = eos_id < 0 ? steps : 32;
+  while (s < steps) {
+    const size_t n = std::min(chunk, steps - s);
+    for (size_t i = 0; i < n; ++i) CK(cudaGraphLaunch(graph_, stream_));
+    CK(cudaMemcpyAsync(pinned_, loop_ids_, static_cast<size_t>(stride) * B * 8, cudaMemcpyDeviceToHost,
+                       stream_));
+    CK(cudaStreamSynchronize(stream_));
+    bool all_done = true;
+    for (int b = 0; b < B; ++b) {
+      for (size_t t = s + 1; t <= s + n && !done[b]; ++t) {
+        const int64_t id = pinned_[static_cast<size_t>(b) * stride + t];
+        streams[b].push_back(id);
+        if (id == eos_id) done[b] = 1;
+      }
+      all_done = all_done && done[b];
+    }
+    s += n;
+    if (all_done) break;
+  }
+  check_errors();
+  drop_graph();
 }
 
 void Model::serve_step(const int64_t* in_ids, int64_t* out_ids) {
@@ -1173,6 +1283,28 @@ std::vector<std::vector<int64_t>> Model::generate_serve(
   std::vector<std::vector<int64_t>> streams = prompts;
   if (B == 0) return streams;
   std::vector<int64_t> first(B);
+  if (samp.temperature > 0.0f && !host_sampling_) {
+    // device-sampled lockstep loop: stream b's uniforms come from its mt19937_64 seeded
+    // seed + b (hgrn_model.cpp:368-373), one per token, made up front
+    const int64_t stride = static_cast<int64_t>(std::max<size_t>(new_tokens, 1));
+    std::vector<double> u(B * static_cast<size_t>(stride));
+    std::uniform_real_distribution<double> uni(0.0, 1.0);
+    for (size_t b = 0; b < B; ++b) {
+      std::mt19937_64 rng(samp.seed + b);
+      for (int64_t t = 0; t < stride; ++t) u[b * stride + t] = uni(rng);
+    }
+    upload_uniforms(u);
+    loop_ids(B * static_cast<size_t>(stride));
+    SampScope scope(this, &samp);
+    const int64_t minus1 = -1;
+    CK(cudaMemcpyAsync(pos_, &minus1, 8, cudaMemcpyHostToDevice, stream_));
+    prefill_runs(prompts, nullptr, stride);  // first tokens sampled into loop_ids_[b * stride]
+    CK(cudaMemcpy2DAsync(first.data(), 8, loop_ids_, stride * 8, 8, B, cudaMemcpyDeviceToHost, stream_));
+    CK(cudaStreamSynchronize(stream_));
+    for (size_t b = 0; b < B; ++b) streams[b].push_back(first[b]);
+    if (new_tokens > 1) sampled_loop(static_cast<int>(B), stride, new_tokens - 1, eos_id, streams);
+    return streams;
+  }
   if (samp.temperature > 0.0f) {
     // host-sampled lockstep loop (hgrn_model.cpp:368-406): per-stream RNG seeded seed + b,
     // prefill stream by stream, then one batched step per token.

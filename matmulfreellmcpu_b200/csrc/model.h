@@ -199,6 +199,32 @@ class Model {
   int serve_b_ = 0;                // active serving session batch (0 = none)
   std::vector<int64_t> serve_last_;
 
+  // Sampled decoding on the device: while samp_ is set, decode steps end in sample_at instead
+  // of the greedy argmax, drawing with the per-stream uniforms uni_ [B][stride] (drawn on the
+  // host from each stream's mt19937_64). MMFREE_HOST_SAMPLING=1 keeps the host sampler.
+  const Sampling* samp_ = nullptr;
+  bool host_sampling_ = false;
+  struct SampScope {  // samp_ for one sampled call; its decode graph is dropped on the way out
+    Model* m;
+    SampScope(Model* mm, const Sampling* s) : m(mm) {
+      m->drop_graph();
+      m->samp_ = s;
+    }
+    ~SampScope() {
+      m->samp_ = nullptr;
+      m->drop_graph();
+    }
+  };
+  double* uni_ = nullptr;
+  size_t uni_elems_ = 0;
+  void upload_uniforms(const std::vector<double>& u);
+  void sample_first(int B, int row0, int64_t stride, bool advance);  // from logits_ rows
+  // prefill of every prompt (runs of equal length batched); first tokens greedy into ids_
+  // (first_ids on the host) or, with samp_, sampled into loop_ids_[b * stride]
+  void prefill_runs(const std::vector<std::vector<int64_t>>& prompts, int64_t* first_ids,
+                    int64_t stride);
+  void sampled_loop(int B, int64_t stride, size_t steps, int64_t eos_id,
+                    std::vector<std::vector<int64_t>>& streams);
   // Float-mode prefill: workspace of the chunked scan (nullptr: the exact serial scan)
   void* chunk_ws(int nseq, int len, int H);
   void* chunk_ws_ = nullptr;

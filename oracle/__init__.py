@@ -299,6 +299,12 @@ class Reference:
     def set_threads(self, n: int) -> None:
         self.lib.ref_set_threads(n)
 
+    def uniforms(self, seed: int, n: int) -> np.ndarray:
+        """The first n uniforms the reference's sampler draws for a stream seeded `seed`."""
+        out = np.empty(n, np.float64)
+        self.lib.ref_uniforms(C.c_uint64(seed), SZ(n), out.ctypes.data_as(VP))
+        return out
+
     def sumsq(self, x):
         x = _f(x)
         return np.float32(self.lib.ref_sumsq(x, x.size))

@@ -17,6 +17,7 @@
 #include "mmfree/weights.hpp"
 
 #include <chrono>
+#include <random>
 #include <cstdint>
 #include <cstring>
 #include <memory>
@@ -276,6 +277,15 @@ int ref_model_bench_serve(void* hp, std::size_t B, const std::int64_t* const* pr
     g_err = e.what();
     return -1;
   }
+}
+
+// The uniforms the reference's sampler draws for a stream seeded `seed`, in order
+// (std::mt19937_64 + std::uniform_real_distribution<double>(0, 1), hgrn_model.cpp:263-264,
+// :292), from the same C++ library the reference is built with.
+void ref_uniforms(std::uint64_t seed, std::size_t n, double* out) {
+  std::mt19937_64 rng(seed);
+  std::uniform_real_distribution<double> uni(0.0, 1.0);
+  for (std::size_t i = 0; i < n; ++i) out[i] = uni(rng);
 }
 
 }  // extern "C"

@@ -256,23 +256,89 @@ def test_eos_stops_streams(models):
     assert np.array_equal(streams[0], cut)
 
 
-def test_sampling_matches_reference(models, blob_cache):
-    """temperature/top-k sampling draws the same tokens as the reference for the same seed."""
+def _reference():
     import oracle
     if not os.path.exists(oracle.REF_SO):
         pytest.fail("prebuilt reference library missing (oracle/_ref travels with the repo)")
-    R = oracle.Reference()
-    path = B.cached_blob("small", 0, blob_cache)
-    rm = R.model(path, 1)
+    return oracle.Reference()
+
+
+def test_device_sampling_matches_reference(models, blob_cache):
+    """Full-vocabulary temperature sampling on the device draws the reference's tokens for the
+    same seed: its candidates are every token in index order, as the reference's are
+    (hgrn_model.cpp:274-300), and the uniforms are the reference's own mt19937_64 draws."""
+    R = _reference()
+    rm = R.model(B.cached_blob("small", 0, blob_cache), 1)
     m = models("small", "fixed")
     p = B.seeded_ids(6, 9, 2048)
-    for temp, k, seed in ((0.8, 0, 1), (1.5, 40, 7)):
-        assert np.array_equal(m.generate(p, 12, temperature=temp, top_k=k, seed=seed),
-                              rm.generate(p, 12, temperature=temp, top_k=k, seed=seed))
-        ps = [p, B.seeded_ids(4, 10, 2048)]
-        for a, b in zip(m.generate_serve(ps, 6, temperature=temp, top_k=k, seed=seed),
-                        rm.generate_serve(ps, 6, temperature=temp, top_k=k, seed=seed)):
+    ps = [p, B.seeded_ids(4, 10, 2048), B.seeded_ids(4, 11, 2048)]
+    for temp, seed in ((0.8, 1), (1.5, 7), (0.3, 3)):
+        assert np.array_equal(m.generate(p, 12, temperature=temp, seed=seed),
+                              rm.generate(p, 12, temperature=temp, seed=seed))
+        for a, b in zip(m.generate_serve(ps, 6, temperature=temp, seed=seed),
+                        rm.generate_serve(ps, 6, temperature=temp, seed=seed)):
             assert np.array_equal(a, b)
+    # eos stops a stream (its slot stays, its later draws are dropped) as in the reference
+    s = rm.generate_serve(ps, 8, temperature=1.5, seed=7)
+    eos = int(s[1][len(ps[1]) + 2])
+    for a, b in zip(m.generate_serve(ps, 8, eos_id=eos, temperature=1.5, seed=7),
+                    rm.generate_serve(ps, 8, eos=eos, temperature=1.5, seed=7)):
+        assert np.array_equal(a, b)
+    rm.close()
+
+
+def _device_rule(lg, u, temp, k):
+    """The device sampler's rule on the host: the k highest logits (ties to the lower index)
+    in ascending index order, float p = exp((l - max) / temperature), double running sum,
+    the first candidate whose sum reaches u * total."""
+    lg = np.asarray(lg, np.float32)
+    V = lg.size
+    k = k if 0 < k < V else V
+    cand = np.sort(np.lexsort((np.arange(V), -lg))[:k])
+    z = ((lg[cand] - lg[cand].max()) / np.float32(temp)).astype(np.float32)
+    pr = np.exp(z.astype(np.float64)).astype(np.float32).astype(np.float64)
+    acc = np.cumsum(pr)
+    j = int(np.searchsorted(acc, u * acc[-1], side="left"))
+    return int(cand[min(j, cand.size - 1)])
+
+
+def test_device_top_k_sampling_follows_its_rule(models, blob_cache):
+    """With top_k the reference walks its candidates in std::nth_element's order, which no
+    other implementation reproduces; the device walks them in ascending index order (the same
+    distribution). Every drawn token is checked against that rule applied to the logits of
+    its position and the stream's reference uniform."""
+    R = _reference()
+    m = models("small", "fixed")
+    p = B.seeded_ids(6, 9, 2048)
+    temp, k, seed = 1.5, 40, 7
+    s = m.generate(p, 12, temperature=temp, top_k=k, seed=seed)
+    u = R.uniforms(seed, 12)
+    for t in range(12):
+        assert s[p.size + t] == _device_rule(m.forward_last(s[:p.size + t]), u[t], temp, k)
+    ps = [p, B.seeded_ids(4, 10, 2048)]
+    for b, sb in enumerate(m.generate_serve(ps, 5, temperature=temp, top_k=k, seed=seed)):
+        ub = R.uniforms(seed + b, 5)
+        n0 = ps[b].size
+        for t in range(5):
+            assert sb[n0 + t] == _device_rule(m.forward_last(sb[:n0 + t]), ub[t], temp, k)
+
+
+def test_host_sampling_matches_reference_with_top_k(cuda, blob_cache, monkeypatch):
+    """MMFREE_HOST_SAMPLING=1 samples on the host with the reference's own algorithm
+    (nth_element order included): draw-identical with top_k too."""
+    monkeypatch.setenv("MMFREE_HOST_SAMPLING", "1")
+    R = _reference()
+    path = B.cached_blob("small", 0, blob_cache)
+    rm = R.model(path, 1)
+    p = B.seeded_ids(6, 9, 2048)
+    with api.Model(path, "fixed") as m:
+        for temp, k, seed in ((0.8, 0, 1), (1.5, 40, 7)):
+            assert np.array_equal(m.generate(p, 12, temperature=temp, top_k=k, seed=seed),
+                                  rm.generate(p, 12, temperature=temp, top_k=k, seed=seed))
+            ps = [p, B.seeded_ids(4, 10, 2048)]
+            for a, b in zip(m.generate_serve(ps, 6, temperature=temp, top_k=k, seed=seed),
+                            rm.generate_serve(ps, 6, temperature=temp, top_k=k, seed=seed)):
+                assert np.array_equal(a, b)
     rm.close()
 
 
