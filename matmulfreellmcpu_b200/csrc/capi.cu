@@ -1,6 +1,7 @@
 // capi.cu -- the extern "C" boundary of libmmfree_cuda.so (declared in include/mmfree_cuda.h).
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -145,6 +146,13 @@ void check_dims(size_t rows, size_t in_dim, size_t out_dim) {
   need(out_dim <= (size_t(1) << 30) && rows <= (size_t(1) << 30), "dimension too large");
 }
 
+int sm_count_of_device() {
+  int dev = 0, n = 0;
+  ck(cudaGetDevice(&dev), "cudaGetDevice");
+  ck(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev), "cudaDeviceGetAttribute");
+  return n > 0 ? n : 148;
+}
+
 // One or more BitLinear projections sharing x (bitlinear / bitlinear_cluster).
 void run_bitlinear(int k, float* const* outs, const float* x, const float* const* nws,
                    const void* const* ws, const float* scales, size_t rows, size_t in_dim,
@@ -155,6 +163,25 @@ void run_bitlinear(int k, float* const* outs, const float* x, const float* const
   need(x != nullptr, "null x");
   for (int j = 0; j < k; ++j) need(outs[j] && nws[j] && ws[j], "null output, norm weight or weights");
   if (rows == 0) return;
+  if (k == 1 && rows <= static_cast<size_t>(kDecMaxRows) && !norm_out && !acc_out) {
+    // a few rows: one fused launch (each CTA normalises and quantises the rows itself, its
+    // first weight unit staged in shared memory), the batch-1 decode kernel of the model
+    DecArgs d;
+    d.x = x;
+    d.normw[0] = nws[0];
+    d.w[0] = ws[0];
+    d.M = static_cast<int>(rows);
+    d.K = static_cast<int>(in_dim);
+    d.N = static_cast<int>(out_dim);
+    d.eps = eps;
+    d.qs = static_cast<float>(1u << frac_bits);
+    d.scale[0] = fixed ? 1.0f / (d.qs * scales[0]) : 1.0f / scales[0];
+    d.out[0] = outs[0];
+    d.fl = fixed ? 0 : 1;
+    const int grid = std::max(1, std::min(dec_units(d, kDecEpiResid), 2 * sm_count_of_device()));
+    if (launch_dec(d, kDecProPlain, kDecEpiResid, grid, st, false) == cudaSuccess) return;
+    (void)cudaGetLastError();  // shape the fused kernel cannot stage: the general path below
+  }
   const size_t kp = static_cast<size_t>(padded_k(static_cast<int64_t>(in_dim)));
   const size_t per = fixed ? a256(2 * rows * kp) + a256(rows * 4) : a256(rows * kp * 4);
   char* base = scratch(static_cast<size_t>(k) * per);

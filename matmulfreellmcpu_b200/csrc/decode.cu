@@ -479,7 +479,7 @@ __device__ __forceinline__ bool dec_body(const DecArgs& a, int cta, int ncta, un
         } else if (EPI == kDecEpiResid) {
           if (n < a.N) {
             const int64_t e = static_cast<int64_t>(t) * a.N + n;
-            a.out[0][e] = __fadd_rn(__ldcg(a.resid + e), val[0][t]);
+            a.out[0][e] = a.resid ? __fadd_rn(__ldcg(a.resid + e), val[0][t]) : val[0][t];
           }
         } else if (EPI == kDecEpiSwiglu) {
           const int I = a.N / 2;

@@ -47,7 +47,9 @@ def test_bitlinear_timeout_is_reported_then_cleared(cuda, orc, M):
     wp = api.repack_ternary(_dev(wq, cuda))
     api.kernel_status()  # nothing pending from earlier tests
     with _GiveUp():
-        api.bitlinear(xd, nwd, wp, 20.0, N)  # queued: the failure happens on the device
+        # queued: the failure happens on the device (asking for the accumulators keeps a
+        # few-row call on the prologue + matmul kernels, whose row wait this gives up)
+        api.bitlinear(xd, nwd, wp, 20.0, N, want_acc=True)
     with pytest.raises(_lib.MmfreeError) as e:
         api.kernel_status()
     assert e.value.code == _lib.E_TIMEOUT

@@ -1,6 +1,7 @@
 """One rank of the tensor-parallel GPU check (launched by tests/test_gpu_tp.py through
 torch.distributed.run, one process per GPU). Every rank opens a TP handle of each blob and a
-single-GPU handle, runs the same prefills on both and reports, as one JSON line per rank:
+single-GPU handle, runs the same prefills on both and reports, as one JSON file per rank
+($MMFREE_TP_OUT/rank<r>.json):
   * FixedQ510: bit equality of the last-position logits and of the first ids of a batched
     prefill (serve_begin), TP against one GPU; with the configuration-4 fixture, against the
     reference's own logits;
@@ -73,7 +74,8 @@ def main():
             out[f"{name}/{mode}"] = r
     dist.barrier()
     dist.destroy_process_group()
-    print("TPRESULT " + json.dumps(out), flush=True)
+    with open(os.path.join(os.environ["MMFREE_TP_OUT"], f"rank{rank}.json"), "w") as f:
+        json.dump(out, f)
 
 
 if __name__ == "__main__":
