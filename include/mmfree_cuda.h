@@ -218,6 +218,17 @@ int mmfree_cuda_generate(mmfree_cuda_model* m, const int64_t* ids, size_t n,
                          size_t new_tokens, int64_t eos_id, float temperature, int top_k,
                          uint64_t seed, int64_t* out_ids, size_t out_cap, size_t* out_len);
 
+/* Model::generate with its streaming hook (model.hpp:44-50, `on_token`): the same
+ * arguments and results as mmfree_cuda_generate, and on_token(id, ctx) is called on the
+ * calling thread with every generated id in order as soon as the host has it -- each step
+ * when eos_id >= 0 (the step's id is read back to test it), otherwise once the device loop
+ * is done. on_token may be NULL. */
+typedef void (*mmfree_cuda_token_fn)(int64_t id, void* ctx);
+int mmfree_cuda_generate_stream(mmfree_cuda_model* m, const int64_t* ids, size_t n,
+                                size_t new_tokens, int64_t eos_id, float temperature, int top_k,
+                                uint64_t seed, mmfree_cuda_token_fn on_token, void* ctx,
+                                int64_t* out_ids, size_t out_cap, size_t* out_len);
+
 /* Replaces Model::forward (model.hpp:34): logits [T, vocab_size]. */
 int mmfree_cuda_forward(mmfree_cuda_model* m, const int64_t* ids, size_t T, float* logits);
 /* The last row of Model::forward only (what mmfree-cli --logits-out writes, main.cpp:217-224). */

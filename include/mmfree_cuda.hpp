@@ -72,18 +72,21 @@ class Model {
     check(mmfree_cuda_forward(h_, ids, T, logits.data()));
   }
 
-  // Model::generate: prompt + up to new_tokens ids. on_token fires once per generated id
-  // after the call (the device loop does not stop for host callbacks).
+  // Model::generate: prompt + up to new_tokens ids. on_token fires once per generated id, in
+  // order, as soon as the host has it (every step when eos_id >= 0).
   std::vector<std::int64_t> generate(const std::vector<std::int64_t>& ids, std::size_t new_tokens,
                                      std::int64_t eos_id = -1, const Sampling& samp = {},
                                      const std::function<void(std::int64_t)>& on_token = {}) {
     std::vector<std::int64_t> out(ids.size() + new_tokens);
     std::size_t n = 0;
-    check(mmfree_cuda_generate(h_, ids.data(), ids.size(), new_tokens, eos_id, samp.temperature,
-                               samp.top_k, samp.seed, out.data(), out.size(), &n));
+    auto relay = [](std::int64_t id, void* ctx) {
+      (*static_cast<const std::function<void(std::int64_t)>*>(ctx))(id);
+    };
+    check(mmfree_cuda_generate_stream(
+        h_, ids.data(), ids.size(), new_tokens, eos_id, samp.temperature, samp.top_k, samp.seed,
+        on_token ? +relay : nullptr, const_cast<std::function<void(std::int64_t)>*>(&on_token),
+        out.data(), out.size(), &n));
     out.resize(n);
-    if (on_token)
-      for (std::size_t i = ids.size(); i < out.size(); ++i) on_token(out[i]);
     return out;
   }
 

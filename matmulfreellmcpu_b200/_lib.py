@@ -47,6 +47,8 @@ SIGNATURES = {
     "mmfree_cuda_blob_config": (I, [C.c_char_p, VP]),
     "mmfree_cuda_model_weight_bytes": (SZ, [VP]),
     "mmfree_cuda_generate": (I, [VP, VP, SZ, SZ, I64, F, I, U64, VP, SZ, C.POINTER(SZ)]),
+    "mmfree_cuda_generate_stream": (I, [VP, VP, SZ, SZ, I64, F, I, U64, VP, VP, VP, SZ,
+                                        C.POINTER(SZ)]),
     "mmfree_cuda_forward": (I, [VP, VP, SZ, VP]),
     "mmfree_cuda_forward_last": (I, [VP, VP, SZ, VP]),
     "mmfree_cuda_forward_trace": (I, [VP, VP, SZ, VP, VP]),

@@ -86,10 +86,12 @@ CLI_SRC = os.path.join(PKG, "cli", "mmfree_cli.cpp")
 
 def build_cli(force: bool = False) -> str:
     """The CUDA-backed mmfree-cli (host C++ over the C ABI, rpath to the library)."""
-    deps = [CLI_SRC, LIB, os.path.join(INCLUDE, "mmfree_cuda.h"), os.path.join(INCLUDE, "mmfree_cuda.hpp")]
+    srcs = [CLI_SRC, os.path.join(PKG, "cli", "tokenizer.cpp")]
+    deps = srcs + [LIB, os.path.join(PKG, "cli", "tokenizer.hpp"), os.path.join(INCLUDE, "mmfree_cuda.h"),
+                   os.path.join(INCLUDE, "mmfree_cuda.hpp")]
     if force or not os.path.exists(CLI) or os.path.getmtime(CLI) < max(map(os.path.getmtime, deps)):
         cxx = "/usr/bin/g++" if os.path.exists("/usr/bin/g++") else "g++"
-        cmd = [cxx, "-O2", "-std=c++17", "-I" + INCLUDE, CLI_SRC, "-L" + LIBDIR, "-lmmfree_cuda",
+        cmd = [cxx, "-O2", "-std=c++17", "-I" + INCLUDE, *srcs, "-L" + LIBDIR, "-lmmfree_cuda",
                "-Wl,-rpath,$ORIGIN", "-o", CLI]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:

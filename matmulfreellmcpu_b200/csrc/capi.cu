@@ -707,6 +707,23 @@ int mmfree_cuda_generate(mmfree_cuda_model* m, const int64_t* ids, size_t n,
   });
 }
 
+int mmfree_cuda_generate_stream(mmfree_cuda_model* m, const int64_t* ids, size_t n,
+                                size_t new_tokens, int64_t eos_id, float temperature, int top_k,
+                                uint64_t seed, mmfree_cuda_token_fn on_token, void* ctx,
+                                int64_t* out_ids, size_t out_cap, size_t* out_len) {
+  return guard([&] {
+    need(m && ids && out_ids && out_len, "null pointer");
+    need(out_cap >= n + new_tokens, "out_cap < n + new_tokens");
+    Sampling s{temperature, top_k, seed};
+    std::function<void(int64_t)> cb = [&](int64_t id) {
+      if (on_token) on_token(id, ctx);
+    };
+    auto st = m->impl->generate(ids, n, new_tokens, eos_id, s, &cb);
+    std::memcpy(out_ids, st.data(), st.size() * 8);
+    *out_len = st.size();
+  });
+}
+
 int mmfree_cuda_forward(mmfree_cuda_model* m, const int64_t* ids, size_t T, float* logits) {
   return guard([&] {
     need(m && ids && logits, "null pointer");

@@ -966,7 +966,8 @@ struct Sampler {
 }  // namespace
 
 std::vector<int64_t> Model::generate(const int64_t* ids, size_t n, size_t new_tokens,
-                                     int64_t eos_id, const Sampling& samp) {
+                                     int64_t eos_id, const Sampling& samp,
+                                     const std::function<void(int64_t)>* on_token) {
   tp_only_prefill("generate");
   CK(cudaSetDevice(device_));
   if (n == 0) throw std::invalid_argument("generate: empty prompt");
@@ -1002,7 +1003,9 @@ std::vector<int64_t> Model::generate(const int64_t* ids, size_t n, size_t new_to
     check_errors();
     std::vector<std::vector<int64_t>> st = {stream};
     st[0].push_back(first);
-    if (first != eos_id && new_tokens > 1) sampled_loop(1, stride, new_tokens - 1, eos_id, st);
+    if (on_token) (*on_token)(first);
+    if (first != eos_id && new_tokens > 1)
+      sampled_loop(1, stride, new_tokens - 1, eos_id, st, on_token);
     return st[0];
   }
   if (samp.temperature > 0.0f) {
@@ -1021,6 +1024,7 @@ std::vector<int64_t> Model::generate(const int64_t* ids, size_t n, size_t new_to
       CK(cudaStreamSynchronize(stream_));
       const int64_t t = pick(lg.data(), rng);
       stream.push_back(t);
+      if (on_token) (*on_token)(t);
       if (t == eos_id) break;
     }
     check_errors();
@@ -1051,14 +1055,18 @@ std::vector<int64_t> Model::generate(const int64_t* ids, size_t n, size_t new_to
     CK(cudaStreamSynchronize(stream_));
     check_errors();
     stream.insert(stream.end(), pinned_, pinned_ + new_tokens);
+    if (on_token)
+      for (size_t i = 0; i < new_tokens; ++i) (*on_token)(pinned_[i]);
     return stream;
   }
   for (size_t step = 0; step < new_tokens; ++step) {
     if (step > 0) CK(cudaGraphLaunch(graph_, stream_));
     CK(cudaMemcpyAsync(pinned_, loop_ids_ + step, 8, cudaMemcpyDeviceToHost, stream_));
     CK(cudaStreamSynchronize(stream_));
-    stream.push_back(pinned_[0]);
-    if (pinned_[0] == eos_id) break;
+    const int64_t t = pinned_[0];
+    stream.push_back(t);
+    if (on_token) (*on_token)(t);
+    if (t == eos_id) break;
   }
   check_errors();
   return stream;
@@ -1164,7 +1172,8 @@ void Model::sample_first(int B, int row0, int64_t stride, bool advance) {
 // has emitted eos_id (a finished stream keeps its slot; its later ids are dropped, as the
 // reference drops them, hgrn_model.cpp:432-452).
 void Model::sampled_loop(int B, int64_t stride, size_t steps, int64_t eos_id,
-                         std::vector<std::vector<int64_t>>& streams) {
+                         std::vector<std::vector<int64_t>>& streams,
+                         const std::function<void(int64_t)>* on_token) {
   const int64_t zero = 0;
   CK(cudaMemcpyAsync(pos_, &zero, 8, cudaMemcpyHostToDevice, stream_));
   drop_graph();  // the graph bakes the sampling parameters: capture one for this call
@@ -1193,6 +1202,7 @@ void Model::sampled_loop(int B, int64_t stride, size_t steps, int64_t eos_id,
       for (size_t t = s + 1; t <= s + n && !done[b]; ++t) {
         const int64_t id = pinned_[static_cast<size_t>(b) * stride + t];
         streams[b].push_back(id);
+        if (b == 0 && on_token) (*on_token)(id);
         if (id == eos_id) done[b] = 1;
       }
       all_done = all_done && done[b];

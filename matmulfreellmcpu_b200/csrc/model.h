@@ -11,6 +11,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <functional>
 #include <memory>
 #include <random>
 #include <string>
@@ -51,8 +52,12 @@ class Model {
   size_t weight_bytes() const { return packed_bytes_; }
 
   // model.hpp:36-50 / hgrn_model.cpp:249-347.
+  // on_token (nullable, model.hpp:44-50) is called with every generated id, in order, as soon
+  // as the host has it: per step when eos_id >= 0 (the step's id is read back to test it),
+  // otherwise once the device loop is done.
   std::vector<int64_t> generate(const int64_t* ids, size_t n, size_t new_tokens, int64_t eos_id,
-                                const Sampling& samp);
+                                const Sampling& samp,
+                                const std::function<void(int64_t)>* on_token = nullptr);
   // model.hpp:34 / hgrn_model.cpp:239-247: logits [T, V] (host), or only the last row.
   void forward(const int64_t* ids, size_t T, float* logits, bool last_row_only);
   // forward plus a host trace of (1 + 3L) x [T, H]: embeddings, then per layer the
@@ -224,7 +229,8 @@ class Model {
   void prefill_runs(const std::vector<std::vector<int64_t>>& prompts, int64_t* first_ids,
                     int64_t stride);
   void sampled_loop(int B, int64_t stride, size_t steps, int64_t eos_id,
-                    std::vector<std::vector<int64_t>>& streams);
+                    std::vector<std::vector<int64_t>>& streams,
+                    const std::function<void(int64_t)>* on_token = nullptr);  // stream 0's ids
   // Float-mode prefill: workspace of the chunked scan (nullptr: the exact serial scan)
   void* chunk_ws(int nseq, int len, int H);
   void* chunk_ws_ = nullptr;

@@ -39,10 +39,29 @@ def test_cli_matches_reference_cli(cuda, blob_cache, tmp_path, mode):
         assert np.abs(lc - lr).max() <= 1e-3 * float(lr.max() - lr.min())
 
 
-def test_cli_errors(cuda):
+def test_cli_errors(cuda, tmp_path):
     rc, _, err = _run(nb.CLI, ["--bogus"])
     assert rc == 2 and "unknown arg" in err
-    rc, _, err = _run(nb.CLI, ["some text prompt"])
-    assert rc == 2
+    # text mode without a tokenizer file beside the blob
+    rc, _, err = _run(nb.CLI, ["some text prompt", "--blob", str(tmp_path / "model.mmfree")])
+    assert rc == 1 and "tokenizer" in err
     rc, _, err = _run(nb.CLI, ["--ids", "1,2", "--blob", "/nonexistent.mmfree"])
     assert rc == 1 and "cannot open" in err
+
+
+@pytest.mark.parametrize("extra", [[], ["--print-ids"], ["--mode", "float"], ["--no-eos"],
+                                   ["--temp", "0.9", "--seed", "11"]])
+def test_cli_text_mode_matches_reference_cli(cuda, blob_cache, extra):
+    """Text in, text out (tokenize, generate with the EOS stop, stream the decoded text) with
+    the synthetic tokenizer: stdout byte for byte equal to the reference CLI's (FixedQ510
+    greedy, full-vocabulary sampling with a seed; Float greedy agrees on these prompts)."""
+    import oracle
+    from conftest import GOLDEN
+    blob = B.cached_blob("small", 0, blob_cache)
+    tok = os.path.join(GOLDEN, "tokenizer_toy.mmtok")
+    for prompt in ("Once upon a time, there was", "Café crème 中文 😀"):
+        common = ["--blob", blob, "--tokenizer", tok, "--gen", "24", *extra, prompt]
+        rc_r, out_r, _ = _run(oracle.REF_CLI, common)
+        rc_c, out_c, err_c = _run(nb.CLI, common)
+        assert rc_r == 0 and rc_c == 0, err_c
+        assert out_c == out_r, (prompt, out_c, out_r)
