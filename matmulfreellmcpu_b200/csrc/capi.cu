@@ -184,7 +184,7 @@ void run_bitlinear(int k, float* const* outs, const float* x, const float* const
   }
   const size_t kp = static_cast<size_t>(padded_k(static_cast<int64_t>(in_dim)));
   const size_t per = fixed ? a256(2 * rows * kp) + a256(rows * 4) : a256(rows * kp * 4);
-  char* base = scratch(static_cast<size_t>(k) * per);
+  char* base = scratch(static_cast<size_t>(k) * per + a256(rows * 8));
   PrepArgs p;
   p.x = x;
   p.nproj = k;
@@ -196,14 +196,20 @@ void run_bitlinear(int k, float* const* outs, const float* x, const float* const
   p.fixed = fixed;
   // the tensor-core matmul (taken for >= kTcMinRows fixed rows) reads the low plane as lo - 128
   p.lo_signed = fixed && static_cast<int>(rows) >= kTcMinRows;
+  // Float rows on the tensor cores too: the activations as bf16 hi / lo planes (the same 4
+  // bytes per element as fp32 activations)
+  p.bf16 = !fixed && static_cast<int>(rows) >= kTcMinRows;
   uint32_t* err = reinterpret_cast<uint32_t*>(base) + kAsyncFlagWord;
   p.err = err;
+  p.rstd_ws = reinterpret_cast<float2*>(base + 256 + static_cast<size_t>(k) * per);
   for (int j = 0; j < k; ++j) {
     char* b = base + 256 + j * per;
     p.normw[j] = nws[j];
     if (fixed) {
       p.planes[j] = reinterpret_cast<int8_t*>(b);
       p.rowsum[j] = reinterpret_cast<int32_t*>(b + a256(2 * rows * kp));
+    } else if (p.bf16) {
+      p.planes[j] = reinterpret_cast<int8_t*>(b);
     } else {
       p.yf[j] = reinterpret_cast<float*>(b);
     }
@@ -225,6 +231,7 @@ void run_bitlinear(int k, float* const* outs, const float* x, const float* const
     a.fixed = fixed;
     a.allow_tc = true;
     a.lo_signed = p.lo_signed;
+    a.bf16 = p.bf16;
     a.err = err;
     ck(launch_matmul(a, st), "matmul kernel");
   }

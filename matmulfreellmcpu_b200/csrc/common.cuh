@@ -18,6 +18,7 @@
 // (the Q5.10 codes are int16). Both sides are exact in int32 for K <= 65536.
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -67,6 +68,22 @@ __device__ __forceinline__ int dp4a_uu(uint32_t a, uint32_t b, int c) {
 __device__ __forceinline__ float ternary_f32(uint32_t m, int jj) {
   const float f = __uint_as_float(__byte_perm(m, 0x4B000000u, 0x7540u | static_cast<unsigned>(jj)));
   return __fadd_rn(f, -8388609.0f);
+}
+
+// Float-mode activations for the tensor cores: y = hi + lo + e with hi = bf16(y),
+// lo = bf16(y - hi) (the difference is exact in fp32) and |e| <= 2^-17 |y|. Four values per
+// call, packed as two 64-bit words of bf16 (element u in bits 16u..16u+15).
+__device__ __forceinline__ void bf16_split4(const float (&y)[4], uint2& hi, uint2& lo) {
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const __nv_bfloat16 hb = __float2bfloat16_rn(y[u]);
+    const __nv_bfloat16 lb = __float2bfloat16_rn(__fsub_rn(y[u], __bfloat162float(hb)));
+    h[u] = __bfloat16_as_ushort(hb);
+    l[u] = __bfloat16_as_ushort(lb);
+  }
+  hi = make_uint2(h[0] | (h[1] << 16), h[2] | (h[3] << 16));
+  lo = make_uint2(l[0] | (l[1] << 16), l[2] | (l[3] << 16));
 }
 
 // Device-side error flags (bitmask), raised by kernels instead of trapping.

@@ -333,6 +333,11 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepArgs a, int mode
         }
         *reinterpret_cast<uint32_t*>(a.planes[j] + static_cast<int64_t>(m) * Kp + c0) = hi;
         *reinterpret_cast<uint32_t*>(a.planes[j] + (static_cast<int64_t>(a.M) + m) * Kp + c0) = lo;
+      } else if (a.bf16) {
+        uint2 hi, lo;
+        bf16_split4(y, hi, lo);
+        *reinterpret_cast<uint2*>(a.planes[j] + 2 * (static_cast<int64_t>(m) * Kp + c0)) = hi;
+        *reinterpret_cast<uint2*>(a.planes[j] + 2 * ((static_cast<int64_t>(a.M) + m) * Kp + c0)) = lo;
       } else {
         *reinterpret_cast<float4*>(a.yf[j] + static_cast<int64_t>(m) * Kp + c0) = make_float4(y[0], y[1], y[2], y[3]);
       }
@@ -350,6 +355,166 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepArgs a, int mode
     if (warp < a.nproj) {
       const int total = __reduce_add_sync(0xffffffffu, lane < nwarps ? s_red[warp][lane] : 0);
       if (lane == 0) a.rowsum[warp][m] = total;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------ prep, many rows
+// For thousands of rows (prefill) the prep runs in two passes instead of one CTA per row:
+//   prep_rstd_kernel   one 8-lane group per row computes the row's rstd values in the exact
+//                      AVX2 order: the row transform's (r1, from x) and the BitLinear norm's
+//                      (r2, from t), the second chain recomputing t = transform(x) on the fly
+//                      (no row is staged; a warp serves 4 rows, so the serial chains of many
+//                      rows overlap on every SM)
+//   prep_quant_kernel  elementwise over row blocks: t, the projections' normalized inputs,
+//                      Q5.10 planes (or Float activations) and row sums; the norm weights of
+//                      a column are loaded once per block of rows
+// Same arithmetic, element by element, as prep_kernel.
+constexpr int kRstdThreads = 256, kQuantRows = 8, kQuantThreads = 256;
+
+__device__ __forceinline__ float row_transform(const PrepArgs& a, int mode, float x, float r1,
+                                               float w, float o, int c) {
+  if (mode == kPrepPlain) return x;
+  float t = norm_x(x, r1, w);
+  if (mode == kPrepSwishgate) t = __fmul_rn(t, silu_x(o, in_body(c, a.K)));
+  return t;
+}
+
+// The exact sum of squares of f(c), c < K, for the 8-lane group of this thread (lane j runs
+// chain j over c = 8i + j, batches of 8 values are computed before their FMAs), then the
+// AVX2 tree and the scalar tail; every lane of the group gets the sum.
+template <class F>
+__device__ __forceinline__ float sumsq_exact8_f(int K, F&& f) {
+  const int j = threadIdx.x & 7, n8 = K >> 3;
+  float acc = 0.0f;
+  int i = 0;
+  for (; i + 8 <= n8; i += 8) {
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = f(8 * (i + u) + j);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) acc = __fmaf_rn(v[u], v[u], acc);
+  }
+  for (; i < n8; ++i) {
+    const float v = f(8 * i + j);
+    acc = __fmaf_rn(v, v, acc);
+  }
+  float sum = hsum8_lanes(acc);
+  for (int c = n8 * 8; c < K; ++c) {
+    const float v = f(c);
+    sum = __fadd_rn(sum, __fmul_rn(v, v));
+  }
+  return sum;
+}
+
+__global__ void __launch_bounds__(kRstdThreads) prep_rstd_kernel(PrepArgs a, int mode, float2* rstd) {
+  grid_dep_launch();
+  grid_dep_wait();
+  const int64_t g = (blockIdx.x * static_cast<int64_t>(kRstdThreads) + threadIdx.x) >> 3;
+  // groups past the last row repeat it (the 8-lane shuffles involve the whole warp) and
+  // store nothing
+  const int64_t m = g < a.M ? g : a.M - 1;
+  const int K = a.K;
+  const float* x = a.x + m * K;
+  const float* o = a.o ? a.o + m * K : nullptr;
+  const float Kf = static_cast<float>(K);
+  float r1 = 0.0f;
+  if (mode != kPrepPlain) r1 = rstd_of(sumsq_exact8_f(K, [&](int c) { return __ldg(x + c); }), Kf, a.eps);
+  const float r2 = rstd_of(sumsq_exact8_f(K, [&](int c) {
+                             return row_transform(a, mode, __ldg(x + c), r1, mode == kPrepPlain ? 0.0f : __ldg(a.prew + c),
+                                                  mode == kPrepSwishgate ? __ldg(o + c) : 0.0f, c);
+                           }),
+                           Kf, a.eps);
+  if ((threadIdx.x & 7) == 0 && g < a.M) rstd[m] = make_float2(r1, r2);
+}
+
+__global__ void __launch_bounds__(kQuantThreads) prep_quant_kernel(PrepArgs a, int mode,
+                                                                   const float2* __restrict__ rstd) {
+  grid_dep_launch();
+  grid_dep_wait();
+  __shared__ int s_red[3][kQuantRows][kQuantThreads / 32];
+  const int K = a.K, tid = threadIdx.x, nproj = a.nproj;
+  const int64_t Kp = padded_k(K);
+  const int64_t m0 = static_cast<int64_t>(blockIdx.x) * kQuantRows;
+  // rows of a multiple of 4 floats at 16-byte aligned bases: 16-byte loads
+  const bool vec = (K & 3) == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 &&
+                   (mode != kPrepSwishgate || (reinterpret_cast<uintptr_t>(a.o) & 15) == 0);
+  float2 rs[kQuantRows];
+#pragma unroll
+  for (int r = 0; r < kQuantRows; ++r) rs[r] = m0 + r < a.M ? rstd[m0 + r] : make_float2(0.0f, 0.0f);
+  int local[3][kQuantRows] = {};
+  for (int c0 = 4 * tid; c0 < Kp; c0 += 4 * kQuantThreads) {
+    float pw[4], nwv[3][4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int c = c0 + u;
+      pw[u] = (mode != kPrepPlain && c < K) ? __ldg(a.prew + c) : 0.0f;
+#pragma unroll
+      for (int j = 0; j < 3; ++j) nwv[j][u] = (j < nproj && c < K) ? __ldg(a.normw[j] + c) : 0.0f;
+    }
+#pragma unroll  // unrolled: local[][r] and rs[r] stay in registers
+    for (int r = 0; r < kQuantRows; ++r) {
+      const int64_t m = m0 + r;
+      if (m >= a.M) break;
+      float xv[4], ov[4] = {0.0f, 0.0f, 0.0f, 0.0f}, t[4];
+      load4(a.x + m * K, c0, K, vec, xv);
+      if (mode == kPrepSwishgate) load4(a.o + m * K, c0, K, vec, ov);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int c = c0 + u;
+        t[u] = c < K ? row_transform(a, mode, xv[u], rs[r].x, pw[u], ov[u], c) : 0.0f;
+        if (a.pre_out && c < K) a.pre_out[m * K + c] = t[u];
+      }
+#pragma unroll
+      for (int j = 0; j < 3; ++j) {
+        if (j >= nproj) break;
+        float y[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int c = c0 + u;
+          y[u] = c < K ? norm_x(t[u], rs[r].y, nwv[j][u]) : 0.0f;
+          if (j == 0 && a.norm_out && c < K) a.norm_out[m * K + c] = y[u];
+        }
+        if (a.fixed) {
+          uint32_t hi = 0, lo = 0;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int c = c0 + u;
+            const int32_t q = c < K ? quant_x(y[u], a.qs, in_body(c, K)) : 0;
+            local[j][r] += q;
+            hi |= static_cast<uint32_t>((q >> 8) & 0xff) << (8 * u);
+            lo |= static_cast<uint32_t>((q & 0xff) ^ (a.lo_signed ? 0x80 : 0)) << (8 * u);
+          }
+          *reinterpret_cast<uint32_t*>(a.planes[j] + m * Kp + c0) = hi;
+          *reinterpret_cast<uint32_t*>(a.planes[j] + (a.M + m) * Kp + c0) = lo;
+        } else if (a.bf16) {
+          uint2 hi, lo;
+          bf16_split4(y, hi, lo);
+          *reinterpret_cast<uint2*>(a.planes[j] + 2 * (m * Kp + c0)) = hi;
+          *reinterpret_cast<uint2*>(a.planes[j] + 2 * ((a.M + m) * Kp + c0)) = lo;
+        } else {
+          *reinterpret_cast<float4*>(a.yf[j] + m * Kp + c0) = make_float4(y[0], y[1], y[2], y[3]);
+        }
+      }
+    }
+  }
+  if (!a.fixed) return;
+  const int warp = tid >> 5, lane = tid & 31;
+#pragma unroll
+  for (int j = 0; j < 3; ++j)
+#pragma unroll
+    for (int r = 0; r < kQuantRows; ++r) {
+      const int v = __reduce_add_sync(0xffffffffu, local[j][r]);
+      if (lane == 0) s_red[j][r][warp] = v;
+    }
+  __syncthreads();
+  if (tid < nproj * kQuantRows) {
+    const int j = tid / kQuantRows, r = tid % kQuantRows;
+    if (m0 + r < a.M) {
+      int total = 0;
+#pragma unroll
+      for (int w = 0; w < kQuantThreads / 32; ++w) total += s_red[j][r][w];
+      a.rowsum[j][m0 + r] = total;
     }
   }
 }
@@ -383,6 +548,13 @@ cudaError_t launch_prep(const PrepArgs& a, cudaStream_t s) {
         !a.mix_f || !a.mix_state || !al16(a.mix_i) || !al16(a.mix_f) || !al16(a.mix_state) ||
         !al16(a.mix_lb) || !al16(a.mix_out))
       return cudaErrorInvalidValue;
+  }
+  if (a.M >= kPrepManyRows && a.rstd_ws && !a.mix_i) {  // many rows: the two-pass prep
+    cudaError_t e = launch_k(prep_rstd_kernel, dim3(static_cast<unsigned>(ceil_div(int64_t(a.M) * 8, kRstdThreads))),
+                             dim3(kRstdThreads), 0, s, a.pdl, a, mode, a.rstd_ws);
+    if (e != cudaSuccess) return e;
+    return launch_k(prep_quant_kernel, dim3(static_cast<unsigned>(ceil_div(a.M, kQuantRows))),
+                    dim3(kQuantThreads), 0, s, true, a, mode, static_cast<const float2*>(a.rstd_ws));
   }
   if (smem > 48 * 1024) raise_smem_limit(reinterpret_cast<const void*>(prep_kernel));
   PrepArgs q = a;
@@ -571,7 +743,7 @@ static int sm_count() {
 cudaError_t launch_matmul(const MatmulArgs& a, cudaStream_t s) {
   if (a.M <= 0 || a.N <= 0) return cudaSuccess;
   if (matmul_uses_tc(a)) {
-    if (!a.lo_signed) return cudaErrorInvalidValue;  // planes in the wrong form
+    if (a.fixed && !a.lo_signed) return cudaErrorInvalidValue;  // planes in the wrong form
     return launch_matmul_tc(a, tc_splits(a, sm_count()), s);
   }
   if (a.M == 1) return launch_matmul_mt<1>(a, s);

@@ -27,6 +27,8 @@ struct PrepArgs {
                                  // form the tensor-core matmul reads (matmul_uses_tc)
   int32_t* rowsum[3] = {};       // fixed: [M] sum of codes
   float* yf[3] = {};             // float: [M][Kp] normalized activations (zero padded)
+  bool bf16 = false;             // float: write planes[j] as bf16 [2][M][Kp] (hi = bf16(y),
+                                 // lo = bf16(y - hi)) for the tensor-core matmul, not yf
   int M = 0, K = 0;
   float eps = 1e-6f;
   float qs = 1024.0f;            // 2^frac_bits
@@ -34,6 +36,8 @@ struct PrepArgs {
   bool pdl = false;              // launch as a programmatic dependent of the previous kernel
   uint32_t* err = nullptr;       // optional: bit kErrTimeout on a timed-out wait
   uint32_t row_polls = 0;        // set by launch_prep: polls of the row-staging wait
+  float2* rstd_ws = nullptr;     // optional [M] workspace: with it, M >= kPrepManyRows rows
+                                 // take the two-pass prep (rstd pass, then quantisation pass)
   // kPrepSwishgate of one decode step with the token mixer fused in: o is not read but
   // computed here from the i / f projections and the recurrent state (which is updated), as
   // launch_mixer does for len 1; needs K % 4 == 0, 16-byte aligned rows and K >= 8
@@ -64,11 +68,16 @@ struct MatmulArgs {
   uint32_t* err = nullptr;
   bool pdl = false;               // launch as a programmatic dependent of the previous kernel
   bool lo_signed = false;         // planes hold lo - 128 (required by the tensor-core path)
+  bool bf16 = false;              // float: planes hold bf16 hi / lo activations [2][M][Kp]
+                                  // (PrepArgs::bf16); the tensor-core path reads them
 };
 
 constexpr int kTcMinRows = 16;
-// Does launch_matmul take the tensor-core path (whose planes must be lo_signed)?
-inline bool matmul_uses_tc(const MatmulArgs& a) { return a.fixed && a.allow_tc && a.M >= kTcMinRows; }
+// Does launch_matmul take the tensor-core path (FixedQ510 planes lo_signed, or Float bf16
+// planes)?
+inline bool matmul_uses_tc(const MatmulArgs& a) {
+  return a.allow_tc && a.M >= kTcMinRows && (a.fixed || a.bf16);
+}
 
 // ---- fused few-row decode kernels (decode.cu)
 enum DecPro : int {

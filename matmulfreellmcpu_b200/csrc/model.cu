@@ -80,6 +80,8 @@ Model::Model(const std::string& blob_path, int device, bool fixed, int frac_bits
     mix_prep_ok_ = !(menv && menv[0] == '0');
     const char* senv = std::getenv("MMFREE_HOST_SAMPLING");
     host_sampling_ = senv && senv[0] == '1';
+    const char* fenv = std::getenv("MMFREE_FLOAT_TC");
+    float_tc_ = !(fenv && fenv[0] == '0');
   }
   CK(cudaMalloc(&dec_part_v_, sizeof(float) * kDecMaxRows * 2 * 1024));
   CK(cudaMalloc(&dec_part_i_, sizeof(int) * kDecMaxRows * 2 * 1024));
@@ -271,10 +273,10 @@ void Model::ensure_ws(size_t rows) {
   size_t o_h = carve(rows * H * 4), o_resid = carve(rows * H * 4), o_ib = carve(rows * H * 4),
          o_fb = carve(rows * H * 4), o_gb = carve(rows * H * 4), o_recur = carve(rows * H * 4),
          o_y = carve(rows * 2 * I * 4), o_z = carve(rows * I * 4), o_lg = carve(rows * V * 4),
-         o_hl = carve(rows * H * 4), o_ids = carve(rows * 8);
+         o_hl = carve(rows * H * 4), o_ids = carve(rows * 8), o_rstd = carve(rows * 8);
   size_t o_pl[3], o_rs[3], o_yf[3];
   for (int j = 0; j < 3; ++j) {
-    o_pl[j] = fixed_ ? carve(2 * rows * Kp) : 0;
+    o_pl[j] = carve((fixed_ ? 2 : 4) * rows * Kp);  // u8 planes, or Float's bf16 hi / lo planes
     o_rs[j] = carve(rows * 4);
     o_yf[j] = fixed_ ? 0 : carve(rows * Kp * 4);
   }
@@ -291,8 +293,9 @@ void Model::ensure_ws(size_t rows) {
   logits_ = reinterpret_cast<float*>(b + o_lg);
   hl_ = reinterpret_cast<float*>(b + o_hl);
   ids_ = reinterpret_cast<int64_t*>(b + o_ids);
+  rstd_ws_ = reinterpret_cast<float2*>(b + o_rstd);
   for (int j = 0; j < 3; ++j) {
-    planes_[j] = fixed_ ? reinterpret_cast<int8_t*>(b + o_pl[j]) : nullptr;
+    planes_[j] = reinterpret_cast<int8_t*>(b + o_pl[j]);
     rowsum_[j] = reinterpret_cast<int32_t*>(b + o_rs[j]);
     yf_[j] = fixed_ ? nullptr : reinterpret_cast<float*>(b + o_yf[j]);
   }
@@ -388,7 +391,11 @@ void Model::prep(const PrepArgs& p) {
   PrepArgs q = p;
   q.pdl = pdl_;
   q.err = err_;
-  q.lo_signed = tc_rows(q.M);  // the BitLinear of these rows runs on the tensor cores
+  q.rstd_ws = rstd_ws_;
+  // the BitLinear of these rows runs on the tensor cores: FixedQ510 low planes as lo - 128,
+  // Float activations as bf16 hi / lo planes
+  q.lo_signed = fixed_ && tc_rows(q.M);
+  q.bf16 = !fixed_ && tc_rows(q.M);
   timed(kClsPrep, bytes, 0, [&] { CK(launch_prep(q, stream_)); });
 }
 
@@ -416,7 +423,8 @@ MatmulArgs Model::mm_args(const Proj& p, int plane, float* out, int M, const flo
   a.allow_tc = true;
   a.err = err_;
   a.pdl = pdl_;
-  a.lo_signed = tc_rows(M);
+  a.lo_signed = fixed_ && tc_rows(M);
+  a.bf16 = !fixed_ && tc_rows(M);
   return a;
 }
 
@@ -429,7 +437,7 @@ void Model::bitlinear(const Proj& p, int plane, float* out, int M, const float* 
         [&] { CK(launch_matmul(a, stream_)); });
 }
 
-bool Model::tc_rows(int M) const { return fixed_ && M >= kTcMinRows; }
+bool Model::tc_rows(int M) const { return M >= kTcMinRows && (fixed_ || float_tc_); }
 
 void Model::bitlinear_ifg(const Layer& ly, int M) {
   if (!tc_rows(M)) {
@@ -607,10 +615,14 @@ void Model::layers_tp(int nseq, int len, int seg_rows) {
     prep(p);
   };
   // a shard's BitLinear into out (row stride ldo), optionally + resid (row stride ldr)
-  auto shard_mm = [&](const Proj& pj, int plane, float* out, int ldo, const float* resid, int ldr) {
+  // a shard's BitLinear; from_yf: Float row-parallel inputs written as fp32 activations by
+  // launch_norm_slice (the CUDA-core kernel reads them)
+  auto shard_mm = [&](const Proj& pj, int plane, float* out, int ldo, const float* resid, int ldr,
+                      bool from_yf = false) {
     MatmulArgs a = mm_args(pj, plane, out, rows, resid);
     a.ldo = ldo;
     a.ldr = ldr;
+    if (from_yf) a.allow_tc = false;
     timed(kClsMatmul, 0, 2.0 * rows * pj.in * pj.out, [&] { CK(launch_matmul(a, stream_)); });
   };
   for (int l = 0; l < L_; ++l) {
@@ -637,7 +649,7 @@ void Model::layers_tp(int nseq, int len, int seg_rows) {
       tp_->all_reduce_f32(ss_b, rows, stream_);
       const int kp = static_cast<int>(padded_k(Hs));
       CK(launch_norm_slice(yf_[0], tp_ts_, ss_b, ly.p[kO].normw + hoff, rows, Hs, kp, H, eps_, stream_));
-      shard_mm(ly.p[kO], 0, resid_, H, nullptr, 0);  // partial [rows][H]
+      shard_mm(ly.p[kO], 0, resid_, H, nullptr, 0, true);  // partial [rows][H]
       tp_->all_reduce_f32(resid_, static_cast<size_t>(rows) * H, stream_);
       CK(launch_add(resid_, h_, resid_, static_cast<int64_t>(rows) * H, stream_));
     }
@@ -665,7 +677,7 @@ void Model::layers_tp(int nseq, int len, int seg_rows) {
       const int kp = static_cast<int>(padded_k(Is));
       CK(launch_norm_slice(yf_[0], tp_zs_, ss_a, ly.p[kDown].normw + ioff, rows, Is, kp, I_, eps_,
                            stream_));
-      shard_mm(ly.p[kDown], 0, h_, H, nullptr, 0);  // partial [rows][H]
+      shard_mm(ly.p[kDown], 0, h_, H, nullptr, 0, true);  // partial [rows][H]
       tp_->all_reduce_f32(h_, static_cast<size_t>(rows) * H, stream_);
       CK(launch_add(h_, resid_, h_, static_cast<int64_t>(rows) * H, stream_));
     }

@@ -145,6 +145,8 @@ class Model {
   bool pdl_ = true;                // MMFREE_PDL=0: plain stream order between kernels
   bool persist_ok_ = false;        // MMFREE_PERSIST=1: the whole fused step in one launch
   bool mix_prep_ok_ = true;        // MMFREE_MIX_IN_PREP=0: the decode mixer as its own kernel
+  bool float_tc_ = true;           // MMFREE_FLOAT_TC=0: Float BitLinears of >= 16 rows on the
+                                   // CUDA cores instead of the bf16 tensor-core path
   DecArgs* persist_tab_ = nullptr; // device copy of the persistent step's phase table
   int persist_n_ = 0, persist_grid_ = 0, persist_b_ = 0;
   int64_t persist_stride_ = -1;
@@ -178,6 +180,7 @@ class Model {
   int8_t* planes_[3] = {};
   int32_t* rowsum_[3] = {};
   float* yf_[3] = {};
+  float2* rstd_ws_ = nullptr;      // per-row rstd pair of the two-pass prep (many rows)
   int64_t* ids_ = nullptr;
 
   // state and decode loop

@@ -206,6 +206,32 @@ __device__ __forceinline__ void mma_i8_ts(uint32_t d_tmem, uint32_t a_tmem, uint
       : "memory");
 }
 
+// Instruction descriptor of kind::f16 for the Float path: D f32, A and B both bf16 (the same
+// type, as the kind requires), both K-major, M=128, N=bn.
+__host__ __device__ constexpr uint32_t idesc_bf16(int bn) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(bn >> 3) << 17) |
+         (static_cast<uint32_t>(128 >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(
+          d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+      : "memory");
+}
+
+// Two ternary codes (u = w + 1 in the low 2 bits of bytes b and b + 1 of m) as a pair of bf16
+// weights w in {-1, 0, +1} (0xBF80, 0, 0x3F80): the low and high bytes of each bf16 are looked
+// up by byte_perm in the tables 0x00800080 (lows) and 0x003F00BF (highs), indexed by u.
+__device__ __forceinline__ uint32_t ternary_bf16x2(uint32_t m, int b) {
+  const uint32_t u0 = (m >> (8 * b)) & 3u, u1 = (m >> (8 * b + 8)) & 3u;
+  return __byte_perm(0x003F00BFu, 0x00800080u, (4u + u0) | (u0 << 4) | ((4u + u1) << 8) | (u1 << 12));
+}
+
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                    smem_u32(bar))
@@ -274,10 +300,16 @@ __device__ __forceinline__ bool role_wait(uint64_t* bar, uint32_t parity, uint32
 
 }  // namespace
 
-template <int BN, int TT>
+// FL (Float mode): the activation planes are bf16 hi / lo splits of the fp32 activations, the
+// weights are expanded to bf16 {-1, 0, +1} (two per TMEM column) and the MMA is kind::f16 with
+// an f32 accumulator; a k-block is then 64 k (one packed chunk), which keeps every shared- and
+// tensor-memory geometry of the integer path: a 128-byte activation row per plane and k-block,
+// 32 TMEM columns of A per stage, 4 MMAs per stage. D = D_hi + D_lo, dequantised by 1/scale_w.
+template <int BN, int TT, bool FL>
 __global__ void __launch_bounds__(kTcThreads, 2)
     tc_matmul_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcArgs p) {
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 64, "BN must be 16..64, a multiple of 16");
+  constexpr int kKB = FL ? kChunkK : kKBlock;  // k per pipeline stage
   constexpr int kCols = kAStages * 32 + TT * 2 * BN;  // A stages + TT x (D_hi, D_lo)
   constexpr int kAllocCols = kCols <= 128 ? 128 : (kCols <= 256 ? 256 : 512);
   static_assert(kCols <= 512 && (TT > 1 || kAllocCols <= 256),
@@ -309,7 +341,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     return p.pair ? (g < 2 ? 2 * blockIdx.x + g : p.pair + 2 * blockIdx.x + g - 2) : (n0 >> 5) + g;
   };
   const int64_t kc = packed_chunks(a.K);
-  const int nkb = static_cast<int>((kc + 1) / 2);
+  const int nkb = static_cast<int>(FL ? kc : (kc + 1) / 2);
   const int kb0 = static_cast<int>(static_cast<int64_t>(nkb) * split / p.splits);
   const int kb1 = static_cast<int>(static_cast<int64_t>(nkb) * (split + 1) / p.splits);
   const int nk = kb1 - kb0;
@@ -364,9 +396,13 @@ __global__ void __launch_bounds__(kTcThreads, 2)
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       const int t = t0 + c0 + j;
-      const int32_t acc = static_cast<int32_t>(v[j] - static_cast<uint32_t>(s_rowsum[(c0 + j) & (BN - 1)]));
-      if (a.acc_out && n_ok && j < cnt && t < a.M) a.acc_out[static_cast<int64_t>(t) * a.N + n] = acc;
-      o[j] = __fmul_rn(__int2float_rn(acc), P.scale);
+      if (FL) {  // v: the float sum D_hi + D_lo
+        o[j] = __fmul_rn(__uint_as_float(v[j]), P.scale);
+      } else {
+        const int32_t acc = static_cast<int32_t>(v[j] - static_cast<uint32_t>(s_rowsum[(c0 + j) & (BN - 1)]));
+        if (a.acc_out && n_ok && j < cnt && t < a.M) a.acc_out[static_cast<int64_t>(t) * a.N + n] = acc;
+        o[j] = __fmul_rn(__int2float_rn(acc), P.scale);
+      }
       if (a.resid) o[j] = __fadd_rn(r[j], o[j]);
     }
     if (!p.pair) {
@@ -417,8 +453,8 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         // so that the bounded waits never include its run time
         if (i == kWStages) grid_dep_wait();
         if (i >= kWStages && !role_wait(&wempty[s], ((i / kWStages) - 1) & 1, &s_fail)) break;
-        const int64_t c0 = 2 * static_cast<int64_t>(kb0 + i);
-        const uint32_t bytes = c0 + 1 < kc ? 2 * kChunkBytes : kChunkBytes;
+        const int64_t c0 = (FL ? 1 : 2) * static_cast<int64_t>(kb0 + i);  // first chunk
+        const uint32_t bytes = !FL && c0 + 1 < kc ? 2 * kChunkBytes : kChunkBytes;
         uint32_t total = 0;
         for (int g = 0; g < 4; ++g)
           if (tile_group(g) < ngroups) total += bytes;
@@ -445,7 +481,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       for (; i < nk; ++i) {
         const int s = i % kBStages;
         if (i >= kBStages && !role_wait(&bempty[s], ((i / kBStages) - 1) & 1, &s_fail)) break;
-        const int x = (kb0 + i) * kKBlock;
+        const int x = (kb0 + i) * kKB;  // elements: 128 bytes of either plane type
         unsigned char* dst = bst + s * L::kBStage;
         mbar_arrive_tx(&bfull[s], static_cast<uint32_t>(L::kBStage));
 #pragma unroll
@@ -477,14 +513,17 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         // both planes in one instruction: B rows [0, BN) are the high bytes, [BN, 2BN) the
         // low bytes - 128 (both s8, one 128-byte-swizzled tile), D columns likewise; the
         // same A (weight) columns serve every token tile
+        // per MMA: 32 bytes of K from the activation rows and 8 TMEM columns of weights
+        // (32 u8 or 16 bf16 k), 4 per stage either way
 #pragma unroll
         for (int tt = 0; tt < TT; ++tt)
 #pragma unroll
-          for (int j = 0; j < kKBlock / 32; ++j) {
+          for (int j = 0; j < 4; ++j) {
             const uint32_t acc = (i > 0 || j > 0) ? 1u : 0u;
             const uint32_t a_addr = tmem_a + static_cast<uint32_t>(sa * 32 + j * 8);
-            mma_i8_ts(tmem_dhi + tt * 2 * BN, a_addr,
-                      smem_desc_sw128(b_base + tt * L::kBTile + j * 32), idesc_i8(true, 2 * BN), acc);
+            const uint64_t bd = smem_desc_sw128(b_base + tt * L::kBTile + j * 32);
+            if (FL) mma_bf16_ts(tmem_dhi + tt * 2 * BN, a_addr, bd, idesc_bf16(2 * BN), acc);
+            else mma_i8_ts(tmem_dhi + tt * 2 * BN, a_addr, bd, idesc_i8(true, 2 * BN), acc);
           }
         mma_commit(&aempty[sa]);
         mma_commit(&bempty[sb]);
@@ -503,11 +542,11 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       const int sw = i % kWStages, sa = i % kAStages;
       if (!role_wait(&wfull[sw], (i / kWStages) & 1, &s_fail)) { ok = false; break; }
       const uint4* src = reinterpret_cast<const uint4*>(wst + sw * kWBlock + warp * 2 * kChunkBytes) + lane;
-      const uint4 wv[2] = {src[0], src[kChunkBytes / 16]};
+      const uint4 wv[2] = {src[0], FL ? src[0] : src[kChunkBytes / 16]};
       const int nch = 2 * static_cast<int64_t>(kb0 + i) + 1 < kc ? 2 : 1;  // chunks below Kp
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        if (h >= nch) break;
+        if (FL || h >= nch) break;  // (the Float combine needs no code sums)
         const uint32_t wd[4] = {wv[h].x, wv[h].y, wv[h].z, wv[h].w};
 #pragma unroll
         for (int w4 = 0; w4 < 4; ++w4)
@@ -520,12 +559,26 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       tc_fence_after();
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        const uint32_t wd[4] = {wv[h].x, wv[h].y, wv[h].z, wv[h].w};
         uint32_t r[16];
+        if (FL) {
+          // one chunk: column 16h + c holds k = 32h + 2c, 2c + 1 as bf16 weights; word w4 of
+          // the chunk holds k = 16 w4 + 4q + j (j = 0..3) in byte j of (word >> 2q)
+          const uint32_t wd[4] = {wv[0].x, wv[0].y, wv[0].z, wv[0].w};
 #pragma unroll
-        for (int w4 = 0; w4 < 4; ++w4)
+          for (int w = 0; w < 2; ++w)
 #pragma unroll
-          for (int q = 0; q < 4; ++q) r[4 * w4 + q] = (wd[w4] >> (2 * q)) & 0x03030303u;
+            for (int q = 0; q < 4; ++q) {
+              const uint32_t m = (wd[2 * h + w] >> (2 * q)) & 0x03030303u;
+              r[8 * w + 2 * q] = ternary_bf16x2(m, 0);
+              r[8 * w + 2 * q + 1] = ternary_bf16x2(m, 2);
+            }
+        } else {
+          const uint32_t wd[4] = {wv[h].x, wv[h].y, wv[h].z, wv[h].w};
+#pragma unroll
+          for (int w4 = 0; w4 < 4; ++w4)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) r[4 * w4 + q] = (wd[w4] >> (2 * q)) & 0x03030303u;
+        }
         tmem_st16(tmem_a + lane_base + static_cast<uint32_t>(sa * 32 + h * 16), r);
       }
       tmem_st_wait();
@@ -539,7 +592,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     // groups stay rolled. Loads of a group are issued before its stores (a store may alias
     // them) and the next group's residuals are fetched while the current group is written.
     grid_dep_wait();
-    if (tid < BN) s_rowsum[tid] = t0 + tid < a.M ? P.rowsum[t0 + tid] : 0;
+    if (tid < BN) s_rowsum[tid] = (!FL && t0 + tid < a.M) ? P.rowsum[t0 + tid] : 0;
     const bool done = mbar_wait(&dfull, 0);
     tc_fence_after();
     if (!done) atomicOr(&s_fail, 1u);
@@ -553,7 +606,9 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         tmem_ld16(tmem_dhi + tt * 2 * BN + lane_base + c0, dh);
         tmem_ld16(tmem_dlo + tt * 2 * BN + lane_base + c0, dl);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = (dh[j] << 8) + dl[j] + (su << 7);  // mod 2^32
+        for (int j = 0; j < 16; ++j)
+          v[j] = FL ? __float_as_uint(__fadd_rn(__uint_as_float(dh[j]), __uint_as_float(dl[j])))
+                    : (dh[j] << 8) + dl[j] + (su << 7);  // mod 2^32
       };
       if (p.splits == 1) {
 #pragma unroll 1
@@ -562,7 +617,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
             t0 = tb + tt * BN;
             if (t0 >= a.M) break;
             named_sync(1, 128);
-            if (tid < BN) s_rowsum[tid] = t0 + tid < a.M ? P.rowsum[t0 + tid] : 0;
+            if (tid < BN) s_rowsum[tid] = (!FL && t0 + tid < a.M) ? P.rowsum[t0 + tid] : 0;
             named_sync(1, 128);
           }
           float rv[16];
@@ -655,12 +710,19 @@ __global__ void __launch_bounds__(kTcThreads, 2)
               float o[4];
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
-                uint32_t v = 0;
+                if (FL) {  // float partials, summed in split order
+                  float vs = 0.0f;
 #pragma unroll
-                for (int r = 0; r < S; ++r) v += part[r][e];
-                const int32_t acc = static_cast<int32_t>(v - rs);
-                if (a.acc_out && nq + e < a.N) a.acc_out[static_cast<int64_t>(t) * a.N + nq + e] = acc;
-                o[e] = __fmul_rn(__int2float_rn(acc), P.scale);
+                  for (int r = 0; r < S; ++r) vs = __fadd_rn(vs, __uint_as_float(part[r][e]));
+                  o[e] = __fmul_rn(vs, P.scale);
+                } else {
+                  uint32_t v = 0;
+#pragma unroll
+                  for (int r = 0; r < S; ++r) v += part[r][e];
+                  const int32_t acc = static_cast<int32_t>(v - rs);
+                  if (a.acc_out && nq + e < a.N) a.acc_out[static_cast<int64_t>(t) * a.N + nq + e] = acc;
+                  o[e] = __fmul_rn(__int2float_rn(acc), P.scale);
+                }
                 if (a.resid) o[e] = __fadd_rn(rv[e], o[e]);
               }
               if (P.out) {
@@ -720,19 +782,30 @@ __global__ void __launch_bounds__(kTcThreads, 2)
               bool body[4];
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
-                uint32_t vg = 0, vu = 0;
+                if (FL) {
+                  float sg = 0.0f, sv = 0.0f;
 #pragma unroll
-                for (int r = 0; r < S; ++r) {
-                  vg += pg[r][e];
-                  vu += pu[r][e];
+                  for (int r = 0; r < S; ++r) {
+                    sg = __fadd_rn(sg, __uint_as_float(pg[r][e]));
+                    sv = __fadd_rn(sv, __uint_as_float(pu[r][e]));
+                  }
+                  g[e] = __fmul_rn(sg, P.scale);
+                  u[e] = __fmul_rn(sv, P.scale);
+                } else {
+                  uint32_t vg = 0, vu = 0;
+#pragma unroll
+                  for (int r = 0; r < S; ++r) {
+                    vg += pg[r][e];
+                    vu += pu[r][e];
+                  }
+                  const int32_t ag = static_cast<int32_t>(vg - rs), au = static_cast<int32_t>(vu - rs);
+                  if (a.acc_out) {
+                    a.acc_out[static_cast<int64_t>(t) * a.N + col + e] = ag;
+                    a.acc_out[static_cast<int64_t>(t) * a.N + I + col + e] = au;
+                  }
+                  g[e] = __fmul_rn(__int2float_rn(ag), P.scale);
+                  u[e] = __fmul_rn(__int2float_rn(au), P.scale);
                 }
-                const int32_t ag = static_cast<int32_t>(vg - rs), au = static_cast<int32_t>(vu - rs);
-                if (a.acc_out) {
-                  a.acc_out[static_cast<int64_t>(t) * a.N + col + e] = ag;
-                  a.acc_out[static_cast<int64_t>(t) * a.N + I + col + e] = au;
-                }
-                g[e] = __fmul_rn(__int2float_rn(ag), P.scale);
-                u[e] = __fmul_rn(__int2float_rn(au), P.scale);
                 // element (t, col) is in the scalar tail of its segment only in the segment's
                 // last row, at columns >= tail_from (fewer than 8, so the division is rare)
                 body[e] = col + e < p.tail_from || (t + 1) % p.seg_rows != 0;
@@ -793,38 +866,40 @@ EncodeTiledFn encode_tiled() {
   return fn;
 }
 
-// The planes [2][M][Kp] as one 2-D u8 tensor of 2M rows x Kp bytes; a box is BN rows x 128 B
-// (one k-block), written to shared memory with the 128-byte swizzle; reads past row 2M or
-// column Kp return zeros.
-cudaError_t planes_map(CUtensorMap* map, const int8_t* planes, int M, int64_t kp, int bn) {
+// The planes [2][M][Kp] as one 2-D tensor of 2M rows x Kp elements (u8, or bf16 for the Float
+// path); a box is BN rows x 128 B (one k-block), written to shared memory with the 128-byte
+// swizzle; reads past row 2M or column Kp return zeros.
+cudaError_t planes_map(CUtensorMap* map, const int8_t* planes, int M, int64_t kp, int bn, bool bf16) {
   EncodeTiledFn enc = encode_tiled();
   if (!enc) return cudaErrorNotSupported;
   if ((reinterpret_cast<uintptr_t>(planes) & 15) != 0) return cudaErrorMisalignedAddress;
+  const cuuint64_t esize = bf16 ? 2 : 1;
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(kp), 2 * static_cast<cuuint64_t>(M)};
-  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(kp)};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kKBlock), static_cast<cuuint32_t>(bn)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(kp) * esize};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / esize), static_cast<cuuint32_t>(bn)};
   const cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(planes), dims, strides,
-                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+                   const_cast<int8_t*>(planes), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
 }  // namespace
 
-template <int BN, int TT>
+template <int BN, int TT, bool FL>
 static cudaError_t launch_tc_bn(const TcArgs& p, const MatmulArgs* a, bool pdl, cudaStream_t s) {
   using L = TcLayout<BN, TT>;
   TcMaps maps;
   for (int j = 0; j < p.nproj; ++j) {
-    cudaError_t e = planes_map(&maps.m[j], a[j].planes, a[j].M, padded_k(a[j].K), BN);
+    cudaError_t e = planes_map(&maps.m[j], a[j].planes, a[j].M, padded_k(a[j].K), BN, FL);
     if (e != cudaSuccess) return e;
   }
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_set[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(tc_matmul_kernel<BN, TT>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kDyn);
+    cudaError_t e = cudaFuncSetAttribute(tc_matmul_kernel<BN, TT, FL>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kDyn);
     if (e != cudaSuccess) return e;
     attr_set[dev & 63] = true;
   }
@@ -850,7 +925,13 @@ static cudaError_t launch_tc_bn(const TcArgs& p, const MatmulArgs* a, bool pdl, 
   }
   cfg.attrs = at;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, tc_matmul_kernel<BN, TT>, maps, p);
+  return cudaLaunchKernelEx(&cfg, tc_matmul_kernel<BN, TT, FL>, maps, p);
+}
+
+// k-blocks of a reduction over K: 128 k per block for the integer path, 64 for Float
+static int tc_kblocks(const MatmulArgs& a) {
+  const int64_t kc = packed_chunks(a.K);
+  return static_cast<int>(a.fixed ? (kc + 1) / 2 : kc);
 }
 
 int tc_token_tile(int M) { return M <= 16 ? 16 : (M <= 32 ? 32 : 64); }
@@ -865,7 +946,7 @@ int tc_splits(const MatmulArgs& a, int sm_count, int nproj) {
     return (e && std::atoi(e) == 1) ? 1 : 2;
   }();
   const int64_t tiles = ceil_div(a.N, 128) * ceil_div(a.M, tc_token_tile(a.M)) * nproj;
-  const int nkb = static_cast<int>((packed_chunks(a.K) + 1) / 2);
+  const int nkb = tc_kblocks(a);
   int splits = 1;
   while (splits < 8 && tiles * splits * 2 <= per_sm * sm_count && nkb / (splits * 2) >= 2) splits *= 2;
   return splits;
@@ -877,12 +958,15 @@ static cudaError_t launch_tc(const MatmulArgs* a, int nproj, int pair, int64_t s
                              cudaStream_t s) {
   const MatmulArgs& m = a[0];
   if (m.M <= 0 || m.N <= 0) return cudaSuccess;
-  const int nkb = static_cast<int>((packed_chunks(m.K) + 1) / 2);
+  const int nkb = tc_kblocks(m);
   if (nproj < 1 || nproj > 3 || splits < 1 || splits > 8 || (splits & (splits - 1)) || splits > nkb)
     return cudaErrorInvalidValue;
   if (pair && (nproj != 1 || m.N != 64 * pair || pair % 2 != 0)) return cudaErrorInvalidValue;
+  // FixedQ510: low planes stored lo - 128; Float: bf16 planes (no raw accumulators)
   for (int j = 0; j < nproj; ++j)
-    if (a[j].M != m.M || a[j].N != m.N || a[j].K != m.K || !a[j].lo_signed) return cudaErrorInvalidValue;
+    if (a[j].M != m.M || a[j].N != m.N || a[j].K != m.K || a[j].fixed != m.fixed ||
+        (m.fixed ? !a[j].lo_signed : (!a[j].bf16 || a[j].acc_out)))
+      return cudaErrorInvalidValue;
   TcArgs p{};
   p.m = m;
   p.nproj = nproj;
@@ -906,13 +990,17 @@ static cudaError_t launch_tc(const MatmulArgs* a, int nproj, int pair, int64_t s
     p.vec = vec ? 1 : 0;
   }
   for (int j = 0; j < nproj; ++j) p.pj[j] = TcProj{a[j].w, a[j].rowsum, a[j].out, a[j].scale};
-  switch (tc_token_tile(m.M)) {
-    case 16: return launch_tc_bn<16, 1>(p, a, m.pdl, s);
-    case 32: return launch_tc_bn<32, 1>(p, a, m.pdl, s);
-    // (three 64-row token tiles per CTA sharing each expanded weight k-block, TT = 3, were
-    // measured 1.3x slower on the 2.7B prefill than two one-tile CTAs per SM)
-    default: return launch_tc_bn<64, 1>(p, a, m.pdl, s);
+  const int bn = tc_token_tile(m.M);
+  // (three 64-row token tiles per CTA sharing each expanded weight k-block, TT = 3, were
+  // measured 1.3x slower on the 2.7B prefill than two one-tile CTAs per SM)
+  if (!m.fixed) {
+    if (bn == 16) return launch_tc_bn<16, 1, true>(p, a, m.pdl, s);
+    if (bn == 32) return launch_tc_bn<32, 1, true>(p, a, m.pdl, s);
+    return launch_tc_bn<64, 1, true>(p, a, m.pdl, s);
   }
+  if (bn == 16) return launch_tc_bn<16, 1, false>(p, a, m.pdl, s);
+  if (bn == 32) return launch_tc_bn<32, 1, false>(p, a, m.pdl, s);
+  return launch_tc_bn<64, 1, false>(p, a, m.pdl, s);
 }
 
 cudaError_t launch_matmul_tc(const MatmulArgs& a, int splits, cudaStream_t s) {

@@ -61,7 +61,8 @@ def test_cli_text_mode_matches_reference_cli(cuda, blob_cache, extra):
     tok = os.path.join(GOLDEN, "tokenizer_toy.mmtok")
     for prompt in ("Once upon a time, there was", "Café crème 中文 😀"):
         common = ["--blob", blob, "--tokenizer", tok, "--gen", "24", *extra, prompt]
-        rc_r, out_r, _ = _run(oracle.REF_CLI, common)
-        rc_c, out_c, err_c = _run(nb.CLI, common)
-        assert rc_r == 0 and rc_c == 0, err_c
-        assert out_c == out_r, (prompt, out_c, out_r)
+        # raw bytes: a random-init model emits byte-fallback tokens, not always valid UTF-8
+        r = subprocess.run([oracle.REF_CLI] + common, capture_output=True, timeout=600)
+        c = subprocess.run([nb.CLI] + common, capture_output=True, timeout=600)
+        assert r.returncode == 0 and c.returncode == 0, c.stderr
+        assert c.stdout == r.stdout, (prompt, c.stdout, r.stdout)

@@ -85,37 +85,55 @@ def test_bitlinear_sweep_fixed_exact(cuda, orc, M, K, N):
     assert bits_equal(norm, r_norm)
 
 
-@pytest.mark.parametrize("K,N", [(2048, 2048), (6912, 2560)])
-def test_bitlinear_sweep_float(cuda, orc, K, N):
-    x, nw, wq = sweep_inputs(16, K, N, seed=K + N)
+@pytest.mark.parametrize("K,N", SWEEP_KN)
+@pytest.mark.parametrize("M", [1, 16, 64])
+def test_bitlinear_sweep_float(cuda, orc, M, K, N):
+    """Float on every sweep shape: the few-row fused kernel (M = 1) and the bf16 tensor-core
+    path (M >= 16); norms bit for bit, outputs within the Float tolerance."""
+    x, nw, wq = sweep_inputs(M, K, N, seed=K + N + M)
     out, _, norm = run_gpu(cuda, x, nw, wq, 20.0, "float")
     r_out, _, r_norm = orc.bitlinear(x, nw, wq, 20.0, act_quant=0, want_norm=True)
     assert bits_equal(norm, r_norm)
     assert_float_close(out, r_out)
+    if M == 1:  # without norm_out the C ABI takes the single fused launch
+        o1, _, _ = api.bitlinear(to_dev(x, cuda), to_dev(nw, cuda), api.repack_ternary(to_dev(wq, cuda)),
+                                 20.0, N, act_quant="float")
+        assert_float_close(o1.cpu().numpy(), r_out)
 
 
+@pytest.mark.parametrize("K,N", [(2560, 13824), (2048, 11264), (6912, 2560)])
 @pytest.mark.parametrize("M", [512, 4096])
-def test_bitlinear_large_m_rows(cuda, orc, M):
+def test_bitlinear_large_m_rows(cuda, orc, M, K, N):
     """Full sweep sizes: rows are independent, so sampled rows must match the oracle run on
-    those rows alone (bit-exact) -- a size-independent check of the large-M path."""
-    K, N = 2560, 13824
-    x, nw, wq = sweep_inputs(M, K, N, seed=M)
-    out, acc, _ = run_gpu(cuda, x, nw, wq, 20.0, "fixed")
+    those rows alone (bit-exact in FixedQ510, within tolerance in Float) -- a size-independent
+    check of the large-M path."""
+    x, nw, wq = sweep_inputs(M, K, N, seed=M + K)
     rows = np.random.default_rng(M).choice(M, 6, replace=False)
+    out, acc, _ = run_gpu(cuda, x, nw, wq, 20.0, "fixed")
     r_out, r_acc, _ = orc.bitlinear(x[rows], nw, wq, 20.0, act_quant=1)
     assert np.array_equal(acc[rows], r_acc)
     assert bits_equal(out[rows], r_out)
+    fo, _, _ = run_gpu(cuda, x, nw, wq, 20.0, "float")
+    f_out, _, _ = orc.bitlinear(x[rows], nw, wq, 20.0, act_quant=0)
+    assert_float_close(fo[rows], f_out)
 
 
-def test_bitlinear_many_rows_all_match(cuda, orc):
-    """M >= 1024 without a k-split (many token tiles); ragged M, K and N, every row checked
-    bit for bit."""
-    M, K, N = 1100, 1000, 700
-    x, nw, wq = sweep_inputs(M, K, N, seed=11)
-    out, acc, _ = run_gpu(cuda, x, nw, wq, 20.0, "fixed")
-    r_out, r_acc, _ = orc.bitlinear(x, nw, wq, 20.0, act_quant=1)
+@pytest.mark.parametrize("M,K,N", [(1100, 1000, 700), (1030, 1003, 96), (1024, 5632, 64)])
+def test_bitlinear_many_rows_all_match(cuda, orc, M, K, N):
+    """M >= 1024: the two-pass prep (an 8-lane exact chain per row, then the quantisation
+    pass) and the tensor-core matmul without a k-split; ragged M, K and N, a K % 8 scalar
+    tail, saturating outliers; every row's accumulators, outputs and norm bit for bit."""
+    x, nw, wq = sweep_inputs(M, K, N, seed=11 + K)
+    x[::7, :4] = np.float32(600.0)  # y * 1024 past the int16 range on some rows
+    out, acc, norm = run_gpu(cuda, x, nw, wq, 20.0, "fixed")
+    r_out, r_acc, r_norm = orc.bitlinear(x, nw, wq, 20.0, act_quant=1, want_norm=True)
     assert np.array_equal(acc, r_acc)
     assert bits_equal(out, r_out)
+    assert bits_equal(norm, r_norm)
+    fo, _, fn = run_gpu(cuda, x, nw, wq, 20.0, "float")
+    f_out, _, f_norm = orc.bitlinear(x, nw, wq, 20.0, act_quant=0, want_norm=True)
+    assert bits_equal(fn, f_norm)
+    assert_float_close(fo, f_out)
 
 
 @pytest.mark.parametrize("M,K,N", [(64, 2048, 101), (40, 2048, 200), (20, 1000, 66), (64, 5632, 256),
