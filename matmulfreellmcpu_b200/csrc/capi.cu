@@ -184,7 +184,7 @@ void run_bitlinear(int k, float* const* outs, const float* x, const float* const
   }
   const size_t kp = static_cast<size_t>(padded_k(static_cast<int64_t>(in_dim)));
   const size_t per = fixed ? a256(2 * rows * kp) + a256(rows * 4) : a256(rows * kp * 4);
-  char* base = scratch(static_cast<size_t>(k) * per + a256(rows * 8));
+  char* base = scratch(static_cast<size_t>(k) * per);
   PrepArgs p;
   p.x = x;
   p.nproj = k;
@@ -201,7 +201,6 @@ void run_bitlinear(int k, float* const* outs, const float* x, const float* const
   p.bf16 = !fixed && static_cast<int>(rows) >= kTcMinRows;
   uint32_t* err = reinterpret_cast<uint32_t*>(base) + kAsyncFlagWord;
   p.err = err;
-  p.rstd_ws = reinterpret_cast<float2*>(base + 256 + static_cast<size_t>(k) * per);
   for (int j = 0; j < k; ++j) {
     char* b = base + 256 + j * per;
     p.normw[j] = nws[j];

@@ -360,119 +360,138 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepArgs a, int mode
 }
 
 // ------------------------------------------------------------------------------ prep, many rows
-// For thousands of rows (prefill) the prep runs in two passes instead of one CTA per row:
-//   prep_rstd_kernel   one 8-lane group per row computes the row's rstd values in the exact
-//                      AVX2 order: the row transform's (r1, from x) and the BitLinear norm's
-//                      (r2, from t), the second chain recomputing t = transform(x) on the fly
-//                      (no row is staged; a warp serves 4 rows, so the serial chains of many
-//                      rows overlap on every SM)
-//   prep_quant_kernel  elementwise over row blocks: t, the projections' normalized inputs,
-//                      Q5.10 planes (or Float activations) and row sums; the norm weights of
-//                      a column are loaded once per block of rows
-// Same arithmetic, element by element, as prep_kernel.
-constexpr int kRstdThreads = 256, kQuantRows = 8, kQuantThreads = 256;
+// Thousands of rows (prefill): R <= 8 rows per CTA instead of one, each staged by one bulk
+// copy (with the gate operand in the gated mode). The norm weights are read through L1 -- every
+// CTA reads the same ones -- instead of being staged per row, which dominated the per-row CTA.
+// The flow per row is prep_kernel's: chain 1 (an 8-lane group per row, all R rows at once),
+// the row transform by all threads, chain 2, then the projections' normalisation, Q5.10 planes
+// (or Float activations) and row sums; the arithmetic is the same element by element.
+constexpr int kRowsThreads = 256, kRowsMax = 8, kRowsSmem = 96 * 1024;
 
-__device__ __forceinline__ float row_transform(const PrepArgs& a, int mode, float x, float r1,
-                                               float w, float o, int c) {
-  if (mode == kPrepPlain) return x;
-  float t = norm_x(x, r1, w);
-  if (mode == kPrepSwishgate) t = __fmul_rn(t, silu_x(o, in_body(c, a.K)));
-  return t;
+// rows per CTA: as many as fit kRowsSmem (at least 1, at most kRowsMax)
+static int prep_rows_per_cta(int K, int mode) {
+  const int64_t per_row = static_cast<int64_t>((K + 3) & ~3) * 4 * (mode == kPrepSwishgate ? 2 : 1);
+  const int64_t r = kRowsSmem / per_row;
+  return static_cast<int>(r < 1 ? 1 : (r > kRowsMax ? kRowsMax : r));
 }
 
-// The exact sum of squares of f(c), c < K, for the 8-lane group of this thread (lane j runs
-// chain j over c = 8i + j, batches of 8 values are computed before their FMAs), then the
-// AVX2 tree and the scalar tail; every lane of the group gets the sum.
-template <class F>
-__device__ __forceinline__ float sumsq_exact8_f(int K, F&& f) {
-  const int j = threadIdx.x & 7, n8 = K >> 3;
-  float acc = 0.0f;
-  int i = 0;
-  for (; i + 8 <= n8; i += 8) {
-    float v[8];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) v[u] = f(8 * (i + u) + j);
-#pragma unroll
-    for (int u = 0; u < 8; ++u) acc = __fmaf_rn(v[u], v[u], acc);
-  }
-  for (; i < n8; ++i) {
-    const float v = f(8 * i + j);
-    acc = __fmaf_rn(v, v, acc);
-  }
-  float sum = hsum8_lanes(acc);
-  for (int c = n8 * 8; c < K; ++c) {
-    const float v = f(c);
-    sum = __fadd_rn(sum, __fmul_rn(v, v));
-  }
-  return sum;
-}
-
-__global__ void __launch_bounds__(kRstdThreads) prep_rstd_kernel(PrepArgs a, int mode, float2* rstd) {
-  grid_dep_launch();
-  grid_dep_wait();
-  const int64_t g = (blockIdx.x * static_cast<int64_t>(kRstdThreads) + threadIdx.x) >> 3;
-  // groups past the last row repeat it (the 8-lane shuffles involve the whole warp) and
-  // store nothing
-  const int64_t m = g < a.M ? g : a.M - 1;
-  const int K = a.K;
-  const float* x = a.x + m * K;
-  const float* o = a.o ? a.o + m * K : nullptr;
-  const float Kf = static_cast<float>(K);
-  float r1 = 0.0f;
-  if (mode != kPrepPlain) r1 = rstd_of(sumsq_exact8_f(K, [&](int c) { return __ldg(x + c); }), Kf, a.eps);
-  const float r2 = rstd_of(sumsq_exact8_f(K, [&](int c) {
-                             return row_transform(a, mode, __ldg(x + c), r1, mode == kPrepPlain ? 0.0f : __ldg(a.prew + c),
-                                                  mode == kPrepSwishgate ? __ldg(o + c) : 0.0f, c);
-                           }),
-                           Kf, a.eps);
-  if ((threadIdx.x & 7) == 0 && g < a.M) rstd[m] = make_float2(r1, r2);
-}
-
-__global__ void __launch_bounds__(kQuantThreads) prep_quant_kernel(PrepArgs a, int mode,
-                                                                   const float2* __restrict__ rstd) {
-  grid_dep_launch();
-  grid_dep_wait();
-  __shared__ int s_red[3][kQuantRows][kQuantThreads / 32];
-  const int K = a.K, tid = threadIdx.x, nproj = a.nproj;
+__global__ void __launch_bounds__(kRowsThreads) prep_rows_kernel(PrepArgs a, int mode, int R) {
+  extern __shared__ __align__(16) float sb[];
+  __shared__ float s_r1[kRowsMax], s_r2[kRowsMax];
+  __shared__ int s_red[3][kRowsMax][kRowsThreads / 32];
+  __shared__ __align__(8) uint64_t s_bar;
+  const int K = a.K, tid = threadIdx.x, K4 = (K + 3) & ~3;
   const int64_t Kp = padded_k(K);
-  const int64_t m0 = static_cast<int64_t>(blockIdx.x) * kQuantRows;
-  // rows of a multiple of 4 floats at 16-byte aligned bases: 16-byte loads
-  const bool vec = (K & 3) == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 &&
-                   (mode != kPrepSwishgate || (reinterpret_cast<uintptr_t>(a.o) & 15) == 0);
-  float2 rs[kQuantRows];
-#pragma unroll
-  for (int r = 0; r < kQuantRows; ++r) rs[r] = m0 + r < a.M ? rstd[m0 + r] : make_float2(0.0f, 0.0f);
-  int local[3][kQuantRows] = {};
-  for (int c0 = 4 * tid; c0 < Kp; c0 += 4 * kQuantThreads) {
-    float pw[4], nwv[3][4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int c = c0 + u;
-      pw[u] = (mode != kPrepPlain && c < K) ? __ldg(a.prew + c) : 0.0f;
-#pragma unroll
-      for (int j = 0; j < 3; ++j) nwv[j][u] = (j < nproj && c < K) ? __ldg(a.normw[j] + c) : 0.0f;
-    }
-#pragma unroll  // unrolled: local[][r] and rs[r] stay in registers
-    for (int r = 0; r < kQuantRows; ++r) {
-      const int64_t m = m0 + r;
-      if (m >= a.M) break;
-      float xv[4], ov[4] = {0.0f, 0.0f, 0.0f, 0.0f}, t[4];
-      load4(a.x + m * K, c0, K, vec, xv);
-      if (mode == kPrepSwishgate) load4(a.o + m * K, c0, K, vec, ov);
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int c = c0 + u;
-        t[u] = c < K ? row_transform(a, mode, xv[u], rs[r].x, pw[u], ov[u], c) : 0.0f;
-        if (a.pre_out && c < K) a.pre_out[m * K + c] = t[u];
+  const int64_t m0 = static_cast<int64_t>(blockIdx.x) * R;
+  const int nr = static_cast<int>(a.M - m0 < R ? a.M - m0 : R);  // rows of this CTA
+  const bool swish = mode == kPrepSwishgate;
+  float* xs = sb;                                  // [R][K4]: x, then t in place
+  float* os = sb + static_cast<int64_t>(R) * K4;   // [R][K4]: the gate operand (gated mode)
+  const bool bulk = (K & 3) == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 &&
+                    (!swish || (reinterpret_cast<uintptr_t>(a.o) & 15) == 0);
+  if (bulk && tid == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(shared_addr(&s_bar)));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (bulk) __syncthreads();
+  grid_dep_launch();
+  grid_dep_wait();
+  if (bulk) {
+    if (tid == 0) {
+      const uint32_t bytes = static_cast<uint32_t>(K) * 4u;
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(shared_addr(&s_bar)),
+                   "r"(bytes * static_cast<uint32_t>(nr) * (swish ? 2u : 1u))
+                   : "memory");
+      for (int r = 0; r < nr; ++r) {
+        row_bulk_copy(xs + static_cast<int64_t>(r) * K4, a.x + (m0 + r) * K, bytes, &s_bar);
+        if (swish) row_bulk_copy(os + static_cast<int64_t>(r) * K4, a.o + (m0 + r) * K, bytes, &s_bar);
       }
+    }
+    bool done = false;
+    for (uint32_t i = 0; i < a.row_polls && !done; ++i) done = row_bar_done(&s_bar);
+    if (__syncthreads_or(!done)) {  // (uniform) report, drain the copies, leave no output
+      if (tid == 0 && a.err) atomicOr(a.err, kErrTimeout);
+      for (uint32_t i = 0; i < kRowSpin && !row_bar_done(&s_bar); ++i) {
+      }
+      return;
+    }
+  } else {
+    for (int64_t i = tid; i < static_cast<int64_t>(nr) * K; i += kRowsThreads) {
+      const int r = static_cast<int>(i / K), c = static_cast<int>(i % K);
+      xs[static_cast<int64_t>(r) * K4 + c] = a.x[(m0 + r) * K + c];
+      if (swish) os[static_cast<int64_t>(r) * K4 + c] = a.o[(m0 + r) * K + c];
+    }
+    __syncthreads();
+  }
+  // the 8-lane groups of the chains: rows 0..nr-1 on threads 0..8 nr-1
+  const int active = 8 * nr - 32 * (tid >> 5);
+  const unsigned mask = active >= 32 ? 0xffffffffu : (active > 0 ? (1u << active) - 1u : 0u);
+  const int cr = tid >> 3;  // the chain row of this thread (tid < 8 nr)
+  if (mode != kPrepPlain) {
+    if (tid < 8 * nr) {
+      const float r = rstd_of(sumsq_exact8(xs + static_cast<int64_t>(cr) * K4, K, mask), static_cast<float>(K), a.eps);
+      if ((tid & 7) == 0) s_r1[cr] = r;
+    }
+    __syncthreads();
+    // t = rmsnorm(x) * prew (* silu(o)) in place, four columns per thread and step
+    for (int r = 0; r < nr; ++r) {
+      const float r1 = s_r1[r];
+      float* xr = xs + static_cast<int64_t>(r) * K4;
+      const float* orow = os + static_cast<int64_t>(r) * K4;
+      for (int c0 = tid; c0 < K; c0 += 4 * kRowsThreads) {
+        float sg[4] = {1.0f, 1.0f, 1.0f, 1.0f};
+        if (swish) {
+          float xo[4];
+          bool bd[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int c = c0 + u * kRowsThreads;
+            xo[u] = c < K ? orow[c] : 0.0f;
+            bd[u] = in_body(c, K);
+          }
+          silu_n(xo, bd, sg);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int c = c0 + u * kRowsThreads;
+          if (c >= K) break;
+          float t = norm_x(xr[c], r1, __ldg(a.prew + c));
+          if (swish) t = __fmul_rn(t, sg[u]);
+          xr[c] = t;
+          if (a.pre_out) a.pre_out[(m0 + r) * K + c] = t;
+        }
+      }
+    }
+    __syncthreads();
+  }
+  if (a.nproj == 0) return;
+  if (tid < 8 * nr) {
+    const float r = rstd_of(sumsq_exact8(xs + static_cast<int64_t>(cr) * K4, K, mask), static_cast<float>(K), a.eps);
+    if ((tid & 7) == 0) s_r2[cr] = r;
+  }
+  __syncthreads();
+  int local[3][kRowsMax] = {};
+  for (int c0 = 4 * tid; c0 < Kp; c0 += 4 * kRowsThreads) {
+    float nwv[3][4];
+#pragma unroll
+    for (int j = 0; j < 3; ++j)
+#pragma unroll
+      for (int u = 0; u < 4; ++u) nwv[j][u] = (j < a.nproj && c0 + u < K) ? __ldg(a.normw[j] + c0 + u) : 0.0f;
+#pragma unroll
+    for (int r = 0; r < kRowsMax; ++r) {
+      if (r >= nr) break;
+      const int64_t m = m0 + r;
+      float t[4];
+      load4(xs + static_cast<int64_t>(r) * K4, c0, K, true, t);
+      const float r2 = s_r2[r];
 #pragma unroll
       for (int j = 0; j < 3; ++j) {
-        if (j >= nproj) break;
+        if (j >= a.nproj) break;
         float y[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           const int c = c0 + u;
-          y[u] = c < K ? norm_x(t[u], rs[r].y, nwv[j][u]) : 0.0f;
+          y[u] = c < K ? norm_x(t[u], r2, nwv[j][u]) : 0.0f;
           if (j == 0 && a.norm_out && c < K) a.norm_out[m * K + c] = y[u];
         }
         if (a.fixed) {
@@ -503,17 +522,17 @@ __global__ void __launch_bounds__(kQuantThreads) prep_quant_kernel(PrepArgs a, i
 #pragma unroll
   for (int j = 0; j < 3; ++j)
 #pragma unroll
-    for (int r = 0; r < kQuantRows; ++r) {
+    for (int r = 0; r < kRowsMax; ++r) {
       const int v = __reduce_add_sync(0xffffffffu, local[j][r]);
       if (lane == 0) s_red[j][r][warp] = v;
     }
   __syncthreads();
-  if (tid < nproj * kQuantRows) {
-    const int j = tid / kQuantRows, r = tid % kQuantRows;
-    if (m0 + r < a.M) {
+  if (tid < a.nproj * kRowsMax) {
+    const int j = tid / kRowsMax, r = tid % kRowsMax;
+    if (r < nr) {
       int total = 0;
 #pragma unroll
-      for (int w = 0; w < kQuantThreads / 32; ++w) total += s_red[j][r][w];
+      for (int w = 0; w < kRowsThreads / 32; ++w) total += s_red[j][r][w];
       a.rowsum[j][m0 + r] = total;
     }
   }
@@ -549,12 +568,16 @@ cudaError_t launch_prep(const PrepArgs& a, cudaStream_t s) {
         !al16(a.mix_lb) || !al16(a.mix_out))
       return cudaErrorInvalidValue;
   }
-  if (a.M >= kPrepManyRows && a.rstd_ws && !a.mix_i) {  // many rows: the two-pass prep
-    cudaError_t e = launch_k(prep_rstd_kernel, dim3(static_cast<unsigned>(ceil_div(int64_t(a.M) * 8, kRstdThreads))),
-                             dim3(kRstdThreads), 0, s, a.pdl, a, mode, a.rstd_ws);
-    if (e != cudaSuccess) return e;
-    return launch_k(prep_quant_kernel, dim3(static_cast<unsigned>(ceil_div(a.M, kQuantRows))),
-                    dim3(kQuantThreads), 0, s, true, a, mode, static_cast<const float2*>(a.rstd_ws));
+  if (a.M >= kPrepManyRows && !a.mix_i) {  // many rows: several per CTA
+    const int R = prep_rows_per_cta(a.K, mode);
+    const size_t rsmem = static_cast<size_t>(R) * ((a.K + 3) & ~3) * 4 * (mode == kPrepSwishgate ? 2 : 1);
+    if (rsmem <= kMaxDynSmem) {
+      if (rsmem > 48 * 1024) raise_smem_limit(reinterpret_cast<const void*>(prep_rows_kernel));
+      PrepArgs q = a;
+      q.row_polls = row_polls();
+      return launch_k(prep_rows_kernel, dim3(static_cast<unsigned>(ceil_div(int64_t(a.M), R))), dim3(kRowsThreads),
+                      rsmem, s, a.pdl, q, mode, R);
+    }
   }
   if (smem > 48 * 1024) raise_smem_limit(reinterpret_cast<const void*>(prep_kernel));
   PrepArgs q = a;

@@ -36,8 +36,6 @@ struct PrepArgs {
   bool pdl = false;              // launch as a programmatic dependent of the previous kernel
   uint32_t* err = nullptr;       // optional: bit kErrTimeout on a timed-out wait
   uint32_t row_polls = 0;        // set by launch_prep: polls of the row-staging wait
-  float2* rstd_ws = nullptr;     // optional [M] workspace: with it, M >= kPrepManyRows rows
-                                 // take the two-pass prep (rstd pass, then quantisation pass)
   // kPrepSwishgate of one decode step with the token mixer fused in: o is not read but
   // computed here from the i / f projections and the recurrent state (which is updated), as
   // launch_mixer does for len 1; needs K % 4 == 0, 16-byte aligned rows and K >= 8

@@ -273,7 +273,7 @@ void Model::ensure_ws(size_t rows) {
   size_t o_h = carve(rows * H * 4), o_resid = carve(rows * H * 4), o_ib = carve(rows * H * 4),
          o_fb = carve(rows * H * 4), o_gb = carve(rows * H * 4), o_recur = carve(rows * H * 4),
          o_y = carve(rows * 2 * I * 4), o_z = carve(rows * I * 4), o_lg = carve(rows * V * 4),
-         o_hl = carve(rows * H * 4), o_ids = carve(rows * 8), o_rstd = carve(rows * 8);
+         o_hl = carve(rows * H * 4), o_ids = carve(rows * 8);
   size_t o_pl[3], o_rs[3], o_yf[3];
   for (int j = 0; j < 3; ++j) {
     o_pl[j] = carve((fixed_ ? 2 : 4) * rows * Kp);  // u8 planes, or Float's bf16 hi / lo planes
@@ -293,7 +293,6 @@ void Model::ensure_ws(size_t rows) {
   logits_ = reinterpret_cast<float*>(b + o_lg);
   hl_ = reinterpret_cast<float*>(b + o_hl);
   ids_ = reinterpret_cast<int64_t*>(b + o_ids);
-  rstd_ws_ = reinterpret_cast<float2*>(b + o_rstd);
   for (int j = 0; j < 3; ++j) {
     planes_[j] = reinterpret_cast<int8_t*>(b + o_pl[j]);
     rowsum_[j] = reinterpret_cast<int32_t*>(b + o_rs[j]);
@@ -391,7 +390,6 @@ void Model::prep(const PrepArgs& p) {
   PrepArgs q = p;
   q.pdl = pdl_;
   q.err = err_;
-  q.rstd_ws = rstd_ws_;
   // the BitLinear of these rows runs on the tensor cores: FixedQ510 low planes as lo - 128,
   // Float activations as bf16 hi / lo planes
   q.lo_signed = fixed_ && tc_rows(q.M);

@@ -180,7 +180,6 @@ class Model {
   int8_t* planes_[3] = {};
   int32_t* rowsum_[3] = {};
   float* yf_[3] = {};
-  float2* rstd_ws_ = nullptr;      // per-row rstd pair of the two-pass prep (many rows)
   int64_t* ids_ = nullptr;
 
   // state and decode loop

@@ -120,9 +120,10 @@ def test_bitlinear_large_m_rows(cuda, orc, M, K, N):
 
 @pytest.mark.parametrize("M,K,N", [(1100, 1000, 700), (1030, 1003, 96), (1024, 5632, 64)])
 def test_bitlinear_many_rows_all_match(cuda, orc, M, K, N):
-    """M >= 1024: the two-pass prep (an 8-lane exact chain per row, then the quantisation
-    pass) and the tensor-core matmul without a k-split; ragged M, K and N, a K % 8 scalar
-    tail, saturating outliers; every row's accumulators, outputs and norm bit for bit."""
+    """M >= 1024: the many-rows prep (up to 8 rows per CTA, their 8-lane exact chains side by
+    side; a ragged last CTA; K % 4 != 0 rows staged without the bulk copy) and the tensor-core
+    matmul without a k-split; ragged M, K and N, a K % 8 scalar tail, saturating outliers;
+    every row's accumulators, outputs and norm bit for bit."""
     x, nw, wq = sweep_inputs(M, K, N, seed=11 + K)
     x[::7, :4] = np.float32(600.0)  # y * 1024 past the int16 range on some rows
     out, acc, norm = run_gpu(cuda, x, nw, wq, 20.0, "fixed")
