@@ -128,6 +128,30 @@ __device__ __forceinline__ int32_t quant_x(float y, float qs, bool body) {
   return body ? bq : tq;
 }
 
+// quant_x's SIMD-body form for 4 elements of the body, straight into the two byte-plane words
+// (byte u = element u) plus their code sum, without a float->int conversion: clamping before
+// rounding equals rounding before clamping (integer bounds); NaN and q <= -2^31 clamp to
+// -32768 like cvtps2dq's INT32_MIN does, q >= 2^31 is selected to it; the clamped value is
+// rounded half to even by one round-to-nearest add of 1.5 * 2^23 (the sum lies in [2^23,
+// 2^24), where the float spacing is 1), after which its low 16 bits hold the code in two's
+// complement. `lo_xor` is 0x80808080 for the signed low plane, else 0.
+__device__ __forceinline__ void quant4_body_planes(const float (&y)[4], float qs, uint32_t lo_xor,
+                                                   uint32_t& hi, uint32_t& lo, int32_t& sum) {
+  uint32_t b[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const float q = __fmul_rn(y[u], qs);
+    float c = fminf(fmaxf(q, -32768.0f), 32767.0f);  // fmaxf(NaN, v) = v
+    c = q >= 2147483648.0f ? -32768.0f : c;
+    b[u] = __float_as_uint(__fadd_rn(c, 12582912.0f));
+    sum += static_cast<int32_t>(b[u] - 0x4B400000u);
+  }
+  const uint32_t t01 = __byte_perm(b[0], b[1], 0x5140);  // [lo0, lo1, hi0, hi1]
+  const uint32_t t23 = __byte_perm(b[2], b[3], 0x5140);  // [lo2, lo3, hi2, hi3]
+  lo = __byte_perm(t01, t23, 0x5410) ^ lo_xor;
+  hi = __byte_perm(t01, t23, 0x7632);
+}
+
 // Lower-bounded forget gate of layers > 0 (hgrn_model.cpp:116-124), as fused by the build.
 __device__ __forceinline__ float lower_bound_x(float f, float lb) {
   return __fmaf_rn(__fadd_rn(1.0f, -lb), f, lb);

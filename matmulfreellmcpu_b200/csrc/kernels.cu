@@ -323,13 +323,17 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepArgs a, int mode
       }
       if (a.fixed) {
         uint32_t hi = 0, lo = 0;
+        if (c0 + 3 < (K & ~7)) {  // 4 body elements
+          quant4_body_planes(y, a.qs, a.lo_signed ? 0x80808080u : 0u, hi, lo, local[j]);
+        } else {
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int c = c0 + u;
-          const int32_t q = c < K ? quant_x(y[u], a.qs, in_body(c, K)) : 0;
-          local[j] += q;
-          hi |= static_cast<uint32_t>((q >> 8) & 0xff) << (8 * u);
-          lo |= static_cast<uint32_t>((q & 0xff) ^ (a.lo_signed ? 0x80 : 0)) << (8 * u);
+          for (int u = 0; u < 4; ++u) {
+            const int c = c0 + u;
+            const int32_t q = c < K ? quant_x(y[u], a.qs, in_body(c, K)) : 0;
+            local[j] += q;
+            hi |= static_cast<uint32_t>((q >> 8) & 0xff) << (8 * u);
+            lo |= static_cast<uint32_t>((q & 0xff) ^ (a.lo_signed ? 0x80 : 0)) << (8 * u);
+          }
         }
         *reinterpret_cast<uint32_t*>(a.planes[j] + static_cast<int64_t>(m) * Kp + c0) = hi;
         *reinterpret_cast<uint32_t*>(a.planes[j] + (static_cast<int64_t>(a.M) + m) * Kp + c0) = lo;
@@ -368,9 +372,17 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepArgs a, int mode
 // (or Float activations) and row sums; the arithmetic is the same element by element.
 constexpr int kRowsThreads = 256, kRowsMax = 8, kRowsSmem = 96 * 1024;
 
+// Floats from one staged row to the next: a multiple of 4 (rows 16-byte aligned) that is 8
+// more than a multiple of 32, so that the 8-lane chain groups of the 4 rows of a warp read
+// 4 different octets of banks.
+__host__ __device__ inline int rows_stride(int K) {
+  const int k4 = (K + 3) & ~3;
+  return k4 + ((8 - (k4 & 31)) & 31);
+}
+
 // rows per CTA: as many as fit kRowsSmem (at least 1, at most kRowsMax)
 static int prep_rows_per_cta(int K, int mode) {
-  const int64_t per_row = static_cast<int64_t>((K + 3) & ~3) * 4 * (mode == kPrepSwishgate ? 2 : 1);
+  const int64_t per_row = static_cast<int64_t>(rows_stride(K)) * 4 * (mode == kPrepSwishgate ? 2 : 1);
   const int64_t r = kRowsSmem / per_row;
   return static_cast<int>(r < 1 ? 1 : (r > kRowsMax ? kRowsMax : r));
 }
@@ -380,13 +392,13 @@ __global__ void __launch_bounds__(kRowsThreads) prep_rows_kernel(PrepArgs a, int
   __shared__ float s_r1[kRowsMax], s_r2[kRowsMax];
   __shared__ int s_red[3][kRowsMax][kRowsThreads / 32];
   __shared__ __align__(8) uint64_t s_bar;
-  const int K = a.K, tid = threadIdx.x, K4 = (K + 3) & ~3;
+  const int K = a.K, tid = threadIdx.x, RS = rows_stride(K);
   const int64_t Kp = padded_k(K);
   const int64_t m0 = static_cast<int64_t>(blockIdx.x) * R;
   const int nr = static_cast<int>(a.M - m0 < R ? a.M - m0 : R);  // rows of this CTA
   const bool swish = mode == kPrepSwishgate;
-  float* xs = sb;                                  // [R][K4]: x, then t in place
-  float* os = sb + static_cast<int64_t>(R) * K4;   // [R][K4]: the gate operand (gated mode)
+  float* xs = sb;                                  // [R][RS]: x, then t in place
+  float* os = sb + static_cast<int64_t>(R) * RS;   // [R][RS]: the gate operand (gated mode)
   const bool bulk = (K & 3) == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 &&
                     (!swish || (reinterpret_cast<uintptr_t>(a.o) & 15) == 0);
   if (bulk && tid == 0) {
@@ -403,8 +415,8 @@ __global__ void __launch_bounds__(kRowsThreads) prep_rows_kernel(PrepArgs a, int
                    "r"(bytes * static_cast<uint32_t>(nr) * (swish ? 2u : 1u))
                    : "memory");
       for (int r = 0; r < nr; ++r) {
-        row_bulk_copy(xs + static_cast<int64_t>(r) * K4, a.x + (m0 + r) * K, bytes, &s_bar);
-        if (swish) row_bulk_copy(os + static_cast<int64_t>(r) * K4, a.o + (m0 + r) * K, bytes, &s_bar);
+        row_bulk_copy(xs + static_cast<int64_t>(r) * RS, a.x + (m0 + r) * K, bytes, &s_bar);
+        if (swish) row_bulk_copy(os + static_cast<int64_t>(r) * RS, a.o + (m0 + r) * K, bytes, &s_bar);
       }
     }
     bool done = false;
@@ -418,8 +430,8 @@ __global__ void __launch_bounds__(kRowsThreads) prep_rows_kernel(PrepArgs a, int
   } else {
     for (int64_t i = tid; i < static_cast<int64_t>(nr) * K; i += kRowsThreads) {
       const int r = static_cast<int>(i / K), c = static_cast<int>(i % K);
-      xs[static_cast<int64_t>(r) * K4 + c] = a.x[(m0 + r) * K + c];
-      if (swish) os[static_cast<int64_t>(r) * K4 + c] = a.o[(m0 + r) * K + c];
+      xs[static_cast<int64_t>(r) * RS + c] = a.x[(m0 + r) * K + c];
+      if (swish) os[static_cast<int64_t>(r) * RS + c] = a.o[(m0 + r) * K + c];
     }
     __syncthreads();
   }
@@ -429,15 +441,15 @@ __global__ void __launch_bounds__(kRowsThreads) prep_rows_kernel(PrepArgs a, int
   const int cr = tid >> 3;  // the chain row of this thread (tid < 8 nr)
   if (mode != kPrepPlain) {
     if (tid < 8 * nr) {
-      const float r = rstd_of(sumsq_exact8(xs + static_cast<int64_t>(cr) * K4, K, mask), static_cast<float>(K), a.eps);
+      const float r = rstd_of(sumsq_exact8(xs + static_cast<int64_t>(cr) * RS, K, mask), static_cast<float>(K), a.eps);
       if ((tid & 7) == 0) s_r1[cr] = r;
     }
     __syncthreads();
     // t = rmsnorm(x) * prew (* silu(o)) in place, four columns per thread and step
     for (int r = 0; r < nr; ++r) {
       const float r1 = s_r1[r];
-      float* xr = xs + static_cast<int64_t>(r) * K4;
-      const float* orow = os + static_cast<int64_t>(r) * K4;
+      float* xr = xs + static_cast<int64_t>(r) * RS;
+      const float* orow = os + static_cast<int64_t>(r) * RS;
       for (int c0 = tid; c0 < K; c0 += 4 * kRowsThreads) {
         float sg[4] = {1.0f, 1.0f, 1.0f, 1.0f};
         if (swish) {
@@ -466,12 +478,14 @@ __global__ void __launch_bounds__(kRowsThreads) prep_rows_kernel(PrepArgs a, int
   }
   if (a.nproj == 0) return;
   if (tid < 8 * nr) {
-    const float r = rstd_of(sumsq_exact8(xs + static_cast<int64_t>(cr) * K4, K, mask), static_cast<float>(K), a.eps);
+    const float r = rstd_of(sumsq_exact8(xs + static_cast<int64_t>(cr) * RS, K, mask), static_cast<float>(K), a.eps);
     if ((tid & 7) == 0) s_r2[cr] = r;
   }
   __syncthreads();
   int local[3][kRowsMax] = {};
+  const uint32_t lo_xor = a.lo_signed ? 0x80808080u : 0u;
   for (int c0 = 4 * tid; c0 < Kp; c0 += 4 * kRowsThreads) {
+    const bool body4 = c0 + 3 < (K & ~7);  // 4 body elements
     float nwv[3][4];
 #pragma unroll
     for (int j = 0; j < 3; ++j)
@@ -482,7 +496,7 @@ __global__ void __launch_bounds__(kRowsThreads) prep_rows_kernel(PrepArgs a, int
       if (r >= nr) break;
       const int64_t m = m0 + r;
       float t[4];
-      load4(xs + static_cast<int64_t>(r) * K4, c0, K, true, t);
+      load4(xs + static_cast<int64_t>(r) * RS, c0, K, true, t);
       const float r2 = s_r2[r];
 #pragma unroll
       for (int j = 0; j < 3; ++j) {
@@ -496,13 +510,17 @@ __global__ void __launch_bounds__(kRowsThreads) prep_rows_kernel(PrepArgs a, int
         }
         if (a.fixed) {
           uint32_t hi = 0, lo = 0;
+          if (body4) {
+            quant4_body_planes(y, a.qs, lo_xor, hi, lo, local[j][r]);
+          } else {
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int c = c0 + u;
-            const int32_t q = c < K ? quant_x(y[u], a.qs, in_body(c, K)) : 0;
-            local[j][r] += q;
-            hi |= static_cast<uint32_t>((q >> 8) & 0xff) << (8 * u);
-            lo |= static_cast<uint32_t>((q & 0xff) ^ (a.lo_signed ? 0x80 : 0)) << (8 * u);
+            for (int u = 0; u < 4; ++u) {
+              const int c = c0 + u;
+              const int32_t q = c < K ? quant_x(y[u], a.qs, in_body(c, K)) : 0;
+              local[j][r] += q;
+              hi |= static_cast<uint32_t>((q >> 8) & 0xff) << (8 * u);
+              lo |= static_cast<uint32_t>((q & 0xff) ^ (a.lo_signed ? 0x80 : 0)) << (8 * u);
+            }
           }
           *reinterpret_cast<uint32_t*>(a.planes[j] + m * Kp + c0) = hi;
           *reinterpret_cast<uint32_t*>(a.planes[j] + (a.M + m) * Kp + c0) = lo;
@@ -570,7 +588,7 @@ cudaError_t launch_prep(const PrepArgs& a, cudaStream_t s) {
   }
   if (a.M >= kPrepManyRows && !a.mix_i) {  // many rows: several per CTA
     const int R = prep_rows_per_cta(a.K, mode);
-    const size_t rsmem = static_cast<size_t>(R) * ((a.K + 3) & ~3) * 4 * (mode == kPrepSwishgate ? 2 : 1);
+    const size_t rsmem = static_cast<size_t>(R) * rows_stride(a.K) * 4 * (mode == kPrepSwishgate ? 2 : 1);
     if (rsmem <= kMaxDynSmem) {
       if (rsmem > 48 * 1024) raise_smem_limit(reinterpret_cast<const void*>(prep_rows_kernel));
       PrepArgs q = a;

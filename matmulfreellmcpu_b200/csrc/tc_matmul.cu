@@ -99,6 +99,12 @@ __device__ __forceinline__ uint64_t l2_evict_first() {
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
   return pol;
 }
+// L2 policy for weights that several token tiles of one launch read (prefill): evict last
+__device__ __forceinline__ uint64_t l2_evict_last() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
 // bulk global -> shared copy completing on an mbarrier (no multicast), with an L2 policy
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
                                          uint64_t pol) {
@@ -445,7 +451,9 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     if (lane == 0) {
       const int64_t ngroups = packed_groups(a.N);
       const unsigned char* wbase = static_cast<const unsigned char*>(P.w);
-      const uint64_t pol = l2_evict_first();
+      // one token tile: the weights are read once (decode); more: every token tile re-reads
+      // them, so they stay in L2 (prefill)
+      const uint64_t pol = a.M > BN * TT ? l2_evict_last() : l2_evict_first();
       int i = 0;
       for (; i < nk; ++i) {
         const int s = i % kWStages;

@@ -167,6 +167,31 @@ def test_bitlinear_saturation_and_ragged(cuda, orc):
         del torch
 
 
+@pytest.mark.parametrize("M", [3, 20, 1100])
+@pytest.mark.parametrize("K,nan_row", [(203, False), (200, True)])
+def test_bitlinear_quant_extremes(cuda, orc, M, K, nan_row):
+    """Q5.10 codes at the edges of cvtps2dq: y*1024 >= 2^31 (INT32_MIN, clamped to -32768),
+    <= -2^31, +-inf, in the SIMD body and in the K % 8 tail, and a NaN row (every code
+    -32768) at K % 8 == 0; through the dp4a path (3 rows), the per-row prep (20) and the
+    many-rows prep (1100). A NaN row with a K % 8 tail is not compared: the reference's
+    scalar-tail cast gives INT32_MIN there, which its int32 dot product multiplies by the
+    weight, a value the 16-bit code planes cannot hold."""
+    rng = np.random.default_rng(17 + M)
+    N = 40
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    if nan_row:
+        x[1, 10] = np.float32(np.nan)
+    nw = (0.5 + rng.random(K)).astype(np.float32)
+    nw[5], nw[6], nw[7], nw[8] = 1e7, -1e7, np.inf, 3e38
+    nw[K - 3], nw[K - 2], nw[K - 1] = 1e7, -np.inf, 3e38
+    wq = rng.choice(np.array([-1, 0, 1], np.int8), size=(N, K))
+    out, acc, norm = run_gpu(cuda, x, nw, wq, 20.0, "fixed")
+    r_out, r_acc, r_norm = orc.bitlinear(x, nw, wq, 20.0, act_quant=1, want_norm=True)
+    assert np.array_equal(acc, r_acc)
+    assert bits_equal(out, r_out)
+    assert bits_equal(norm, r_norm)
+
+
 def test_bitlinear_cluster(cuda, orc):
     rng = np.random.default_rng(5)
     M, K, N = 4, 2048, 2048
