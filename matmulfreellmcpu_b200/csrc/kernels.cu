@@ -370,7 +370,10 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepArgs a, int mode
 // The flow per row is prep_kernel's: chain 1 (an 8-lane group per row, all R rows at once),
 // the row transform by all threads, chain 2, then the projections' normalisation, Q5.10 planes
 // (or Float activations) and row sums; the arithmetic is the same element by element.
-constexpr int kRowsThreads = 256, kRowsMax = 8, kRowsSmem = 96 * 1024;
+// Two shapes: 128 threads with <= 42 KB of rows (five CTAs per SM, whose copy and chain phases
+// overlap) for rows that fit at least twice, else 256 threads with <= 96 KB (long rows: one
+// row per 128-thread CTA spent most of its time in the serial chain with the SM half idle)
+constexpr int kRowsMax = 8, kRowsSmemSmall = 42 * 1024, kRowsSmemLarge = 96 * 1024;
 
 // Floats from one staged row to the next: a multiple of 4 (rows 16-byte aligned) that is 8
 // more than a multiple of 32, so that the 8-lane chain groups of the 4 rows of a warp read
@@ -380,14 +383,19 @@ __host__ __device__ inline int rows_stride(int K) {
   return k4 + ((8 - (k4 & 31)) & 31);
 }
 
-// rows per CTA: as many as fit kRowsSmem (at least 1, at most kRowsMax)
-static int prep_rows_per_cta(int K, int mode) {
+// rows per CTA and its threads: as many rows as fit the shape's budget (at least 1, at most
+// kRowsMax)
+static int prep_rows_per_cta(int K, int mode, int* threads) {
   const int64_t per_row = static_cast<int64_t>(rows_stride(K)) * 4 * (mode == kPrepSwishgate ? 2 : 1);
-  const int64_t r = kRowsSmem / per_row;
+  const bool small = 2 * per_row <= kRowsSmemSmall;
+  *threads = small ? 128 : 256;
+  const int64_t r = (small ? kRowsSmemSmall : kRowsSmemLarge) / per_row;
   return static_cast<int>(r < 1 ? 1 : (r > kRowsMax ? kRowsMax : r));
 }
 
-__global__ void __launch_bounds__(kRowsThreads) prep_rows_kernel(PrepArgs a, int mode, int R) {
+template <int kRowsThreads>
+__global__ void __launch_bounds__(kRowsThreads, kRowsThreads == 128 ? 5 : 2)
+    prep_rows_kernel(PrepArgs a, int mode, int R) {
   extern __shared__ __align__(16) float sb[];
   __shared__ float s_r1[kRowsMax], s_r2[kRowsMax];
   __shared__ int s_red[3][kRowsMax][kRowsThreads / 32];
@@ -587,14 +595,19 @@ cudaError_t launch_prep(const PrepArgs& a, cudaStream_t s) {
       return cudaErrorInvalidValue;
   }
   if (a.M >= kPrepManyRows && !a.mix_i) {  // many rows: several per CTA
-    const int R = prep_rows_per_cta(a.K, mode);
+    int threads = 128;
+    const int R = prep_rows_per_cta(a.K, mode, &threads);
     const size_t rsmem = static_cast<size_t>(R) * rows_stride(a.K) * 4 * (mode == kPrepSwishgate ? 2 : 1);
     if (rsmem <= kMaxDynSmem) {
-      if (rsmem > 48 * 1024) raise_smem_limit(reinterpret_cast<const void*>(prep_rows_kernel));
       PrepArgs q = a;
       q.row_polls = row_polls();
-      return launch_k(prep_rows_kernel, dim3(static_cast<unsigned>(ceil_div(int64_t(a.M), R))), dim3(kRowsThreads),
-                      rsmem, s, a.pdl, q, mode, R);
+      const dim3 grid(static_cast<unsigned>(ceil_div(int64_t(a.M), R)));
+      if (threads == 128) {
+        if (rsmem > 48 * 1024) raise_smem_limit(reinterpret_cast<const void*>(prep_rows_kernel<128>));
+        return launch_k(prep_rows_kernel<128>, grid, dim3(128), rsmem, s, a.pdl, q, mode, R);
+      }
+      if (rsmem > 48 * 1024) raise_smem_limit(reinterpret_cast<const void*>(prep_rows_kernel<256>));
+      return launch_k(prep_rows_kernel<256>, grid, dim3(256), rsmem, s, a.pdl, q, mode, R);
     }
   }
   if (smem > 48 * 1024) raise_smem_limit(reinterpret_cast<const void*>(prep_kernel));
@@ -785,7 +798,7 @@ cudaError_t launch_matmul(const MatmulArgs& a, cudaStream_t s) {
   if (a.M <= 0 || a.N <= 0) return cudaSuccess;
   if (matmul_uses_tc(a)) {
     if (a.fixed && !a.lo_signed) return cudaErrorInvalidValue;  // planes in the wrong form
-    return launch_matmul_tc(a, tc_splits(a, sm_count()), s);
+    return launch_matmul_tc(a, tc_splits(a, sm_count()), sm_count(), s);
   }
   if (a.M == 1) return launch_matmul_mt<1>(a, s);
   if (a.M == 2) return launch_matmul_mt<2>(a, s);

@@ -137,7 +137,7 @@ cudaError_t launch_dec_persist(const DecArgs* dev_phases, int nphases, int M, un
 // tcgen05 BitLinear matmul (tc_matmul.cu)
 int tc_token_tile(int M);
 int tc_splits(const MatmulArgs& a, int sm_count, int nproj = 1);
-cudaError_t launch_matmul_tc(const MatmulArgs& a, int splits, cudaStream_t s);
+cudaError_t launch_matmul_tc(const MatmulArgs& a, int splits, int sm_count, cudaStream_t s);
 // Several tensor-core BitLinears in one launch: nproj (1..3) projections of one shape (the
 // i/f/g cluster; a[0] carries the error word and the launch mode), or with
 // swiglu_I > 0 (I % 64 == 0, nproj 1) a gate_proj of N = 2I whose epilogue writes

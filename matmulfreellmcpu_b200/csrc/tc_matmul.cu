@@ -34,12 +34,9 @@
 // Every wait on an mbarrier is bounded; on timeout the CTA sets an error flag, the other roles
 // stop, producers wait (bounded) for their copies in flight, the MMA issuer's final commit
 // covers its MMAs, and the tensor memory is freed.
-#include "common.cuh"
 #include "exact.cuh"
-#include "kernels.h"
+#include "tcgen05.cuh"
 
-#include <cuda.h>
-#include <cstdint>
 #include <type_traits>
 #include <cstdlib>
 
@@ -54,223 +51,6 @@ constexpr int kBStages1 = 4;         // activation k-blocks in shared memory (on
 constexpr int kAStages = 4;          // expanded weight k-blocks in tensor memory (32 columns)
 constexpr int kKBlock = 128;         // k per pipeline stage (2 packed chunks)
 constexpr int kWBlock = 4 * 2 * kChunkBytes;  // bytes of one weight k-block (4 groups)
-constexpr uint32_t kSpinLimit = 1u << 26;  // bounded mbarrier waits
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-
-// true when the phase with the given parity has completed
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// bounded wait; returns false on timeout
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i)
-    if (mbar_try_wait(bar, parity)) return true;
-  return false;
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-// arrive and add `bytes` to the transaction count the phase waits for
-__device__ __forceinline__ void mbar_arrive_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-               : "memory");
-}
-// L2 policy for data read once per launch (the weights): evict first, so that the stream
-// does not displace activations and kernel code
-__device__ __forceinline__ uint64_t l2_evict_first() {
-  uint64_t pol;
-  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
-  return pol;
-}
-// L2 policy for weights that several token tiles of one launch read (prefill): evict last
-__device__ __forceinline__ uint64_t l2_evict_last() {
-  uint64_t pol;
-  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
-  return pol;
-}
-// bulk global -> shared copy completing on an mbarrier (no multicast), with an L2 policy
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
-                                         uint64_t pol) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
-          smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
-      : "memory");
-}
-// 2-D tiled TMA load (no multicast); x is a multiple of 128 bytes
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
-__device__ __forceinline__ void named_sync(int id, int threads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
-// all threads of all CTAs of the cluster (release / acquire of shared memory)
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-// address of the same shared-memory location in CTA `rank` of this cluster
-__device__ __forceinline__ uint32_t cluster_map(uint32_t saddr, int rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
-  return r;
-}
-// 16-byte load from a peer's shared memory (no memory clobber: callers read peer data
-// written before a cluster barrier, whose asm orders it; without the clobber a batch of
-// these loads is issued before its first use)
-__device__ __forceinline__ void ld_cluster_v4(uint32_t addr, uint32_t* v) {
-  asm volatile("ld.shared::cluster.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
-               : "r"(addr));
-}
-// the same from this CTA's own shared memory
-__device__ __forceinline__ void ld_shared_v4(uint32_t addr, uint32_t* v) {
-  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
-               : "r"(addr));
-}
-
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-
-// 16 consecutive 32-bit TMEM columns of this warp's 32 lanes <- 16 registers per thread
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
-      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
-      "r"(r[15])
-      : "memory");
-}
-__device__ __forceinline__ void tmem_st_wait() {
-  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-}
-
-// 16 consecutive TMEM columns of this warp's 32 lanes -> 16 registers per thread
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr)
-      : "memory");
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row core groups 1024 B apart.
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);  // start address (16-B units)
-  d |= static_cast<uint64_t>(1) << 16;                  // leading byte offset (unused, K-major SW)
-  d |= static_cast<uint64_t>(1024 >> 4) << 32;          // stride byte offset: next 8 rows
-  d |= static_cast<uint64_t>(1) << 46;                  // descriptor version (sm_100)
-  d |= static_cast<uint64_t>(2) << 61;                  // layout: SWIZZLE_128B
-  return d;
-}
-
-// Instruction descriptor of kind::i8: D s32, A u8 (K-major), B u8/s8 (K-major), M=128, N=bn.
-__host__ __device__ constexpr uint32_t idesc_i8(bool b_signed, int bn) {
-  return (2u << 4) | (0u << 7) | ((b_signed ? 1u : 0u) << 10) |
-         (static_cast<uint32_t>(bn >> 3) << 17) | (static_cast<uint32_t>(128 >> 4) << 24);
-}
-
-__device__ __forceinline__ void mma_i8_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                          uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(
-          d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
-      : "memory");
-}
-
-// Instruction descriptor of kind::f16 for the Float path: D f32, A and B both bf16 (the same
-// type, as the kind requires), both K-major, M=128, N=bn.
-__host__ __device__ constexpr uint32_t idesc_bf16(int bn) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(bn >> 3) << 17) |
-         (static_cast<uint32_t>(128 >> 4) << 24);
-}
-
-__device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                            uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(
-          d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
-      : "memory");
-}
-
-// Two ternary codes (u = w + 1 in the low 2 bits of bytes b and b + 1 of m) as a pair of bf16
-// weights w in {-1, 0, +1} (0xBF80, 0, 0x3F80): the low and high bytes of each bf16 are looked
-// up by byte_perm in the tables 0x00800080 (lows) and 0x003F00BF (highs), indexed by u.
-__device__ __forceinline__ uint32_t ternary_bf16x2(uint32_t m, int b) {
-  const uint32_t u0 = (m >> (8 * b)) & 3u, u1 = (m >> (8 * b + 8)) & 3u;
-  return __byte_perm(0x003F00BFu, 0x00800080u, (4u + u0) | (u0 << 4) | ((4u + u1) << 8) | (u1 << 12));
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   smem_u32(bar))
-               : "memory");
-}
-
-}  // namespace
-
-// One projection of a launch (i/f/g share a launch; they differ only in these).
-struct TcProj {
-  const void* w;           // packed weights
-  const int32_t* rowsum;   // [M] code sums of the projection's activation rows
-  float* out;              // [M, ldo]
-  float scale;             // 1 / (2^f * scale_w)
-};
-
-struct TcArgs {
-  MatmulArgs m;       // shape, residual and raw-accumulator output (single projection)
-  TcProj pj[3];
-  int nproj;          // grid.z = nproj * splits
-  int pair;           // SwiGLU gate_proj: I/32, the first group of the up rows; 0 otherwise
-  int seg_rows;       // SwiGLU: token rows of one reference vector call (SIMD tails) ...
-  int tail_from;      // ... whose last row's columns >= tail_from are its scalar tail
-  uint32_t* err;      // bit kErrTimeout on a timed-out wait
-  int splits;         // k-block ranges per tile = cluster size along z (1, 2, 4 or 8)
-  int vec;            // outputs, residual and raw accumulators allow 16-byte accesses
-};
-
-struct TcMaps {
-  CUtensorMap m[3];   // activation planes of each projection
-};
-
-namespace {
 
 // Smem layout of one CTA (offsets from a 1024-byte aligned base): the activation ring first
 // (1024-aligned stages, as the 128-byte swizzle wants), then the weight ring.
@@ -291,18 +71,6 @@ struct TcLayout {
   static_assert(TT == 1 || kDyn > 114 * 1024, "TT > 1 must keep one CTA per SM");
 };
 
-__device__ __forceinline__ bool cta_failed(const uint32_t* f) {
-  return *reinterpret_cast<const volatile uint32_t*>(f) != 0;
-}
-
-// bounded wait that gives up early once another role of the CTA has failed
-__device__ __forceinline__ bool role_wait(uint64_t* bar, uint32_t parity, uint32_t* s_fail) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255) == 255 && cta_failed(s_fail)) return false;
-  }
-  return false;
-}
 
 }  // namespace
 
@@ -874,6 +642,8 @@ EncodeTiledFn encode_tiled() {
   return fn;
 }
 
+}  // namespace
+
 // The planes [2][M][Kp] as one 2-D tensor of 2M rows x Kp elements (u8, or bf16 for the Float
 // path); a box is BN rows x 128 B (one k-block), written to shared memory with the 128-byte
 // swizzle; reads past row 2M or column Kp return zeros.
@@ -893,7 +663,40 @@ cudaError_t planes_map(CUtensorMap* map, const int8_t* planes, int M, int64_t kp
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-}  // namespace
+// The same planes as a 3-D tensor {Kp, M, 2} (u8): one box of 128 B x bn rows x both planes
+// is a whole activation k-block (high rows, then low rows) in one copy; rows past M read 0.
+cudaError_t planes_map3(CUtensorMap* map, const int8_t* planes, int M, int64_t kp, int bn) {
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) return cudaErrorNotSupported;
+  if ((reinterpret_cast<uintptr_t>(planes) & 15) != 0) return cudaErrorMisalignedAddress;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kp), static_cast<cuuint64_t>(M), 2};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(kp), static_cast<cuuint64_t>(kp) * static_cast<cuuint64_t>(M)};
+  const cuuint32_t box[3] = {128, static_cast<cuuint32_t>(bn), 2};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<int8_t*>(planes), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+// Packed ternary weights [groups][chunks][512 B] as a 2-D tensor of 32-bit words, one row per
+// 32-row group (kc * 128 words); a box is 256 words (two chunks, 128 k) x `rows` groups, so
+// one copy brings a k-block of several groups; groups past N and chunks past Kp read 0.
+cudaError_t weights_map(CUtensorMap* map, const void* w, int64_t n, int64_t k, int rows) {
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) return cudaErrorNotSupported;
+  if ((reinterpret_cast<uintptr_t>(w) & 15) != 0) return cudaErrorMisalignedAddress;
+  const int64_t kc = packed_chunks(k);
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(kc) * (kChunkBytes / 4), static_cast<cuuint64_t>(packed_groups(n))};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(kc) * kChunkBytes};
+  const cuuint32_t box[2] = {2 * kChunkBytes / 4, static_cast<cuuint32_t>(rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(w), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 
 template <int BN, int TT, bool FL>
 static cudaError_t launch_tc_bn(const TcArgs& p, const MatmulArgs* a, bool pdl, cudaStream_t s) {
@@ -963,13 +766,13 @@ int tc_splits(const MatmulArgs& a, int sm_count, int nproj) {
 // nproj projections of one shape in one launch; pair > 0: a SwiGLU gate_proj (N = 2I,
 // pair = I / 32, out = z [M, I], tails per seg)
 static cudaError_t launch_tc(const MatmulArgs* a, int nproj, int pair, int64_t seg, int splits,
-                             cudaStream_t s) {
+                             int sm_count, cudaStream_t s) {
   const MatmulArgs& m = a[0];
   if (m.M <= 0 || m.N <= 0) return cudaSuccess;
   const int nkb = tc_kblocks(m);
   if (nproj < 1 || nproj > 3 || splits < 1 || splits > 8 || (splits & (splits - 1)) || splits > nkb)
     return cudaErrorInvalidValue;
-  if (pair && (nproj != 1 || m.N != 64 * pair || pair % 2 != 0)) return cudaErrorInvalidValue;
+  if (pair && (nproj != 1 || m.N != 64 * pair)) return cudaErrorInvalidValue;
   // FixedQ510: low planes stored lo - 128; Float: bf16 planes (no raw accumulators)
   for (int j = 0; j < nproj; ++j)
     if (a[j].M != m.M || a[j].N != m.N || a[j].K != m.K || a[j].fixed != m.fixed ||
@@ -998,6 +801,12 @@ static cudaError_t launch_tc(const MatmulArgs* a, int nproj, int pair, int64_t s
     p.vec = vec ? 1 : 0;
   }
   for (int j = 0; j < nproj; ++j) p.pj[j] = TcProj{a[j].w, a[j].rowsum, a[j].out, a[j].scale};
+  // thousands of rows: the persistent kernel, once every SM gets two tiles or more
+  if (m.fixed && tc_rows_enabled() && tc_rows_tiles(m, nproj, pair) >= 2 * static_cast<int64_t>(sm_count)) {
+    p.splits = 1;
+    return launch_tc_rows(p, a, sm_count, s);
+  }
+  if (pair % 2 != 0) return cudaErrorInvalidValue;  // 64-row pair tiles below
   const int bn = tc_token_tile(m.M);
   // (three 64-row token tiles per CTA sharing each expanded weight k-block, TT = 3, were
   // measured 1.3x slower on the 2.7B prefill than two one-tile CTAs per SM)
@@ -1011,13 +820,14 @@ static cudaError_t launch_tc(const MatmulArgs* a, int nproj, int pair, int64_t s
   return launch_tc_bn<64, 1, false>(p, a, m.pdl, s);
 }
 
-cudaError_t launch_matmul_tc(const MatmulArgs& a, int splits, cudaStream_t s) {
-  return launch_tc(&a, 1, 0, 1, splits, s);
+cudaError_t launch_matmul_tc(const MatmulArgs& a, int splits, int sm_count, cudaStream_t s) {
+  return launch_tc(&a, 1, 0, 1, splits, sm_count, s);
 }
 
 cudaError_t launch_matmul_tc_group(const MatmulArgs* a, int nproj, int swiglu_I, int64_t seg,
                                    int sm_count, cudaStream_t s) {
-  return launch_tc(a, nproj, swiglu_I > 0 ? swiglu_I / 32 : 0, seg, tc_splits(a[0], sm_count, nproj), s);
+  return launch_tc(a, nproj, swiglu_I > 0 ? swiglu_I / 32 : 0, seg, tc_splits(a[0], sm_count, nproj),
+                   sm_count, s);
 }
 
 }  // namespace mmfree_cuda

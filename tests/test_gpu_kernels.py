@@ -167,6 +167,22 @@ def test_bitlinear_saturation_and_ragged(cuda, orc):
         del torch
 
 
+@pytest.mark.parametrize("M,K,N", [(2100, 960, 5000), (1500, 2048, 13000)])
+def test_bitlinear_rows_kernel_ragged(cuda, orc, M, K, N):
+    """Enough output tiles for the persistent large-M kernel (two or more per SM): ragged
+    tokens (2100 = 32 x 64 + 52), an odd chunk count (K = 960: the last 128-k block holds one
+    chunk), partial last weight tiles (5000 and 13000 rows: 136 and 200 rows in the last
+    256-row tile, a partial 32-row group), saturating outliers; every accumulator, output and
+    norm bit for bit."""
+    x, nw, wq = sweep_inputs(M, K, N, seed=23 + K)
+    x[::9, :4] = np.float32(600.0)
+    out, acc, norm = run_gpu(cuda, x, nw, wq, 20.0, "fixed")
+    r_out, r_acc, r_norm = orc.bitlinear(x, nw, wq, 20.0, act_quant=1, want_norm=True)
+    assert np.array_equal(acc, r_acc)
+    assert bits_equal(out, r_out)
+    assert bits_equal(norm, r_norm)
+
+
 @pytest.mark.parametrize("M", [3, 20, 1100])
 @pytest.mark.parametrize("K,nan_row", [(203, False), (200, True)])
 def test_bitlinear_quant_extremes(cuda, orc, M, K, nan_row):
