@@ -612,9 +612,9 @@ void Model::layers_tp(int nseq, int len, int seg_rows) {
     }
     prep(p);
   };
-  // a shard's BitLinear into out (row stride ldo), optionally + resid (row stride ldr)
-  // a shard's BitLinear; from_yf: Float row-parallel inputs written as fp32 activations by
-  // launch_norm_slice (the CUDA-core kernel reads them)
+  // a shard's BitLinear into out (row stride ldo), optionally + resid (row stride ldr);
+  // from_yf: Float row-parallel inputs written as fp32 activations by launch_norm_slice (below
+  // the tensor-core row count: the CUDA-core kernel reads them)
   auto shard_mm = [&](const Proj& pj, int plane, float* out, int ldo, const float* resid, int ldr,
                       bool from_yf = false) {
     MatmulArgs a = mm_args(pj, plane, out, rows, resid);
@@ -646,8 +646,14 @@ void Model::layers_tp(int nseq, int len, int seg_rows) {
                            stream_));
       tp_->all_reduce_f32(ss_b, rows, stream_);
       const int kp = static_cast<int>(padded_k(Hs));
-      CK(launch_norm_slice(yf_[0], tp_ts_, ss_b, ly.p[kO].normw + hoff, rows, Hs, kp, H, eps_, stream_));
-      shard_mm(ly.p[kO], 0, resid_, H, nullptr, 0, true);  // partial [rows][H]
+      if (tc_rows(rows)) {  // bf16 planes for the tensor cores
+        CK(launch_norm_slice_planes(planes_[0], tp_ts_, ss_b, ly.p[kO].normw + hoff, rows, Hs, kp, H, eps_,
+                                    stream_));
+        shard_mm(ly.p[kO], 0, resid_, H, nullptr, 0);  // partial [rows][H]
+      } else {
+        CK(launch_norm_slice(yf_[0], tp_ts_, ss_b, ly.p[kO].normw + hoff, rows, Hs, kp, H, eps_, stream_));
+        shard_mm(ly.p[kO], 0, resid_, H, nullptr, 0, true);
+      }
       tp_->all_reduce_f32(resid_, static_cast<size_t>(rows) * H, stream_);
       CK(launch_add(resid_, h_, resid_, static_cast<int64_t>(rows) * H, stream_));
     }
@@ -673,9 +679,15 @@ void Model::layers_tp(int nseq, int len, int seg_rows) {
       CK(launch_row_sumsq(ss_a, tp_zs_, rows, Is, Is, stream_));
       tp_->all_reduce_f32(ss_a, rows, stream_);
       const int kp = static_cast<int>(padded_k(Is));
-      CK(launch_norm_slice(yf_[0], tp_zs_, ss_a, ly.p[kDown].normw + ioff, rows, Is, kp, I_, eps_,
-                           stream_));
-      shard_mm(ly.p[kDown], 0, h_, H, nullptr, 0, true);  // partial [rows][H]
+      if (tc_rows(rows)) {
+        CK(launch_norm_slice_planes(planes_[0], tp_zs_, ss_a, ly.p[kDown].normw + ioff, rows, Is, kp, I_,
+                                    eps_, stream_));
+        shard_mm(ly.p[kDown], 0, h_, H, nullptr, 0);  // partial [rows][H]
+      } else {
+        CK(launch_norm_slice(yf_[0], tp_zs_, ss_a, ly.p[kDown].normw + ioff, rows, Is, kp, I_, eps_,
+                             stream_));
+        shard_mm(ly.p[kDown], 0, h_, H, nullptr, 0, true);
+      }
       tp_->all_reduce_f32(h_, static_cast<size_t>(rows) * H, stream_);
       CK(launch_add(h_, resid_, h_, static_cast<int64_t>(rows) * H, stream_));
     }

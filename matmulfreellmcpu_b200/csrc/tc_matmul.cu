@@ -230,7 +230,22 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         if (i == kWStages) grid_dep_wait();
         if (i >= kWStages && !role_wait(&wempty[s], ((i / kWStages) - 1) & 1, &s_fail)) break;
         const int64_t c0 = (FL ? 1 : 2) * static_cast<int64_t>(kb0 + i);  // first chunk
-        const uint32_t bytes = !FL && c0 + 1 < kc ? 2 * kChunkBytes : kChunkBytes;
+        if (!FL) {
+          // one tensor copy of the k-block's 4 groups (2 + 2 for a pair tile); groups past the
+          // rows and a chunk past Kp arrive as zeros, whole boxes counted
+          mbar_arrive_tx(&wfull[s], static_cast<uint32_t>(kWBlock));
+          const CUtensorMap* wmap = &maps.w[proj];
+          const int x = static_cast<int>(c0) * (kChunkBytes / 4);  // 32-bit words
+          if (p.pair) {
+            tma_load_2d_hint(wst + s * kWBlock, wmap, x, static_cast<int>(tile_group(0)), &wfull[s], pol);
+            tma_load_2d_hint(wst + s * kWBlock + 2 * 2 * kChunkBytes, wmap, x, static_cast<int>(tile_group(2)),
+                             &wfull[s], pol);
+          } else {
+            tma_load_2d_hint(wst + s * kWBlock, wmap, x, static_cast<int>(tile_group(0)), &wfull[s], pol);
+          }
+          continue;
+        }
+        const uint32_t bytes = kChunkBytes;
         uint32_t total = 0;
         for (int g = 0; g < 4; ++g)
           if (tile_group(g) < ngroups) total += bytes;
@@ -704,6 +719,7 @@ static cudaError_t launch_tc_bn(const TcArgs& p, const MatmulArgs* a, bool pdl, 
   TcMaps maps;
   for (int j = 0; j < p.nproj; ++j) {
     cudaError_t e = planes_map(&maps.m[j], a[j].planes, a[j].M, padded_k(a[j].K), BN, FL);
+    if (e == cudaSuccess && !FL) e = weights_map(&maps.w[j], a[j].w, a[j].N, a[j].K, p.pair ? 2 : 4);
     if (e != cudaSuccess) return e;
   }
   static bool attr_set[64] = {false};

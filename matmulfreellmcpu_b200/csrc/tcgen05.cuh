@@ -257,6 +257,8 @@ struct TcArgs {
 
 struct TcMaps {
   CUtensorMap m[3];   // activation planes of each projection
+  CUtensorMap w[3];   // packed weights of each projection (FixedQ510: a k-block of a tile's
+                      // 4 groups, or 2 + 2 for a SwiGLU pair tile, per copy)
 };
 
 // The activation planes [2][M][Kp] as one 2-D tensor map of 2M rows (u8, or bf16 for the Float

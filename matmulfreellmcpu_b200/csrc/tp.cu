@@ -196,6 +196,36 @@ cudaError_t launch_norm_slice(float* yf, const float* x, const float* ss, const 
   return cudaGetLastError();
 }
 
+// The same rows as bf16 hi / lo planes [2][T][kp] for the tensor-core Float BitLinear (hi =
+// bf16(y), lo = bf16(y - hi)), four elements per thread.
+__global__ void norm_slice_planes_kernel(int8_t* __restrict__ planes, const float* __restrict__ x,
+                                         const float* __restrict__ ss, const float* __restrict__ w, int T,
+                                         int n, int kp, int K, float eps) {
+  const int t = blockIdx.y;
+  const int c0 = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
+  if (t >= T || c0 >= kp) return;
+  const float r = rstd_of(ss[t], static_cast<float>(K), eps);
+  float y[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int c = c0 + u;
+    y[u] = c < n ? norm_x(x[static_cast<int64_t>(t) * n + c], r, w[c]) : 0.0f;
+  }
+  uint2 hi, lo;
+  bf16_split4(y, hi, lo);
+  *reinterpret_cast<uint2*>(planes + 2 * (static_cast<int64_t>(t) * kp + c0)) = hi;
+  *reinterpret_cast<uint2*>(planes + 2 * ((static_cast<int64_t>(T) + t) * kp + c0)) = lo;
+}
+
+cudaError_t launch_norm_slice_planes(int8_t* planes, const float* x, const float* ss, const float* w, int T,
+                                     int n, int kp, int K, float eps, cudaStream_t s) {
+  if (T <= 0) return cudaSuccess;
+  if (T > 65535 || kp % 4 != 0 || (reinterpret_cast<uintptr_t>(planes) & 7) != 0) return cudaErrorInvalidValue;
+  norm_slice_planes_kernel<<<dim3(static_cast<unsigned>(ceil_div(kp / 4, 256)), T), 256, 0, s>>>(
+      planes, x, ss, w, T, n, kp, K, eps);
+  return cudaGetLastError();
+}
+
 __global__ void add_kernel(float* __restrict__ out, const float* __restrict__ a,
                            const float* __restrict__ b, int64_t n) {
   const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;

@@ -60,6 +60,9 @@ cudaError_t launch_gate_slice(float* t, float* ss_t, const float* g, const float
 // column slice, bitlinear.cpp:95-105, into the float matmul's activation layout).
 cudaError_t launch_norm_slice(float* yf, const float* x, const float* ss, const float* w, int T,
                               int n, int kp, int K, float eps, cudaStream_t s);
+// The same as bf16 hi / lo planes [2][T][kp] (the tensor-core Float BitLinear's input).
+cudaError_t launch_norm_slice_planes(int8_t* planes, const float* x, const float* ss, const float* w, int T,
+                                     int n, int kp, int K, float eps, cudaStream_t s);
 // out[i] = a[i] + b[i]
 cudaError_t launch_add(float* out, const float* a, const float* b, int64_t n, cudaStream_t s);
 
