@@ -16,8 +16,9 @@ steps stream them from HBM without an explicit flush.
 
 Also reported: e2e (the same metric through the public serving API, one
 mmfree_cuda_serve_step call per step: pinned host ids in, next ids out), b=1 decode tok/s
-(configuration 2 shape, rank 0), the per-kernel roofline of the dominant kernel class and
-the reference CPU engine timed on this host on a bounded sample (rank 0, N=1).
+(configuration 2 shape, rank 0), the per-kernel roofline of the dominant kernel class, the
+configuration-4 prefill (2.7B, 8 x 2048 tokens; N=1, `prefill_2.7B`, --no-prefill skips it)
+and the reference CPU engine timed on this host on a bounded sample (rank 0, N=1).
 """
 from __future__ import annotations
 
@@ -584,6 +585,12 @@ def run_ours(a, rank, world, local):
             with api.Model(path, "float", 10, device=local) as mf:
                 sf_ = torch.cuda.ExternalStream(mf.stream_ptr, device=torch.device("cuda", local))
                 b1f = run_b1(mf, sf_, b1_steps, "float")
+    prefill = None
+    if rank == 0 and world == 1 and not a.no_prefill:
+        try:
+            prefill = prefill_extra(a.mode, local)
+        except Exception as ex:  # reported beside the headline, never required
+            prefill = {"unavailable": str(ex)}
     op_m1 = None
     if rank == 0 and not a.no_op:
         peaks_, src_ = load_peaks()
@@ -621,6 +628,7 @@ def run_ours(a, rank, world, local):
                     "h2d_bytes_per_step": 8 * S + 16, "d2h_bytes_per_step": 8 * S},
             "gpu_launches": int(round(launches_per_step * K)),
             "roofline": roof, "cpu_baseline": cpu, "b1": b1, "b1_float": b1f, "op_m1": op_m1,
+            "prefill_2.7B": prefill,
             "strong_scaling": strong,
             "kernel_ms_per_step_serialised": {k: v["ms"] / prof_steps for k, v in prof.items()},
             "clocks": clk}
@@ -662,6 +670,47 @@ def cpu_prefill(threads=0):
     return {"value": P4_CPU_LEN / dt, "unit": "tok/s", "cores": R.threads(), "kind": "reference",
             "sample": f"Model::forward of one {P4_CPU_LEN}-token prompt (2.7B, fixed) in {dt:.2f} s",
             "ms_per_step": 1e3 * dt}
+
+
+def prefill_extra(mode, local, steps=3):
+    """Configuration 4 on one GPU, attached to the default decode line: the 8 x 2048-token
+    prefill of the 2.7B model through the public serve_begin call, one warm-up forward and
+    `steps` timed ones (CUDA events on the model's stream), sequence 0's first id checked
+    against the reference's fixture; the roofline as `--workload prefill` reports it."""
+    import torch
+
+    from matmulfreellmcpu_b200 import api
+
+    seqs = p4_prompts()
+    with api.Model(blob_path(0, 1, "2.7B"), mode, 10, device=local) as m:
+        st = torch.cuda.ExternalStream(m.stream_ptr, device=torch.device("cuda", local))
+        m.serve_begin(seqs)
+        m.serve_end()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(steps):
+            first = m.serve_begin(seqs)
+            m.serve_end()
+        e1.record(st)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+    peaks, src = load_peaks()
+    int8_peak = 2.0 * float(peaks["bf16_tflops"])
+    tokens = P4_SEQS * P4_LEN * steps
+    tops = p4_ops_per_token() * tokens / (ms / 1e3) / 1e12
+    g4 = golden("config4_prefill_2.7B.npz")
+    parity = None
+    if g4 is not None:
+        parity = {"ok": bool(first[0] == int(g4[f"{mode}_argmax"][0])),
+                  "checked": "sequence 0's first id vs the reference's argmax of its last position"}
+    return {"metric": "HGRN-Bit 2.7B prefill tok/s (8 x 2048 tokens, config 4)",
+            "value": tokens / (ms / 1e3), "unit": "tok/s", "ms_per_step": ms / steps, "steps": steps,
+            "warmup": 1, "mode": mode, "parity": parity,
+            "roofline": {"bound": "tensor", "achieved": tops, "peak": int8_peak, "unit": "TOP/s",
+                         "frac": tops / int8_peak,
+                         "kernel": "whole prefill forward (algorithmic 2*T*weights int ops)",
+                         "peak_source": f"int8 dense = 2 x bf16_tflops of {src} peaks"}}
 
 
 def run_prefill(a, rank, world, local):
@@ -820,6 +869,8 @@ def main():
     ap.add_argument("--mode", choices=["fixed", "float"], default="fixed")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-op", action="store_true", help="skip the op_m1 rows (config 1, M=1)")
+    ap.add_argument("--no-prefill", action="store_true",
+                    help="skip the config-4 prefill attached to the default decode line")
     ap.add_argument("--no-tp", action="store_true",
                     help="prefill at N > 1: skip the tensor-parallel leg")
     ap.add_argument("--tp-float", action="store_true",
