@@ -173,7 +173,8 @@ def test_bitlinear_rows_kernel_ragged(cuda, orc, M, K, N):
     tokens (2100 = 32 x 64 + 52), an odd chunk count (K = 960: the last 128-k block holds one
     chunk), partial last weight tiles (5000 and 13000 rows: 136 and 200 rows in the last
     256-row tile, a partial 32-row group), saturating outliers; every accumulator, output and
-    norm bit for bit."""
+    norm bit for bit. The same shapes in Float (bf16 planes on the one-tile-per-CTA kernel):
+    norms bit for bit, outputs within the Float tolerance."""
     x, nw, wq = sweep_inputs(M, K, N, seed=23 + K)
     x[::9, :4] = np.float32(600.0)
     out, acc, norm = run_gpu(cuda, x, nw, wq, 20.0, "fixed")
@@ -181,6 +182,10 @@ def test_bitlinear_rows_kernel_ragged(cuda, orc, M, K, N):
     assert np.array_equal(acc, r_acc)
     assert bits_equal(out, r_out)
     assert bits_equal(norm, r_norm)
+    fo, _, fn = run_gpu(cuda, x, nw, wq, 20.0, "float")
+    f_out, _, f_norm = orc.bitlinear(x, nw, wq, 20.0, act_quant=0, want_norm=True)
+    assert bits_equal(fn, f_norm)
+    assert_float_close(fo, f_out)
 
 
 @pytest.mark.parametrize("M", [3, 20, 1100])
