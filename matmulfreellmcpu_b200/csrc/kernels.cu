@@ -393,12 +393,14 @@ static int prep_rows_per_cta(int K, int mode, int* threads) {
   return static_cast<int>(r < 1 ? 1 : (r > kRowsMax ? kRowsMax : r));
 }
 
-template <int kRowsThreads>
-__global__ void __launch_bounds__(kRowsThreads, kRowsThreads == 128 ? 5 : 2)
+// NP: projections (a.nproj, 1 or 3); FX: FixedQ510 (a.fixed) -- compile-time, so that the
+// unrolled per-element loops carry no runtime exits
+template <int kRowsThreads, int NP, bool FX>
+__global__ void __launch_bounds__(kRowsThreads, kRowsThreads == 128 ? (NP == 3 ? 4 : 5) : 2)
     prep_rows_kernel(PrepArgs a, int mode, int R) {
   extern __shared__ __align__(16) float sb[];
   __shared__ float s_r1[kRowsMax], s_r2[kRowsMax];
-  __shared__ int s_red[3][kRowsMax][kRowsThreads / 32];
+  __shared__ int s_red[NP][kRowsMax][kRowsThreads / 32];
   __shared__ __align__(8) uint64_t s_bar;
   const int K = a.K, tid = threadIdx.x, RS = rows_stride(K);
   const int64_t Kp = padded_k(K);
@@ -484,21 +486,34 @@ __global__ void __launch_bounds__(kRowsThreads, kRowsThreads == 128 ? 5 : 2)
     }
     __syncthreads();
   }
-  if (a.nproj == 0) return;
   if (tid < 8 * nr) {
     const float r = rstd_of(sumsq_exact8(xs + static_cast<int64_t>(cr) * RS, K, mask), static_cast<float>(K), a.eps);
     if ((tid & 7) == 0) s_r2[cr] = r;
   }
   __syncthreads();
-  int local[3][kRowsMax] = {};
+  int local[NP][kRowsMax] = {};
   const uint32_t lo_xor = a.lo_signed ? 0x80808080u : 0u;
+  float* const norm_out = a.norm_out;
+  bool nw16[NP];  // norm weights 16-byte aligned: 4 per load
+#pragma unroll
+  for (int j = 0; j < NP; ++j) nw16[j] = (reinterpret_cast<uintptr_t>(a.normw[j]) & 15) == 0;
   for (int c0 = 4 * tid; c0 < Kp; c0 += 4 * kRowsThreads) {
     const bool body4 = c0 + 3 < (K & ~7);  // 4 body elements
-    float nwv[3][4];
+    const bool full4 = c0 + 3 < K;
+    float nwv[NP][4];
 #pragma unroll
-    for (int j = 0; j < 3; ++j)
+    for (int j = 0; j < NP; ++j) {
+      if (full4 && nw16[j]) {
+        const float4 w4 = __ldg(reinterpret_cast<const float4*>(a.normw[j] + c0));
+        nwv[j][0] = w4.x;
+        nwv[j][1] = w4.y;
+        nwv[j][2] = w4.z;
+        nwv[j][3] = w4.w;
+      } else {
 #pragma unroll
-      for (int u = 0; u < 4; ++u) nwv[j][u] = (j < a.nproj && c0 + u < K) ? __ldg(a.normw[j] + c0 + u) : 0.0f;
+        for (int u = 0; u < 4; ++u) nwv[j][u] = c0 + u < K ? __ldg(a.normw[j] + c0 + u) : 0.0f;
+      }
+    }
 #pragma unroll
     for (int r = 0; r < kRowsMax; ++r) {
       if (r >= nr) break;
@@ -507,16 +522,15 @@ __global__ void __launch_bounds__(kRowsThreads, kRowsThreads == 128 ? 5 : 2)
       load4(xs + static_cast<int64_t>(r) * RS, c0, K, true, t);
       const float r2 = s_r2[r];
 #pragma unroll
-      for (int j = 0; j < 3; ++j) {
-        if (j >= a.nproj) break;
+      for (int j = 0; j < NP; ++j) {
         float y[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           const int c = c0 + u;
           y[u] = c < K ? norm_x(t[u], r2, nwv[j][u]) : 0.0f;
-          if (j == 0 && a.norm_out && c < K) a.norm_out[m * K + c] = y[u];
+          if (j == 0 && norm_out && c < K) norm_out[m * K + c] = y[u];
         }
-        if (a.fixed) {
+        if (FX) {
           uint32_t hi = 0, lo = 0;
           if (body4) {
             quant4_body_planes(y, a.qs, lo_xor, hi, lo, local[j][r]);
@@ -543,17 +557,17 @@ __global__ void __launch_bounds__(kRowsThreads, kRowsThreads == 128 ? 5 : 2)
       }
     }
   }
-  if (!a.fixed) return;
+  if (!FX) return;
   const int warp = tid >> 5, lane = tid & 31;
 #pragma unroll
-  for (int j = 0; j < 3; ++j)
+  for (int j = 0; j < NP; ++j)
 #pragma unroll
     for (int r = 0; r < kRowsMax; ++r) {
       const int v = __reduce_add_sync(0xffffffffu, local[j][r]);
       if (lane == 0) s_red[j][r][warp] = v;
     }
   __syncthreads();
-  if (tid < a.nproj * kRowsMax) {
+  if (tid < NP * kRowsMax) {
     const int j = tid / kRowsMax, r = tid % kRowsMax;
     if (r < nr) {
       int total = 0;
@@ -594,7 +608,7 @@ cudaError_t launch_prep(const PrepArgs& a, cudaStream_t s) {
         !al16(a.mix_lb) || !al16(a.mix_out))
       return cudaErrorInvalidValue;
   }
-  if (a.M >= kPrepManyRows && !a.mix_i) {  // many rows: several per CTA
+  if (a.M >= kPrepManyRows && !a.mix_i && (a.nproj == 1 || a.nproj == 3)) {  // many rows: several per CTA
     int threads = 128;
     const int R = prep_rows_per_cta(a.K, mode, &threads);
     const size_t rsmem = static_cast<size_t>(R) * rows_stride(a.K) * 4 * (mode == kPrepSwishgate ? 2 : 1);
@@ -602,12 +616,17 @@ cudaError_t launch_prep(const PrepArgs& a, cudaStream_t s) {
       PrepArgs q = a;
       q.row_polls = row_polls();
       const dim3 grid(static_cast<unsigned>(ceil_div(int64_t(a.M), R)));
+      auto go = [&](auto kern, int nt) {
+        if (rsmem > 48 * 1024) raise_smem_limit(reinterpret_cast<const void*>(kern));
+        return launch_k(kern, grid, dim3(nt), rsmem, s, a.pdl, q, mode, R);
+      };
+      const bool three = a.nproj == 3;
       if (threads == 128) {
-        if (rsmem > 48 * 1024) raise_smem_limit(reinterpret_cast<const void*>(prep_rows_kernel<128>));
-        return launch_k(prep_rows_kernel<128>, grid, dim3(128), rsmem, s, a.pdl, q, mode, R);
+        if (a.fixed) return three ? go(prep_rows_kernel<128, 3, true>, 128) : go(prep_rows_kernel<128, 1, true>, 128);
+        return three ? go(prep_rows_kernel<128, 3, false>, 128) : go(prep_rows_kernel<128, 1, false>, 128);
       }
-      if (rsmem > 48 * 1024) raise_smem_limit(reinterpret_cast<const void*>(prep_rows_kernel<256>));
-      return launch_k(prep_rows_kernel<256>, grid, dim3(256), rsmem, s, a.pdl, q, mode, R);
+      if (a.fixed) return three ? go(prep_rows_kernel<256, 3, true>, 256) : go(prep_rows_kernel<256, 1, true>, 256);
+      return three ? go(prep_rows_kernel<256, 3, false>, 256) : go(prep_rows_kernel<256, 1, false>, 256);
     }
   }
   if (smem > 48 * 1024) raise_smem_limit(reinterpret_cast<const void*>(prep_kernel));
