@@ -179,7 +179,11 @@ void run_bitlinear(int k, float* const* outs, const float* x, const float* const
     d.out[0] = outs[0];
     d.fl = fixed ? 0 : 1;
     const int grid = std::max(1, std::min(dec_units(d, kDecEpiResid), 2 * sm_count_of_device()));
-    if (launch_dec(d, kDecProPlain, kDecEpiResid, grid, st, false) == cudaSuccess) return;
+    // as a programmatic dependent: back-to-back calls stream the next call's first weight
+    // units while this one finishes (before its dependency wait the kernel reads only weights
+    // and writes nothing; a previous kernel that does not trigger early, like the repack,
+    // still completes before it starts)
+    if (launch_dec(d, kDecProPlain, kDecEpiResid, grid, st, true) == cudaSuccess) return;
     (void)cudaGetLastError();  // shape the fused kernel cannot stage: the general path below
   }
   const size_t kp = static_cast<size_t>(padded_k(static_cast<int64_t>(in_dim)));
