@@ -888,13 +888,33 @@ __global__ void gates_kernel(float* __restrict__ iv, float* __restrict__ fv,
   float a[4], b[4], l[4];
   bool body[4];
   const bool vec = e0 + 3 < n;
+  const bool al = ((reinterpret_cast<uintptr_t>(iv) | reinterpret_cast<uintptr_t>(fv)) & 15) == 0;
+  if (vec && al && H % 4 == 0) {
+    // the 4 elements share a row (H and seg multiples of 4): one remainder each, 16-byte loads
+    const int c0 = static_cast<int>(e0 % H);
+    const int64_t s0 = e0 % seg;
+    const float4 a4 = __ldcs(reinterpret_cast<const float4*>(iv + e0));
+    const float4 b4 = __ldcs(reinterpret_cast<const float4*>(fv + e0));
+    a[0] = a4.x; a[1] = a4.y; a[2] = a4.z; a[3] = a4.w;
+    b[0] = b4.x; b[1] = b4.y; b[2] = b4.z; b[3] = b4.w;
+    if (lb && (reinterpret_cast<uintptr_t>(lb) & 15) == 0) {
+      const float4 l4 = __ldg(reinterpret_cast<const float4*>(lb + c0));
+      l[0] = l4.x; l[1] = l4.y; l[2] = l4.z; l[3] = l4.w;
+    } else {
 #pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    const int64_t e = e0 + u;
-    a[u] = (vec || e < n) ? __ldcs(iv + e) : 0.0f;
-    b[u] = (vec || e < n) ? __ldcs(fv + e) : 0.0f;
-    l[u] = lb ? __ldg(lb + e % H) : 0.0f;
-    body[u] = e % seg < body_n;
+      for (int u = 0; u < 4; ++u) l[u] = lb ? __ldg(lb + c0 + u) : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) body[u] = s0 + u < body_n;
+  } else {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int64_t e = e0 + u;
+      a[u] = (vec || e < n) ? __ldcs(iv + e) : 0.0f;
+      b[u] = (vec || e < n) ? __ldcs(fv + e) : 0.0f;
+      l[u] = lb ? __ldg(lb + e % H) : 0.0f;
+      body[u] = e % seg < body_n;
+    }
   }
   float f[4], om[4], x[4];
   sigmoid_n(b, body, f);
