@@ -310,8 +310,9 @@ __global__ void __launch_bounds__(kRThreads, 1)
     }
     if (!ok) atomicOr(&s_fail, 1u);
   } else if (warp >= kREpi0) {
-    // ---- epilogue: warp 8 + w reads TMEM lanes 32 (w % 4) .. + 31 (weight rows of both
-    //      operands) for tokens 32 (w / 4) .. + 31 of the tile
+    // ---- epilogue: warp 12 + w reads TMEM lanes 32 (w % 4) .. + 31 (weight rows of both
+    //      operands; a warp reaches the lane quarter of its warp index mod 4) for tokens
+    //      32 (w / 4) .. + 31 of the tile
     const int ew = warp - kREpi0, lq = ew & 3, half = ew >> 2;
     const int c = 32 * lq + lane;  // row within each operand
     const uint32_t lane_base = static_cast<uint32_t>(32 * lq) << 16;
